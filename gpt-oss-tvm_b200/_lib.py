@@ -1,0 +1,82 @@
+"""ctypes binding of libgptoss_b200.so (the C ABI in include/gptoss_b200.h).
+
+The product path has no CPU fallback: loading fails loudly when the library
+is missing, and every call raises GptossError when the C ABI reports an
+error.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("GPTOSS_B200_LIB", os.path.join(HERE, "libgptoss_b200.so"))
+
+
+class GptossError(RuntimeError):
+    pass
+
+
+class gptoss_moe_weights(ctypes.Structure):
+    _fields_ = [
+        ("num_experts", ctypes.c_int32), ("num_local_experts", ctypes.c_int32), ("expert_offset", ctypes.c_int32),
+        ("hidden", ctypes.c_int32), ("intermediate", ctypes.c_int32), ("top_k", ctypes.c_int32),
+        ("swiglu_alpha", ctypes.c_float), ("swiglu_limit", ctypes.c_float), ("rms_eps", ctypes.c_float),
+        ("norm_weight", ctypes.c_void_p), ("gate_weight", ctypes.c_void_p), ("gate_bias", ctypes.c_void_p),
+        ("mlp1_blocks", ctypes.c_void_p), ("mlp1_scales", ctypes.c_void_p), ("mlp1_bias", ctypes.c_void_p),
+        ("mlp2_blocks", ctypes.c_void_p), ("mlp2_scales", ctypes.c_void_p), ("mlp2_bias", ctypes.c_void_p),
+    ]
+
+
+_P, _I64, _I32, _F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
+
+# name -> (restype, argtypes); mirrors include/gptoss_b200.h
+SIGNATURES = {
+    "gptoss_version": (ctypes.c_int, []),
+    "gptoss_last_error": (ctypes.c_char_p, []),
+    "gptoss_moe_workspace_create": (_P, [_I64, _I32, _I32, _I32, _I32]),
+    "gptoss_moe_workspace_destroy": (None, [_P]),
+    "gptoss_moe_workspace_error": (ctypes.c_uint32, [_P]),
+    "gptoss_moe_forward": (ctypes.c_int, [_P, _I64, ctypes.POINTER(gptoss_moe_weights), _P, _P, _P]),
+    "gptoss_rms_norm": (ctypes.c_int, [_P, _P, _I64, _I32, _F, _P, _P]),
+    "gptoss_moe_router": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P]),
+    "gptoss_moe_topk_softmax": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _P, _P, _P]),
+    "gptoss_moe_permute": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "gptoss_moe_gather": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _P]),
+    "gptoss_moe_mlp1": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _F, _F, _P, _P, _P]),
+    "gptoss_moe_mlp2": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
+    "gptoss_moe_combine": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P]),
+    "gptoss_mxfp4_dequant": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _P]),
+}
+
+_lib = None
+
+
+def load(path: str | None = None) -> ctypes.CDLL:
+    """Load the CUDA library (raises if it was not built)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise GptossError(f"libgptoss_b200.so not found at {p}; build it with __graft_entry__.build()")
+    lib = ctypes.CDLL(p)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name, None)
+        if fn is None:
+            continue
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def check(rc: int) -> None:
+    if rc != 0:
+        msg = load().gptoss_last_error()
+        raise GptossError(f"gptoss call failed ({rc}): {msg.decode() if msg else ''}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))

@@ -1,0 +1,312 @@
+// capi.cu -- the extern "C" boundary of libgptoss_b200.so (see include/gptoss_b200.h).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/gptoss_b200.h"
+#include "common.cuh"
+
+namespace gptoss {
+// moe_route.cu
+int launch_rmsnorm(const uint16_t*, const uint16_t*, int64_t, int32_t, float, uint16_t*, cudaStream_t);
+int launch_router(const uint16_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t, uint16_t*,
+                  cudaStream_t);
+int launch_topk_softmax(const uint16_t*, int64_t, int32_t, int32_t, uint16_t*, int32_t*, uint32_t*, cudaStream_t);
+int launch_permute(const int32_t*, int64_t, int32_t, int32_t, int32_t*, int32_t*, int32_t*, int32_t*, int32_t*,
+                   int32_t*, uint32_t*, cudaStream_t);
+int launch_gather(const uint16_t*, const int32_t*, int64_t, int32_t, uint16_t*, cudaStream_t);
+int launch_combine(const float*, const int32_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t,
+                   uint16_t*, cudaStream_t);
+int launch_mxfp4_dequant(const uint8_t*, const uint8_t*, int64_t, uint16_t*, cudaStream_t);
+// moe_gemm.cu
+struct GemmLaunch {
+  const uint16_t* act;
+  int64_t act_rows;
+  const uint8_t* blocks;
+  const uint8_t* scales;
+  const uint16_t* bias;
+  const int32_t* indptr;
+  const int32_t* tile_ptr;
+  const int32_t* tile_rows;
+  void* out;
+  int32_t E, N, K, ldo;
+  float alpha, limit;
+  uint32_t* err;
+  int grid;
+};
+int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream);
+}  // namespace gptoss
+
+using namespace gptoss;
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+static int check_launch(int rc, const char* what) {
+  if (rc == 0) return 0;
+  cudaError_t e = cudaGetLastError();
+  return fail(rc < 0 ? rc : -3, "%s failed (code %d, cuda: %s)", what, rc, cudaGetErrorString(e));
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+#define GPTOSS_STREAM(s) ((cudaStream_t)(s))
+
+extern "C" {
+
+int gptoss_version(void) { return 1; }
+const char* gptoss_last_error(void) { return g_last_error.c_str(); }
+
+// ---------------------------------------------------------------- pieces --
+int gptoss_rms_norm(const uint16_t* x, const uint16_t* weight, int64_t M, int32_t H, float eps, uint16_t* out,
+                    void* stream) {
+  if (M < 0 || H <= 0 || (H & 1)) return fail(-1, "gptoss_rms_norm: bad shape M=%lld H=%d", (long long)M, H);
+  if (M && (!x || !weight || !out)) return fail(-1, "gptoss_rms_norm: null pointer");
+  return check_launch(launch_rmsnorm(x, weight, M, H, eps, out, GPTOSS_STREAM(stream)), "rms_norm");
+}
+
+int gptoss_moe_router(const uint16_t* t, const uint16_t* gate_weight, const uint16_t* gate_bias, int64_t M,
+                      int32_t E, int32_t H, int32_t K, uint16_t* logits, uint16_t* topk_weights,
+                      int32_t* topk_indices, uint32_t* err, void* stream) {
+  if (M < 0 || E <= 0 || E > 256 || E % 16 || K < 1 || K > 8 || K > E || H <= 0)
+    return fail(-1, "gptoss_moe_router: unsupported shape M=%lld E=%d H=%d K=%d (E must be a multiple of 16, <= 256)",
+                (long long)M, E, H, K);
+  int rc = launch_router(t, gate_weight, gate_bias, M, E, H, logits, GPTOSS_STREAM(stream));
+  if (rc) return check_launch(rc, "router");
+  return check_launch(launch_topk_softmax(logits, M, E, K, topk_weights, topk_indices, err, GPTOSS_STREAM(stream)),
+                      "topk_softmax");
+}
+
+int gptoss_moe_topk_softmax(const uint16_t* logits, int64_t M, int32_t E, int32_t K, uint16_t* topk_weights,
+                            int32_t* topk_indices, uint32_t* err, void* stream) {
+  if (M < 0 || E <= 0 || E > 256 || K < 1 || K > 8 || K > E)
+    return fail(-1, "gptoss_moe_topk_softmax: unsupported shape M=%lld E=%d K=%d", (long long)M, E, K);
+  return check_launch(launch_topk_softmax(logits, M, E, K, topk_weights, topk_indices, err, GPTOSS_STREAM(stream)),
+                      "topk_softmax");
+}
+
+int gptoss_moe_permute(const int32_t* topk_indices, int64_t M, int32_t K, int32_t E, int32_t* indptr,
+                       int32_t* token_of_row, int32_t* row_of_pair, int32_t* expert_of_row, int32_t* tile_ptr,
+                       int32_t* tile_rows, uint32_t* err, void* stream) {
+  if (M < 0 || K < 1 || E < 1 || E > 4096) return fail(-1, "gptoss_moe_permute: bad shape");
+  return check_launch(launch_permute(topk_indices, M, K, E, indptr, tile_ptr, tile_rows, token_of_row, row_of_pair,
+                                     expert_of_row, err, GPTOSS_STREAM(stream)),
+                      "permute");
+}
+
+int gptoss_moe_gather(const uint16_t* t, const int32_t* token_of_row, int64_t rows, int32_t H, uint16_t* act,
+                      void* stream) {
+  if (rows < 0 || H <= 0 || H % 8) return fail(-1, "gptoss_moe_gather: H must be a multiple of 8");
+  return check_launch(launch_gather(t, token_of_row, rows, H, act, GPTOSS_STREAM(stream)), "gather");
+}
+
+static int gemm_common(int mode, const uint16_t* act, int64_t act_rows, const int32_t* indptr,
+                       const int32_t* tile_ptr, const int32_t* tile_rows, int32_t E, int32_t N, int32_t K,
+                       const uint8_t* blocks, const uint8_t* scales, const uint16_t* bias, float alpha, float limit,
+                       void* out, int32_t ldo, uint32_t* err, void* stream) {
+  if (act_rows <= 0) return 0;
+  if (E <= 0 || N <= 0 || K <= 0 || K % 64)
+    return fail(-1, "moe gemm: K must be a positive multiple of 64 (got %d)", K);
+  if (((uintptr_t)act & 15) || ((uintptr_t)blocks & 15) || ((uintptr_t)scales & 15))
+    return fail(-1, "moe gemm: act, blocks and scales must be 16-byte aligned");
+  GemmLaunch L;
+  L.act = act;
+  L.act_rows = act_rows;
+  L.blocks = blocks;
+  L.scales = scales;
+  L.bias = bias;
+  L.indptr = indptr;
+  L.tile_ptr = tile_ptr;
+  L.tile_rows = tile_rows;
+  L.out = out;
+  L.E = E;
+  L.N = N;
+  L.K = K;
+  L.ldo = ldo;
+  L.alpha = alpha;
+  L.limit = limit;
+  L.err = err;
+  L.grid = num_sms();
+  return check_launch(launch_moe_gemm(mode, L, GPTOSS_STREAM(stream)), mode == 0 ? "moe_mlp1" : "moe_mlp2");
+}
+
+int gptoss_moe_mlp1(const uint16_t* act, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
+                    const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
+                    const uint8_t* scales, const uint16_t* bias, float alpha, float limit, uint16_t* y,
+                    uint32_t* err, void* stream) {
+  return gemm_common(0, act, act_rows, indptr, tile_ptr, tile_rows, E, 2 * I, H, blocks, scales, bias, alpha, limit,
+                     y, I, err, stream);
+}
+
+int gptoss_moe_mlp2(const uint16_t* y, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
+                    const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
+                    const uint8_t* scales, const uint16_t* bias, float* h2, uint32_t* err, void* stream) {
+  return gemm_common(1, y, act_rows, indptr, tile_ptr, tile_rows, E, H, I, blocks, scales, bias, 0.f, 0.f, h2, H,
+                     err, stream);
+}
+
+int gptoss_moe_combine(const float* h2, const int32_t* row_of_pair, const uint16_t* topk_weights,
+                       const uint16_t* x, int64_t M, int32_t K, int32_t H, uint16_t* out, void* stream) {
+  if (M < 0 || K < 1 || H <= 0) return fail(-1, "gptoss_moe_combine: bad shape");
+  return check_launch(launch_combine(h2, row_of_pair, topk_weights, x, M, K, H, out, GPTOSS_STREAM(stream)),
+                      "combine");
+}
+
+int gptoss_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t rows, int32_t groups,
+                         uint16_t* out, void* stream) {
+  if (rows < 0 || groups <= 0) return fail(-1, "gptoss_mxfp4_dequant: bad shape");
+  if (((uintptr_t)blocks & 15) || ((uintptr_t)out & 15)) return fail(-1, "gptoss_mxfp4_dequant: 16-byte alignment");
+  return check_launch(launch_mxfp4_dequant(blocks, scales, rows * (int64_t)groups, out, GPTOSS_STREAM(stream)),
+                      "mxfp4_dequant");
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------- workspace --
+struct gptoss_moe_workspace {
+  int64_t max_tokens;
+  int32_t E, K, H, I;
+  void* base;
+  size_t bytes;
+  uint16_t* t;
+  uint16_t* logits;
+  uint16_t* topk_w;
+  int32_t* topk_idx;
+  int32_t* indptr;
+  int32_t* tile_ptr;
+  int32_t* tile_rows;
+  int32_t* token_of_row;
+  int32_t* row_of_pair;
+  int32_t* expert_of_row;
+  uint16_t* act;
+  uint16_t* y;
+  float* h2;
+  uint32_t* err;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+extern "C" {
+
+gptoss_moe_workspace* gptoss_moe_workspace_create(int64_t max_tokens, int32_t num_experts, int32_t top_k,
+                                                  int32_t hidden, int32_t intermediate) {
+  if (max_tokens <= 0 || num_experts <= 0 || top_k <= 0 || hidden <= 0 || intermediate <= 0) {
+    fail(-1, "gptoss_moe_workspace_create: bad sizes");
+    return nullptr;
+  }
+  gptoss_moe_workspace* ws = new gptoss_moe_workspace();
+  ws->max_tokens = max_tokens;
+  ws->E = num_experts;
+  ws->K = top_k;
+  ws->H = hidden;
+  ws->I = intermediate;
+  const int64_t M = max_tokens, R = max_tokens * top_k, E = num_experts;
+  size_t off[16], o = 0;
+  int i = 0;
+  off[i++] = o; o = align256(o + (size_t)M * hidden * 2);        // t
+  off[i++] = o; o = align256(o + (size_t)M * E * 2);             // logits
+  off[i++] = o; o = align256(o + (size_t)M * top_k * 2);         // topk_w
+  off[i++] = o; o = align256(o + (size_t)M * top_k * 4);         // topk_idx
+  off[i++] = o; o = align256(o + (size_t)(E + 1) * 4);           // indptr
+  off[i++] = o; o = align256(o + (size_t)(E + 1) * 4);           // tile_ptr
+  off[i++] = o; o = align256(o + (size_t)E * 4);                 // tile_rows
+  off[i++] = o; o = align256(o + (size_t)R * 4);                 // token_of_row
+  off[i++] = o; o = align256(o + (size_t)R * 4);                 // row_of_pair
+  off[i++] = o; o = align256(o + (size_t)R * 4);                 // expert_of_row
+  off[i++] = o; o = align256(o + (size_t)R * hidden * 2);        // act
+  off[i++] = o; o = align256(o + (size_t)R * intermediate * 2);  // y
+  off[i++] = o; o = align256(o + (size_t)R * hidden * 4);        // h2
+  off[i++] = o; o = align256(o + 256);                           // err
+  ws->bytes = o;
+  if (cudaMalloc(&ws->base, o) != cudaSuccess) {
+    cudaGetLastError();
+    fail(-4, "gptoss_moe_workspace_create: cudaMalloc of %zu bytes failed", o);
+    delete ws;
+    return nullptr;
+  }
+  char* b = (char*)ws->base;
+  i = 0;
+  ws->t = (uint16_t*)(b + off[i++]);
+  ws->logits = (uint16_t*)(b + off[i++]);
+  ws->topk_w = (uint16_t*)(b + off[i++]);
+  ws->topk_idx = (int32_t*)(b + off[i++]);
+  ws->indptr = (int32_t*)(b + off[i++]);
+  ws->tile_ptr = (int32_t*)(b + off[i++]);
+  ws->tile_rows = (int32_t*)(b + off[i++]);
+  ws->token_of_row = (int32_t*)(b + off[i++]);
+  ws->row_of_pair = (int32_t*)(b + off[i++]);
+  ws->expert_of_row = (int32_t*)(b + off[i++]);
+  ws->act = (uint16_t*)(b + off[i++]);
+  ws->y = (uint16_t*)(b + off[i++]);
+  ws->h2 = (float*)(b + off[i++]);
+  ws->err = (uint32_t*)(b + off[i++]);
+  cudaMemset(ws->err, 0, 256);
+  return ws;
+}
+
+void gptoss_moe_workspace_destroy(gptoss_moe_workspace* ws) {
+  if (!ws) return;
+  cudaFree(ws->base);
+  delete ws;
+}
+
+uint32_t gptoss_moe_workspace_error(gptoss_moe_workspace* ws) {
+  if (!ws) return 0;
+  uint32_t v = 0;
+  cudaDeviceSynchronize();
+  cudaMemcpy(&v, ws->err, 4, cudaMemcpyDeviceToHost);
+  cudaMemset(ws->err, 0, 4);
+  return v;
+}
+
+int gptoss_moe_forward(const uint16_t* x, int64_t M, const gptoss_moe_weights* w, gptoss_moe_workspace* ws,
+                       uint16_t* out, void* stream) {
+  if (!w || !ws) return fail(-1, "gptoss_moe_forward: null weights or workspace");
+  if (M < 0 || M > ws->max_tokens)
+    return fail(-1, "gptoss_moe_forward: M=%lld exceeds workspace max_tokens=%lld", (long long)M,
+                (long long)ws->max_tokens);
+  if (w->num_experts != ws->E || w->top_k != ws->K || w->hidden != ws->H || w->intermediate != ws->I)
+    return fail(-1, "gptoss_moe_forward: weights and workspace disagree on shapes");
+  if (w->num_local_experts != w->num_experts || w->expert_offset != 0)
+    return fail(-1, "gptoss_moe_forward: expert-parallel weights need the dispatch/combine path");
+  if (M == 0) return 0;
+  const int32_t E = w->num_experts, K = w->top_k, H = w->hidden, I = w->intermediate;
+  const int64_t R = M * K;
+  int rc;
+  if ((rc = gptoss_rms_norm(x, w->norm_weight, M, H, w->rms_eps, ws->t, stream))) return rc;
+  if ((rc = gptoss_moe_router(ws->t, w->gate_weight, w->gate_bias, M, E, H, K, ws->logits, ws->topk_w, ws->topk_idx,
+                              ws->err, stream)))
+    return rc;
+  if ((rc = gptoss_moe_permute(ws->topk_idx, M, K, E, ws->indptr, ws->token_of_row, ws->row_of_pair,
+                               ws->expert_of_row, ws->tile_ptr, ws->tile_rows, ws->err, stream)))
+    return rc;
+  if ((rc = gptoss_moe_gather(ws->t, ws->token_of_row, R, H, ws->act, stream))) return rc;
+  if ((rc = gptoss_moe_mlp1(ws->act, R, ws->indptr, ws->tile_ptr, ws->tile_rows, E, H, I, w->mlp1_blocks,
+                            w->mlp1_scales, w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, ws->y, ws->err, stream)))
+    return rc;
+  if ((rc = gptoss_moe_mlp2(ws->y, R, ws->indptr, ws->tile_ptr, ws->tile_rows, E, H, I, w->mlp2_blocks,
+                            w->mlp2_scales, w->mlp2_bias, ws->h2, ws->err, stream)))
+    return rc;
+  return gptoss_moe_combine(ws->h2, ws->row_of_pair, ws->topk_w, x, M, K, H, out, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,437 @@
+// moe_gemm.cu -- grouped MXFP4 expert GEMMs on the 5th-generation tensor cores.
+//
+// Computes, for every expert e and every permuted row r of that expert
+// (rows indptr[e] .. indptr[e+1] of the expert-major activation matrix),
+//     h[r, n] = bias[e, n] + sum_k W_e[n, k] * act[r, k]
+// with W_e decoded from the checkpoint's native MXFP4 layout
+// (blocks [E, N, K/32, 16] e2m1 nibbles, scales [E, N, K/32] e8m0), i.e. the
+// run_einsum of model/mlp.py:238-326 and the grouped kernels of
+// model/mlp_optimized.py:214-460, and fuses the epilogue:
+//   mode 0 (gate/up):  y[r, n/2] = bf16(swiglu(h[r, 2j], h[r, 2j+1]))
+//                      (clamped SwiGLU, model/mlp.py:29-60)
+//   mode 1 (down):     out[r, n] = h[r, n]   (fp32, combined later)
+//
+// Design (sm_100a, one persistent CTA per SM):
+//   * The weights are the MMA "A" operand and live in TMEM: four dequant warps
+//     (one warpgroup, one TMEM lane = one weight row each) turn e2m1 nibbles
+//     into exact bf16 and write them with tcgen05.st.  This keeps the shared
+//     memory bandwidth for the activation operand only.
+//   * The activations (expert-major rows, bf16, K-major) are the "B" operand,
+//     brought into 128-byte-swizzled shared memory by TMA.
+//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 256
+//     token rows, K = 16 per instruction) accumulates fp32 in TMEM.
+//   * Nibbles are streamed by TMA (32-byte swizzle) through an 8-deep ring;
+//     each tile's 128 x K/32 scale bytes arrive with one bulk copy.
+// Warp roles: 0-3 dequant + epilogue, 4 activation TMA, 5 MMA issuer (also
+// owns TMEM), 6 weight TMA.
+#include "common.cuh"
+
+namespace gptoss {
+
+constexpr int kGemmThreads = 224;
+constexpr int kBM = 128;            // weight rows per tile (MMA M)
+constexpr int kMaxBN = 256;         // token rows per tile (MMA N, max)
+constexpr int kBK = 64;             // K per pipeline chunk (one 128 B swizzle row of bf16)
+constexpr int kStages = 4;          // activation + TMEM A stages
+constexpr int kWStages = 8;         // nibble ring depth
+constexpr int kActStageBytes = kMaxBN * kBK * 2;   // 32 KB
+constexpr int kWStageBytes = kBM * (kBK / 2);      // 4 KB (128 rows x 32 nibble bytes)
+constexpr int kMaxGroups = 96;                     // K/32 upper bound (K <= 3072)
+constexpr int kScaleBytes = kBM * kMaxGroups;      // per-tile scale buffer (row stride = G)
+constexpr int kAccCols = 256;
+constexpr int kTmemCols = 512;
+constexpr int kAColBase = kAccCols;                // A stage s at columns 256 + 32 s
+
+struct GemmParams {
+  const uint8_t* scales;     // [E, N, G]
+  const uint16_t* bias;      // [E, N] bf16
+  const int32_t* indptr;     // [E + 1]  permuted rows of each expert
+  const int32_t* tile_ptr;   // [E + 1]  prefix sum of token tiles per expert
+  const int32_t* tile_rows;  // [E]      rows per token tile of each expert
+  void* out;                 // mode 0: bf16 [R, N/2]; mode 1: f32 [R, N]
+  int32_t num_experts;
+  int32_t N;                 // weight rows per expert (output features)
+  int32_t K;                 // reduction length (multiple of 64)
+  int32_t ldo;               // output row stride in elements
+  float alpha, limit;        // SwiGLU constants (mode 0)
+  uint32_t* err;
+};
+
+struct GemmSmem {
+  // offsets from the 1024-aligned base
+  static constexpr int kAct = 0;
+  static constexpr int kW = kAct + kStages * kActStageBytes;
+  static constexpr int kScale = kW + kWStages * kWStageBytes;
+  static constexpr int kBar = kScale + 2 * kScaleBytes;
+  static constexpr int kNumBars = 2 * kStages + 2 * kWStages + 4 + 2;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kTotal = kMisc + 64;
+  static constexpr int kAlloc = kTotal + 1024;  // slack for manual 1024 B alignment
+};
+
+struct TileInfo {
+  int32_t expert, row0, nrows, f0;
+};
+
+// Tile t -> (expert, first permuted row, rows, first feature row).
+__device__ __forceinline__ bool decode_tile(const GemmParams& p, int32_t t, int32_t ftiles, TileInfo& ti) {
+  const int32_t g = t / ftiles;
+  const int32_t f = t - g * ftiles;
+  int32_t lo = 0, hi = p.num_experts;  // find e with tile_ptr[e] <= g < tile_ptr[e+1]
+  while (hi - lo > 1) {
+    int32_t mid = (lo + hi) >> 1;
+    if (__ldg(p.tile_ptr + mid) <= g) lo = mid; else hi = mid;
+  }
+  const int32_t e = lo;
+  const int32_t tt = g - __ldg(p.tile_ptr + e);
+  const int32_t per = __ldg(p.tile_rows + e);
+  const int32_t base = __ldg(p.indptr + e);
+  const int32_t cnt = __ldg(p.indptr + e + 1) - base;
+  ti.expert = e;
+  ti.row0 = base + tt * per;
+  ti.nrows = min(per, cnt - tt * per);
+  ti.f0 = f * kBM;
+  return ti.nrows > 0;
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_w,
+                       const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* act_s = smem + GemmSmem::kAct;
+  uint8_t* w_s = smem + GemmSmem::kW;
+  uint8_t* sc_s = smem + GemmSmem::kScale;
+  uint64_t* bars = (uint64_t*)(smem + GemmSmem::kBar);
+  uint64_t* full_bar = bars;                      // [kStages] act TMA tx + 4 dequant warps
+  uint64_t* empty_bar = full_bar + kStages;       // [kStages] MMA commit
+  uint64_t* wfull_bar = empty_bar + kStages;      // [kWStages] nibble TMA tx
+  uint64_t* wempty_bar = wfull_bar + kWStages;    // [kWStages] 4 dequant warps
+  uint64_t* scfull_bar = wempty_bar + kWStages;   // [2] scale bulk copy tx
+  uint64_t* scempty_bar = scfull_bar + 2;         // [2] 4 dequant warps
+  uint64_t* accfull_bar = scempty_bar + 2;        // MMA commit
+  uint64_t* accempty_bar = accfull_bar + 1;       // 4 epilogue warps
+  uint32_t* misc = (uint32_t*)(smem + GemmSmem::kMisc);
+  volatile uint32_t* tmem_slot = misc;
+  volatile uint32_t* abort_s = misc + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int32_t G = p.K >> 5;
+  const int32_t nchunks = p.K / kBK;
+  const int32_t ftiles = (p.N + kBM - 1) / kBM;
+  const int32_t total_tiles = __ldg(p.tile_ptr + p.num_experts) * ftiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 5);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int s = 0; s < kWStages; ++s) {
+      mbar_init(&wfull_bar[s], 1);
+      mbar_init(&wempty_bar[s], 4);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&scfull_bar[s], 1);
+      mbar_init(&scempty_bar[s], 4);
+    }
+    mbar_init(accfull_bar, 1);
+    mbar_init(accempty_bar, 4);
+    *abort_s = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc((uint32_t*)tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmap_act);
+    tma_prefetch_desc(&tmap_w);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------ activation producer
+    if (elect_one()) {
+      uint32_t it = 0;
+      for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
+        TileInfo ti;
+        if (!decode_tile(p, t, ftiles, ti)) continue;
+        const int32_t nbox = (ti.nrows + 63) >> 6;
+        for (int32_t c = 0; c < nchunks; ++c, ++it) {
+          const uint32_t s = it % kStages, ph = (it / kStages) & 1;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
+          mbar_arrive_expect_tx(&full_bar[s], (uint32_t)nbox * 64 * 128);
+          for (int32_t b = 0; b < nbox; ++b)
+            tma_load_2d(act_s + s * kActStageBytes + b * 8192, &tmap_act, c * kBK, ti.row0 + b * 64, &full_bar[s]);
+        }
+      }
+    }
+  } else if (warp == 6) {
+    // ---------------------------------------------------- weight producer
+    if (elect_one()) {
+      uint32_t wit = 0, tl = 0;
+      for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
+        TileInfo ti;
+        if (!decode_tile(p, t, ftiles, ti)) continue;
+        const uint32_t sb = tl & 1, sph = (tl >> 1) & 1;
+        ++tl;
+        if (!mbar_wait(&scempty_bar[sb], sph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
+        const int32_t frows = min(kBM, p.N - ti.f0);
+        const uint32_t sbytes = (uint32_t)(frows * G);
+        mbar_arrive_expect_tx(&scfull_bar[sb], sbytes);
+        const uint8_t* src = p.scales + ((size_t)ti.expert * p.N + ti.f0) * G;
+        asm volatile(
+            "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(sc_s + sb * kScaleBytes)),
+            "l"(src), "r"(sbytes), "r"(smem_u32(&scfull_bar[sb]))
+            : "memory");
+        const int32_t wrow = ti.expert * p.N + ti.f0;
+        for (int32_t c = 0; c < nchunks; ++c, ++wit) {
+          const uint32_t s = wit % kWStages, ph = (wit / kWStages) & 1;
+          if (!mbar_wait(&wempty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
+          mbar_arrive_expect_tx(&wfull_bar[s], kWStageBytes);
+          tma_load_2d(w_s + s * kWStageBytes, &tmap_w, c * (kBK / 2), wrow, &wfull_bar[s]);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // --------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      uint32_t it = 0, tl = 0;
+      for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
+        TileInfo ti;
+        if (!decode_tile(p, t, ftiles, ti)) continue;
+        const uint32_t n_mma = (uint32_t)((ti.nrows + 15) & ~15);
+        const uint32_t idesc = make_idesc_bf16(kBM, n_mma);
+        if (!mbar_wait(accempty_bar, (tl & 1) ^ 1, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
+        tc_fence_after();
+        bool ok = true;
+        for (int32_t c = 0; c < nchunks; ++c, ++it) {
+          const uint32_t s = it % kStages, ph = (it / kStages) & 1;
+          if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t b_base = smem_u32(act_s + s * kActStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            tc_mma_ts(tmem_base, tmem_base + kAColBase + s * 32 + kk * 8, make_sdesc_sw128(b_base + kk * 32), idesc,
+                      (c > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty_bar[s]);
+        }
+        if (!ok) { *abort_s = 1; break; }
+        tc_commit(accfull_bar);
+        ++tl;
+      }
+    }
+  } else {
+    // ------------------------------------- dequant (weights -> TMEM) + epilogue
+    const int row = threadIdx.x;  // weight row within the tile == TMEM lane
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    uint32_t it = 0, wit = 0, tl = 0;
+    for (int32_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      TileInfo ti;
+      if (!decode_tile(p, t, ftiles, ti)) continue;
+      if (*abort_s) break;
+      const uint32_t sb = tl & 1, sph = (tl >> 1) & 1;
+      const int32_t frow = ti.f0 + row;
+      const bool row_ok = frow < p.N;
+      bool ok = mbar_wait(&scfull_bar[sb], sph, p.err, kErrTimeoutFull);
+      const uint8_t* srow = sc_s + sb * kScaleBytes + row * G;
+      for (int32_t c = 0; c < nchunks && ok; ++c, ++it, ++wit) {
+        const uint32_t ws = wit % kWStages, wph = (wit / kWStages) & 1;
+        const uint32_t s = it % kStages, ph = (it / kStages) & 1;
+        ok = mbar_wait(&wfull_bar[ws], wph, p.err, kErrTimeoutFull);
+        if (!ok) break;
+        // nibbles of this row: 32 bytes, 32-byte-swizzled rows (16-byte halves
+        // swapped on rows whose bit 2 is set)
+        const uint8_t* wrow = w_s + ws * kWStageBytes + row * 32;
+        const uint32_t sw = (row >> 2) & 1;
+        uint4 n0 = *(const uint4*)(wrow + (sw << 4));
+        uint4 n1 = *(const uint4*)(wrow + ((sw ^ 1) << 4));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wempty_bar[ws]);
+        const uint32_t s0 = srow[2 * c], s1 = srow[2 * c + 1];
+        uint32_t r[32];
+        if (row_ok) {
+          const uint32_t sc0 = e8m0_scale_bf16x2(s0), sc1 = e8m0_scale_bf16x2(s1);
+          uint32_t o[4];
+          fp4x8_to_bf16x8(n0.x, sc0, o); r[0] = o[0]; r[1] = o[1]; r[2] = o[2]; r[3] = o[3];
+          fp4x8_to_bf16x8(n0.y, sc0, o); r[4] = o[0]; r[5] = o[1]; r[6] = o[2]; r[7] = o[3];
+          fp4x8_to_bf16x8(n0.z, sc0, o); r[8] = o[0]; r[9] = o[1]; r[10] = o[2]; r[11] = o[3];
+          fp4x8_to_bf16x8(n0.w, sc0, o); r[12] = o[0]; r[13] = o[1]; r[14] = o[2]; r[15] = o[3];
+          fp4x8_to_bf16x8(n1.x, sc1, o); r[16] = o[0]; r[17] = o[1]; r[18] = o[2]; r[19] = o[3];
+          fp4x8_to_bf16x8(n1.y, sc1, o); r[20] = o[0]; r[21] = o[1]; r[22] = o[2]; r[23] = o[3];
+          fp4x8_to_bf16x8(n1.z, sc1, o); r[24] = o[0]; r[25] = o[1]; r[26] = o[2]; r[27] = o[3];
+          fp4x8_to_bf16x8(n1.w, sc1, o); r[28] = o[0]; r[29] = o[1]; r[30] = o[2]; r[31] = o[3];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = 0u;
+        }
+        ok = mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty);
+        if (!ok) break;
+        __syncwarp();
+        tc_fence_after();
+        tmem_st_x32(tmem_base + lane_base + kAColBase + s * 32, r);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_bar[s]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&scempty_bar[sb]);
+      if (!ok) { *abort_s = 1; break; }
+
+      // ---- epilogue: TMEM accumulator -> registers -> global
+      if (!mbar_wait(accfull_bar, tl & 1, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
+      __syncwarp();
+      tc_fence_after();
+      const float bias = row_ok ? bf16_bits_to_f32(__ldg(p.bias + (size_t)ti.expert * p.N + frow)) : 0.0f;
+      const int32_t ncols = (ti.nrows + 31) & ~31;
+      for (int32_t c0 = 0; c0 < ncols; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_x32(tmem_base + lane_base + (uint32_t)c0, v);
+        tmem_ld_wait();
+        if (kMode == 0) {
+          // lanes (2j, 2j+1) hold the glu / linear rows of output column j
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float h = __uint_as_float(v[j]) + bias;
+            const float partner = __shfl_xor_sync(0xffffffffu, h, 1);
+            const int32_t col = c0 + j;
+            if (!(lane & 1) && row_ok && col < ti.nrows) {
+              const float g = fminf(h, p.limit);
+              const float l = fmaxf(fminf(partner, p.limit), -p.limit);
+              const float sg = 1.0f / (1.0f + expf(-(p.alpha * g)));
+              const float y = (g * sg) * (l + 1.0f);
+              uint16_t* out = (uint16_t*)p.out;
+              out[(size_t)(ti.row0 + col) * p.ldo + (frow >> 1)] = f32_to_bf16_bits(y);
+            }
+          }
+        } else {
+          float* out = (float*)p.out;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int32_t col = c0 + j;
+            if (row_ok && col < ti.nrows)
+              out[(size_t)(ti.row0 + col) * p.ldo + frow] = __uint_as_float(v[j]) + bias;
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(accempty_bar);
+      ++tl;
+    }
+  }
+
+  // ---- teardown: everyone drains, then the allocating warp frees TMEM
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host --
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static PFN_encodeTiled get_encode_fn() {
+  static PFN_encodeTiled fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_encodeTiled)ptr;
+  }
+  return fn;
+}
+
+// 2-D tensor map over a row-major matrix [rows, cols] of `esize`-byte elements.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int esize, uint64_t rows,
+                 uint64_t cols, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * (uint64_t)esize};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
+struct GemmLaunch {
+  const uint16_t* act;       // [R_alloc, K] bf16
+  int64_t act_rows;          // R_alloc
+  const uint8_t* blocks;     // [E, N, G, 16]
+  const uint8_t* scales;     // [E, N, G]
+  const uint16_t* bias;      // [E, N]
+  const int32_t* indptr;
+  const int32_t* tile_ptr;
+  const int32_t* tile_rows;
+  void* out;
+  int32_t E, N, K, ldo;
+  float alpha, limit;
+  uint32_t* err;
+  int grid;
+};
+
+int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
+  if (L.K % kBK != 0 || L.K / 32 > kMaxGroups) return -10;
+  {
+    // every tile's scale block must be a whole number of 16-byte units
+    const int32_t G = L.K / 32;
+    const int32_t last = L.N % kBM ? L.N % kBM : kBM;
+    if (((int64_t)kBM * G) % 16 || ((int64_t)last * G) % 16 || ((int64_t)L.N * G) % 16) return -11;
+  }
+  CUtensorMap tmap_act, tmap_w;
+  int rc = make_tmap_2d(&tmap_act, L.act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)L.act_rows,
+                        (uint64_t)L.K, kBK, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tmap_w, L.blocks, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)L.E * L.N, (uint64_t)L.K / 2,
+                    kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_32B);
+  if (rc) return rc;
+  GemmParams p;
+  p.scales = L.scales;
+  p.bias = L.bias;
+  p.indptr = L.indptr;
+  p.tile_ptr = L.tile_ptr;
+  p.tile_rows = L.tile_rows;
+  p.out = L.out;
+  p.num_experts = L.E;
+  p.N = L.N;
+  p.K = L.K;
+  p.ldo = L.ldo;
+  p.alpha = L.alpha;
+  p.limit = L.limit;
+  p.err = L.err;
+  const int smem = GemmSmem::kAlloc;
+  if (mode == 0) {
+    static bool attr0 = false;
+    if (!attr0) {
+      cudaFuncSetAttribute(moe_gemm_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      attr0 = true;
+    }
+    moe_gemm_tc_kernel<0><<<L.grid, kGemmThreads, smem, stream>>>(tmap_act, tmap_w, p);
+  } else {
+    static bool attr1 = false;
+    if (!attr1) {
+      cudaFuncSetAttribute(moe_gemm_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      attr1 = true;
+    }
+    moe_gemm_tc_kernel<1><<<L.grid, kGemmThreads, smem, stream>>>(tmap_act, tmap_w, p);
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+}  // namespace gptoss

@@ -1,0 +1,140 @@
+/*
+ * gptoss_b200.h -- C ABI of libgptoss_b200.so, the B200 (sm_100a) kernels for
+ * the gpt-oss MXFP4 mixture-of-experts block and sink/YaRN attention.
+ *
+ * Conventions
+ *   - Destination-passing style: the caller owns every input and output
+ *     buffer (device memory) and passes plain pointers and sizes.  bf16 data
+ *     is passed as uint16_t bit patterns.
+ *   - Every call is asynchronous on the given CUDA stream (`stream` is a
+ *     cudaStream_t; NULL = legacy default stream) and returns 0 on success
+ *     or a negative code; gptoss_last_error() describes the last failure of
+ *     the calling host thread.  Calls on one workspace are not re-entrant.
+ *   - Device-side failures (a bounded wait that ran out, an expert index out
+ *     of range) set bits in the workspace's device error word, read with
+ *     gptoss_moe_workspace_error().
+ *
+ * Each entry point names the reference (brekkylab/gpt-oss-tvm) interface it
+ * replaces.  In the reference these are TIR kernels registered with
+ * nn.tensor_ir_op (DPS, single stream) and Relax ops inside MLPBlock.forward
+ * (model/mlp.py:371-402) and AttentionBlock.forward (model/attention.py:182-256).
+ */
+#ifndef GPTOSS_B200_H_
+#define GPTOSS_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+int gptoss_version(void);
+const char* gptoss_last_error(void);
+
+/* ------------------------------------------------------------ MoE weights
+ * The reference MLPBlock parameters, unchanged (model/mlp.py:81-143):
+ *   norm_weight [H], gate_weight [E, H], gate_bias [E] (bf16);
+ *   mlp1_blocks [E, 2I, K/32, 16] u8, mlp1_scales [E, 2I, K/32] u8,
+ *   mlp1_bias [E, 2I] bf16; mlp2_blocks [E, H, I/32, 16] u8,
+ *   mlp2_scales [E, H, I/32] u8, mlp2_bias [E, H] bf16.
+ * With expert parallelism the mlp* pointers cover the `num_local_experts`
+ * experts [expert_offset, expert_offset + num_local_experts); the router
+ * (gate_*) always covers all `num_experts`. */
+typedef struct gptoss_moe_weights {
+  int32_t num_experts;
+  int32_t num_local_experts;
+  int32_t expert_offset;
+  int32_t hidden;        /* H = 2880 */
+  int32_t intermediate;  /* I = 2880 */
+  int32_t top_k;         /* 4 */
+  float swiglu_alpha;    /* 1.702 */
+  float swiglu_limit;    /* 7.0 */
+  float rms_eps;         /* 1e-5 */
+  const uint16_t* norm_weight;
+  const uint16_t* gate_weight;
+  const uint16_t* gate_bias;
+  const uint8_t* mlp1_blocks;
+  const uint8_t* mlp1_scales;
+  const uint16_t* mlp1_bias;
+  const uint8_t* mlp2_blocks;
+  const uint8_t* mlp2_scales;
+  const uint16_t* mlp2_bias;
+} gptoss_moe_weights;
+
+/* Scratch for gptoss_moe_forward (device memory owned by the library). */
+typedef struct gptoss_moe_workspace gptoss_moe_workspace;
+
+gptoss_moe_workspace* gptoss_moe_workspace_create(int64_t max_tokens, int32_t num_experts, int32_t top_k,
+                                                  int32_t hidden, int32_t intermediate);
+void gptoss_moe_workspace_destroy(gptoss_moe_workspace* ws);
+/* Device error word of the workspace (synchronises the device); clears it. */
+uint32_t gptoss_moe_workspace_error(gptoss_moe_workspace* ws);
+
+/* MLPBlock.forward (model/mlp.py:371-402): out = x + MoE(RMSNorm(x)).
+ * x, out: [M, H] bf16 (may alias).  M <= max_tokens of the workspace. */
+int gptoss_moe_forward(const uint16_t* x, int64_t M, const gptoss_moe_weights* w, gptoss_moe_workspace* ws,
+                       uint16_t* out, void* stream);
+
+/* ------------------------------------------------------ MoE building blocks */
+/* nn.RMSNorm (model/mlp.py:81-87, :375; model/attention.py:84, :193).
+ * Bit-exact to the reference's CPU lowering. */
+int gptoss_rms_norm(const uint16_t* x, const uint16_t* weight, int64_t M, int32_t H, float eps, uint16_t* out,
+                    void* stream);
+
+/* self.gate + nn.op.topk + nn.op.softmax (model/mlp.py:376, :381-382).
+ * t [M, H] bf16 (normed), gate_weight [E, H], gate_bias [E] -> logits [M, E]
+ * bf16, topk_weights [M, K] bf16, topk_indices [M, K] int32.  Bit-exact.
+ * err: optional device word for out-of-range detection (may be NULL). */
+int gptoss_moe_router(const uint16_t* t, const uint16_t* gate_weight, const uint16_t* gate_bias, int64_t M,
+                      int32_t E, int32_t H, int32_t K, uint16_t* logits, uint16_t* topk_weights,
+                      int32_t* topk_indices, uint32_t* err, void* stream);
+
+/* nn.op.topk(largest=True) + nn.op.softmax (model/mlp.py:381-382) on given
+ * bf16 logits [M, E] (E <= 256, K <= 8).  Bit-exact. */
+int gptoss_moe_topk_softmax(const uint16_t* logits, int64_t M, int32_t E, int32_t K, uint16_t* topk_weights,
+                            int32_t* topk_indices, uint32_t* err, void* stream);
+
+/* moe_cumsum / get_indices / get_indptr / moe_expand_indptr
+ * (model/mlp_optimized.py:118-148): expert-major order of the M*K
+ * (token, rank) pairs, token-ascending within an expert.  Bit-exact.
+ *   indptr [E+1], token_of_row [M*K], row_of_pair [M*K], expert_of_row [M*K],
+ *   tile_ptr [E+1], tile_rows [E] (token tiles of the grouped GEMMs). */
+int gptoss_moe_permute(const int32_t* topk_indices, int64_t M, int32_t K, int32_t E, int32_t* indptr,
+                       int32_t* token_of_row, int32_t* row_of_pair, int32_t* expert_of_row, int32_t* tile_ptr,
+                       int32_t* tile_rows, uint32_t* err, void* stream);
+
+/* nn.op.take(t, token_indices) (model/mlp_optimized.py:150): act[r] = t[token_of_row[r]]. */
+int gptoss_moe_gather(const uint16_t* t, const int32_t* token_of_row, int64_t rows, int32_t H, uint16_t* act,
+                      void* stream);
+
+/* run_einsum(mlp1) + swiglu (model/mlp.py:238-326, :29-60, :387-390;
+ * grouped form mxfp4_moe_mlp1_prefill, model/mlp_optimized.py:214-351).
+ * act [act_rows, H] bf16 expert-major; weights of E experts;
+ * y [act_rows, I] bf16.  Tolerance (bf16) vs. the reference. */
+int gptoss_moe_mlp1(const uint16_t* act, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
+                    const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
+                    const uint8_t* scales, const uint16_t* bias, float alpha, float limit, uint16_t* y,
+                    uint32_t* err, void* stream);
+
+/* run_einsum(mlp2) (model/mlp.py:395; grouped form mxfp4_moe_mlp2_prefill,
+ * model/mlp_optimized.py:353-460).  y [rows, I] bf16 -> h2 [rows, H] fp32. */
+int gptoss_moe_mlp2(const uint16_t* y, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
+                    const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
+                    const uint8_t* scales, const uint16_t* bias, float* h2, uint32_t* err, void* stream);
+
+/* run_gating + residual (model/mlp.py:328-369, :398-402):
+ * out[m] = bf16(x[m] + bf16(sum_r h2[row_of_pair[m,r]] * w[m,r])). */
+int gptoss_moe_combine(const float* h2, const int32_t* row_of_pair, const uint16_t* topk_weights,
+                       const uint16_t* x, int64_t M, int32_t K, int32_t H, uint16_t* out, void* stream);
+
+/* MLPBlock.__dequantize_mxfp4_weight (model/mlp.py:146-236): exact decode of
+ * MXFP4 blocks [rows, G, 16] + scales [rows, G] to bf16 [rows, G*32]. */
+int gptoss_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t rows, int32_t groups,
+                         uint16_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPTOSS_B200_H_ */

@@ -1,0 +1,226 @@
+"""GPU parity of the MoE block (C ABI) against the CPU oracle.
+
+Bit-exact: RMSNorm, router logits, top-k indices and softmax weights, the
+expert-major permutation and the MXFP4 decode.  Tolerance (bf16): the
+expert GEMM outputs and the block output, with
+max|gpu - ref| / max|ref| <= 2e-2 and cosine >= 0.9995.
+"""
+import numpy as np
+import pytest
+
+from conftest import golden, synth
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+import gpu_util as G  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def params_e8():
+    return synth().moe_params(8, seed=10)
+
+
+def _check_routing(r, ref, M, E, k=4):
+    np.testing.assert_array_equal(r["t"], ref["t"])
+    np.testing.assert_array_equal(r["logits"], ref["logits"])
+    np.testing.assert_array_equal(r["indices"], ref["indices"])
+    np.testing.assert_array_equal(r["weights"], ref["weights"])
+
+
+def _check_permutation(oracle, r, E, k=4):
+    indptr, tok, rev, exp_ = oracle.moe_permute(r["indices"], E)
+    np.testing.assert_array_equal(r["indptr"], indptr)
+    np.testing.assert_array_equal(r["token_of_row"], tok)
+    np.testing.assert_array_equal(r["row_of_pair"], rev)
+    np.testing.assert_array_equal(r["expert_of_row"], exp_)
+
+
+def _check_experts(oracle, r, ref, rows=None):
+    """y and h2 of the sampled tokens (permuted rows) against the oracle."""
+    M, k = r["indices"].shape
+    rows = np.arange(M) if rows is None else rows
+    rev = r["row_of_pair"].reshape(M, k)
+    y_gpu = G.f32(r["y"])[rev[rows].ravel()]
+    y_ref = ref["y"][rows].reshape(-1, ref["y"].shape[-1])
+    G.tol_check(y_gpu, y_ref, what="mlp1+swiglu")
+    h2_gpu = r["h2"][rev[rows].ravel()]
+    h2_ref = ref["h2"][rows].reshape(-1, ref["h2"].shape[-1])
+    G.tol_check(h2_gpu, h2_ref, what="mlp2")
+    G.tol_check(G.f32(r["out"][rows]) - G.f32(ref["x"][rows]), G.f32(ref["gated"][rows]), what="gated sum")
+    G.tol_check(G.f32(r["out"][rows]), G.f32(ref["out"][rows]), what="block output")
+
+
+@pytest.mark.parametrize("M", [1, 5, 37, 300])
+def test_moe_block_e8(oracle, params_e8, M):
+    x = synth().activations(M, seed=100 + M)
+    rows = None if M <= 40 else np.sort(np.random.default_rng(M).choice(M, 24, replace=False))
+    mask = None
+    if rows is not None:
+        mask = np.zeros(M, np.uint8)
+        mask[rows] = 1
+    ref = oracle.moe_forward(x, params_e8, rows_mask=mask, return_all=True)
+    ref["x"] = x
+    r = G.MoEPieces(params_e8).run(x)
+    _check_routing(r, ref, M, 8)
+    _check_permutation(oracle, r, 8)
+    _check_experts(oracle, r, ref, rows)
+
+
+def test_moe_forward_entry_point_matches_pieces(params_e8):
+    """gptoss_moe_forward (one call, library workspace) == the step-by-step path."""
+    import importlib
+    mlp = importlib.import_module("gpt-oss-tvm_b200.mlp")
+    cfg = importlib.import_module("gpt-oss-tvm_b200.config").GPTOssConfig(num_experts=8)
+    blk = mlp.MLPBlock(cfg).load_state(params_e8)
+    x = synth().activations(64, seed=7)
+    out = blk.forward(G.dev(x).reshape(1, 64, 2880))
+    r = G.MoEPieces(params_e8).run(x)
+    np.testing.assert_array_equal(G.host(out).reshape(64, 2880), r["out"])
+    assert blk.device_error() == 0
+
+
+def test_golden_moe_e8_reference_outputs():
+    """Against the reference's own outputs (TVM C target), no oracle involved."""
+    f = golden("moe_e8.npz")
+    p = synth().moe_params(8, seed=10)
+    pieces = G.MoEPieces(p)
+    for M in (1, 5, 16):
+        x = synth().activations(M, seed=int(f[f"m{M}_xseed"]))
+        r = pieces.run(x)
+        np.testing.assert_array_equal(r["logits"], f[f"m{M}_logits"])
+        np.testing.assert_array_equal(r["indices"], f[f"m{M}_indices"])
+        np.testing.assert_array_equal(r["weights"], f[f"m{M}_weights"])
+        G.tol_check(G.f32(r["out"]), G.f32(f[f"m{M}_out"]), what=f"block output M={M}")
+        G.tol_check(G.f32(r["out"]) - G.f32(x), G.f32(f[f"m{M}_gated"].reshape(M, -1)), what=f"gated M={M}")
+
+
+def test_golden_config0_reference_outputs():
+    """gpt-oss-20b MoE block (config 0): 1 decode token and 128 prefill tokens."""
+    f = golden("moe_cfg0.npz")
+    p = synth().moe_params(32, seed=0)
+    pieces = G.MoEPieces(p)
+    x1 = synth().activations(1, seed=1)
+    r = pieces.run(x1)
+    for key in ("t", "logits", "indices", "weights"):
+        np.testing.assert_array_equal(r[key], f["m1_" + key])
+    G.tol_check(G.f32(r["out"]), G.f32(f["m1_out"]), what="config0 decode")
+    x = synth().activations(128, seed=1)
+    r = pieces.run(x)
+    np.testing.assert_array_equal(r["logits"], f["m128_logits"])
+    np.testing.assert_array_equal(r["indices"], f["m128_indices"])
+    np.testing.assert_array_equal(r["weights"], f["m128_weights"])
+    G.tol_check(G.f32(r["out"]), G.f32(f["m128_out"]), what="config0 prefill")
+    G.tol_check(G.f32(r["out"]) - G.f32(x), G.f32(f["m128_out"]) - G.f32(x), what="config0 prefill moe part")
+
+
+def test_config3_scale_routing_bit_exact_and_sampled_experts(oracle):
+    """gpt-oss-120b MoE layer at full prefill size (8192 tokens, 128 experts):
+    routing and permutation bit-exact for every token, expert outputs on a
+    sample of tokens."""
+    S = synth()
+    p = S.moe_params(128, seed=0)
+    M = 8192
+    x = S.activations(M, seed=1)
+    r = G.MoEPieces(p).run(x)
+    t = oracle.rms_norm(x, p["norm_weight"])
+    np.testing.assert_array_equal(r["t"], t)
+    g = oracle.router(t, p["gate_weight"], p["gate_bias"])
+    np.testing.assert_array_equal(r["logits"], g)
+    w, idx, _ = oracle.topk_softmax(g, 4)
+    np.testing.assert_array_equal(r["indices"], idx)
+    np.testing.assert_array_equal(r["weights"], w)
+    _check_permutation(oracle, r, 128)
+    counts = np.diff(r["indptr"])
+    assert counts.max() > 256, "expected some expert with more than one token tile"
+    rows = np.sort(np.random.default_rng(3).choice(M, 12, replace=False))
+    # include a token of the most loaded expert
+    e_max = int(np.argmax(counts))
+    rows = np.unique(np.concatenate([rows, [int(r["token_of_row"][r["indptr"][e_max + 1] - 1])]]))
+    mask = np.zeros(M, np.uint8)
+    mask[rows] = 1
+    ref = oracle.moe_forward(x, p, rows_mask=mask, return_all=True)
+    ref["x"] = x
+    _check_experts(oracle, r, ref, rows)
+
+
+def test_forced_routing_multi_tile_and_empty_experts(oracle, params_e8):
+    """Every token routed to experts 0..3 (600 rows each -> 3 token tiles per
+    expert, 4 empty experts)."""
+    M = 600
+    x = synth().activations(M, seed=9)
+    idx = np.tile(np.array([[2, 0, 3, 1]], np.int32), (M, 1))
+    wts = synth().bf16_bits(np.tile(np.array([[0.4, 0.3, 0.2, 0.1]], np.float32), (M, 1)))
+    r = G.MoEPieces(params_e8).run(x, routing=(wts, idx))
+    indptr, tok, rev, _ = oracle.moe_permute(idx, 8)
+    np.testing.assert_array_equal(r["indptr"], indptr)
+    np.testing.assert_array_equal(r["tile_ptr"], [0, 3, 6, 9, 12, 12, 12, 12, 12])
+    rows = np.array([0, 1, 255, 256, 257, 511, 512, 599])
+    t = oracle.rms_norm(x, params_e8["norm_weight"])
+    h1 = oracle.moe_einsum(t[rows], idx[rows], params_e8["mlp1_weight_blocks"], params_e8["mlp1_weight_scales"],
+                           params_e8["mlp1_bias"])
+    y = oracle.swiglu(h1)
+    h2 = oracle.moe_einsum(y, idx[rows], params_e8["mlp2_weight_blocks"], params_e8["mlp2_weight_scales"],
+                           params_e8["mlp2_bias"])
+    revm = r["row_of_pair"].reshape(M, 4)
+    G.tol_check(G.f32(r["y"])[revm[rows].ravel()], y.reshape(-1, 2880), what="forced mlp1")
+    G.tol_check(r["h2"][revm[rows].ravel()], h2.reshape(-1, 2880), what="forced mlp2")
+    _, out = oracle.gating_residual(h2, wts[rows], x[rows])
+    G.tol_check(G.f32(r["out"][rows]), G.f32(out), what="forced output")
+
+
+def test_topk_ties_golden():
+    f = golden("topk_ties.npz")
+    logits = G.dev(f["logits"])
+    M, E = f["logits"].shape
+    w = torch.empty(M, 4, dtype=torch.bfloat16, device="cuda")
+    idx = torch.empty(M, 4, dtype=torch.int32, device="cuda")
+    G.call("gptoss_moe_topk_softmax", G.P(logits), M, E, 4, G.P(w), G.P(idx), None, G.S())
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(G.host(idx), f["indices"])
+    np.testing.assert_array_equal(G.host(w), f["weights"])
+
+
+def test_mxfp4_dequant_bit_exact_all_scale_codes(oracle):
+    rng = np.random.default_rng(11)
+    rows, Gr = 300, 90
+    blocks = rng.integers(0, 256, size=(rows, Gr, 16), dtype=np.uint8)
+    scales = (np.arange(rows * Gr) % 255).astype(np.uint8).reshape(rows, Gr)  # every code 0..254
+    out = torch.empty(rows, Gr * 32, dtype=torch.bfloat16, device="cuda")
+    G.call("gptoss_mxfp4_dequant", G.P(G.dev(blocks)), G.P(G.dev(scales)), rows, Gr, G.P(out), G.S())
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(G.host(out), oracle.mxfp4_dequant(blocks, scales))
+
+
+def test_mxfp4_dequant_golden_reference():
+    f = golden("mxfp4_decode.npz")
+    rng = np.random.default_rng(5)
+    blocks = rng.integers(0, 256, size=(2, 5760, 90, 16), dtype=np.uint8)
+    scales = rng.integers(100, 150, size=(2, 5760, 90), dtype=np.uint8)
+    scales[0, :8, :] = np.arange(8 * 90).reshape(8, 90) % 256
+    scales[0, :8, :][scales[0, :8, :] == 255] = 254
+    b = np.ascontiguousarray(blocks[:, :64])
+    s = np.ascontiguousarray(scales[:, :64])
+    out = torch.empty(2 * 64, 2880, dtype=torch.bfloat16, device="cuda")
+    G.call("gptoss_mxfp4_dequant", G.P(G.dev(b)), G.P(G.dev(s)), 128, 90, G.P(out), G.S())
+    torch.cuda.synchronize()
+    dec = G.f32(G.host(out)).reshape(2, 64, 2880)
+    kpos, ref = f["kpos"], f["out_rows"]
+    for si in range(64):
+        for rr, e in enumerate((0, 1, 0, 1)):
+            np.testing.assert_array_equal(dec[e, :, kpos[si]] + np.float32(0), ref[si, rr] + np.float32(0))
+
+
+def test_rmsnorm_bit_exact_odd_sizes(oracle):
+    rng = np.random.default_rng(12)
+    for M in (1, 33, 257):
+        x = synth().bf16_bits(rng.standard_normal((M, 2880)).astype(np.float32) * 3)
+        w = synth().bf16_bits(rng.standard_normal(2880).astype(np.float32))
+        out = torch.empty(M, 2880, dtype=torch.bfloat16, device="cuda")
+        G.call("gptoss_rms_norm", G.P(G.dev(x)), G.P(G.dev(w)), M, 2880, G.ctypes.c_float(1e-5),
+               G.P(out), G.S())
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(G.host(out), oracle.rms_norm(x, w))
