@@ -34,7 +34,7 @@ import time
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
-TOKENS = 8192
+TOKENS = 8192  # default; --tokens overrides (smaller cases for profiling)
 NUM_EXPERTS = 128
 TOP_K = 4
 HIDDEN = 2880
@@ -302,16 +302,19 @@ def run_reference(args):
 
 
 def main():
+    global TOKENS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=32, help="token sample of the CPU baseline")
+    ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU (default: the configs[3] 8192)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    TOKENS = args.tokens
     if args.impl == "reference":
         run_reference(args)
     else:

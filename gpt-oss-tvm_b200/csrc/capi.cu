@@ -9,7 +9,7 @@
 
 namespace gptoss {
 // moe_route.cu
-int launch_rmsnorm(const uint16_t*, const uint16_t*, int64_t, int32_t, float, uint16_t*, cudaStream_t);
+int launch_rmsnorm(const uint16_t*, const uint16_t*, int64_t, int32_t, float, uint16_t*, uint32_t*, cudaStream_t);
 int launch_router(const uint16_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t, uint16_t*,
                   cudaStream_t);
 int launch_topk_softmax(const uint16_t*, int64_t, int32_t, int32_t, uint16_t*, int32_t*, uint32_t*, cudaStream_t);
@@ -81,14 +81,14 @@ int gptoss_rms_norm(const uint16_t* x, const uint16_t* weight, int64_t M, int32_
                     void* stream) {
   if (M < 0 || H <= 0 || (H & 1)) return fail(-1, "gptoss_rms_norm: bad shape M=%lld H=%d", (long long)M, H);
   if (M && (!x || !weight || !out)) return fail(-1, "gptoss_rms_norm: null pointer");
-  return check_launch(launch_rmsnorm(x, weight, M, H, eps, out, GPTOSS_STREAM(stream)), "rms_norm");
+  return check_launch(launch_rmsnorm(x, weight, M, H, eps, out, nullptr, GPTOSS_STREAM(stream)), "rms_norm");
 }
 
 int gptoss_moe_router(const uint16_t* t, const uint16_t* gate_weight, const uint16_t* gate_bias, int64_t M,
                       int32_t E, int32_t H, int32_t K, uint16_t* logits, uint16_t* topk_weights,
                       int32_t* topk_indices, uint32_t* err, void* stream) {
-  if (M < 0 || E <= 0 || E > 256 || E % 16 || K < 1 || K > 8 || K > E || H <= 0)
-    return fail(-1, "gptoss_moe_router: unsupported shape M=%lld E=%d H=%d K=%d (E must be a multiple of 16, <= 256)",
+  if (M < 0 || E <= 0 || E > 256 || E % 8 || K < 1 || K > 8 || K > E || H <= 0)
+    return fail(-1, "gptoss_moe_router: unsupported shape M=%lld E=%d H=%d K=%d (E must be a multiple of 8, <= 256)",
                 (long long)M, E, H, K);
   int rc = launch_router(t, gate_weight, gate_bias, M, E, H, logits, GPTOSS_STREAM(stream));
   if (rc) return check_launch(rc, "router");

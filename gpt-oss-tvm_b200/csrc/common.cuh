@@ -26,6 +26,10 @@ enum DeviceError : uint32_t {
   kErrTimeoutFlag = 1u << 5,     // generic bounded flag wait ran out
 };
 
+// Token rows of one grouped-GEMM tile (the MMA N dimension); the permutation
+// plans its token tiles with this bound.
+constexpr int kMoeTileMaxRows = 208;
+
 // Poll budget for one mbarrier wait.  try_wait itself blocks for a bounded,
 // hardware-defined window, so this is several seconds of waiting at most.
 constexpr uint32_t kWaitPolls = 1u << 22;

@@ -12,35 +12,42 @@
 //   mode 1 (down):     out[r, n] = h[r, n]   (fp32, combined later)
 //
 // Design (sm_100a, one persistent CTA per SM):
-//   * The weights are the MMA "A" operand and live in TMEM: four dequant warps
-//     (one warpgroup, one TMEM lane = one weight row each) turn e2m1 nibbles
-//     into exact bf16 and write them with tcgen05.st.  This keeps the shared
-//     memory bandwidth for the activation operand only.
+//   * The weights are the MMA "A" operand and live in TMEM: dequant warps (one
+//     TMEM lane = one weight row each) turn e2m1 nibbles into exact bf16 and
+//     write them with tcgen05.st.  This keeps the shared-memory bandwidth for
+//     the activation operand only.
 //   * The activations (expert-major rows, bf16, K-major) are the "B" operand,
 //     brought into 128-byte-swizzled shared memory by TMA.
-//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 256
+//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 208
 //     token rows, K = 16 per instruction) accumulates fp32 in TMEM.
 //   * Nibbles are streamed by TMA (32-byte swizzle) through an 8-deep ring;
 //     each tile's 128 x K/32 scale bytes arrive with one bulk copy.
-// Warp roles: 0-3 dequant + epilogue, 4 activation TMA, 5 MMA issuer (also
-// owns TMEM), 6 weight TMA.
+// Warp roles: 0-7 dequant (two warpgroups, one 32-element MXFP4 group of each
+// 64-wide K chunk each), 8-11 epilogue (double-buffered TMEM accumulator, so
+// the epilogue of tile i overlaps the main loop of tile i+1), 12 activation
+// TMA, 13 MMA issuer (also owns TMEM), 14 weight TMA.
 #include "common.cuh"
 
 namespace gptoss {
 
-constexpr int kGemmThreads = 224;
+constexpr int kGemmThreads = 480;
 constexpr int kBM = 128;            // weight rows per tile (MMA M)
-constexpr int kMaxBN = 256;         // token rows per tile (MMA N, max)
+constexpr int kMaxBN = kMoeTileMaxRows;  // token rows per tile (MMA N, max)
+constexpr int kBoxRows = 64;        // activation TMA box height
 constexpr int kBK = 64;             // K per pipeline chunk (one 128 B swizzle row of bf16)
-constexpr int kStages = 4;          // activation + TMEM A stages
+constexpr int kStages = 3;          // activation + TMEM A stages
 constexpr int kWStages = 8;         // nibble ring depth
-constexpr int kActStageBytes = kMaxBN * kBK * 2;   // 32 KB
+constexpr int kActStageBytes = 256 * kBK * 2;      // 32 KB (room for 4 boxes of 64 rows)
 constexpr int kWStageBytes = kBM * (kBK / 2);      // 4 KB (128 rows x 32 nibble bytes)
 constexpr int kMaxGroups = 96;                     // K/32 upper bound (K <= 3072)
 constexpr int kScaleBytes = kBM * kMaxGroups;      // per-tile scale buffer (row stride = G)
-constexpr int kAccCols = 256;
+constexpr int kAccCols = kMaxBN;                   // columns of one accumulator buffer
 constexpr int kTmemCols = 512;
-constexpr int kAColBase = kAccCols;                // A stage s at columns 256 + 32 s
+constexpr int kAColBase = 2 * kAccCols;            // A stage s at columns 416 + 32 s
+static_assert(kAColBase + kStages * 32 <= kTmemCols, "TMEM budget");
+constexpr int kDequantWarps = 8;
+constexpr int kEpiWarp0 = 8;
+constexpr int kActWarp = 12, kMmaWarp = 13, kWWarp = 14;
 
 struct GemmParams {
   const uint8_t* scales;     // [E, N, G]
@@ -63,7 +70,7 @@ struct GemmSmem {
   static constexpr int kW = kAct + kStages * kActStageBytes;
   static constexpr int kScale = kW + kWStages * kWStageBytes;
   static constexpr int kBar = kScale + 2 * kScaleBytes;
-  static constexpr int kNumBars = 2 * kStages + 2 * kWStages + 4 + 2;
+  static constexpr int kNumBars = 2 * kStages + 2 * kWStages + 4 + 4;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kTotal = kMisc + 64;
   static constexpr int kAlloc = kTotal + 1024;  // slack for manual 1024 B alignment
@@ -94,6 +101,15 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& p, int32_t t, int3
   return ti.nrows > 0;
 }
 
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 template <int kMode>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_w,
@@ -104,14 +120,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* w_s = smem + GemmSmem::kW;
   uint8_t* sc_s = smem + GemmSmem::kScale;
   uint64_t* bars = (uint64_t*)(smem + GemmSmem::kBar);
-  uint64_t* full_bar = bars;                      // [kStages] act TMA tx + 4 dequant warps
+  uint64_t* full_bar = bars;                      // [kStages] act TMA tx + 8 dequant warps
   uint64_t* empty_bar = full_bar + kStages;       // [kStages] MMA commit
   uint64_t* wfull_bar = empty_bar + kStages;      // [kWStages] nibble TMA tx
-  uint64_t* wempty_bar = wfull_bar + kWStages;    // [kWStages] 4 dequant warps
+  uint64_t* wempty_bar = wfull_bar + kWStages;    // [kWStages] 8 dequant warps
   uint64_t* scfull_bar = wempty_bar + kWStages;   // [2] scale bulk copy tx
-  uint64_t* scempty_bar = scfull_bar + 2;         // [2] 4 dequant warps
-  uint64_t* accfull_bar = scempty_bar + 2;        // MMA commit
-  uint64_t* accempty_bar = accfull_bar + 1;       // 4 epilogue warps
+  uint64_t* scempty_bar = scfull_bar + 2;         // [2] 8 dequant warps
+  uint64_t* accfull_bar = scempty_bar + 2;        // [2] MMA commit
+  uint64_t* accempty_bar = accfull_bar + 2;       // [2] 4 epilogue warps
   uint32_t* misc = (uint32_t*)(smem + GemmSmem::kMisc);
   volatile uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_s = misc + 1;
@@ -125,27 +141,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], 5);
+      mbar_init(&full_bar[s], 1 + kDequantWarps);
       mbar_init(&empty_bar[s], 1);
     }
     for (int s = 0; s < kWStages; ++s) {
       mbar_init(&wfull_bar[s], 1);
-      mbar_init(&wempty_bar[s], 4);
+      mbar_init(&wempty_bar[s], kDequantWarps);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&scfull_bar[s], 1);
-      mbar_init(&scempty_bar[s], 4);
+      mbar_init(&scempty_bar[s], kDequantWarps);
+      mbar_init(&accfull_bar[s], 1);
+      mbar_init(&accempty_bar[s], 4);
     }
-    mbar_init(accfull_bar, 1);
-    mbar_init(accempty_bar, 4);
     *abort_s = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc((uint32_t*)tmem_slot, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == kActWarp && lane == 0) {
     tma_prefetch_desc(&tmap_act);
     tma_prefetch_desc(&tmap_w);
   }
@@ -154,24 +170,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kActWarp) {
     // ------------------------------------------------ activation producer
     if (elect_one()) {
       uint32_t it = 0;
       for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
         TileInfo ti;
         if (!decode_tile(p, t, ftiles, ti)) continue;
-        const int32_t nbox = (ti.nrows + 63) >> 6;
+        const int32_t nbox = (ti.nrows + kBoxRows - 1) / kBoxRows;
         for (int32_t c = 0; c < nchunks; ++c, ++it) {
           const uint32_t s = it % kStages, ph = (it / kStages) & 1;
           if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
-          mbar_arrive_expect_tx(&full_bar[s], (uint32_t)nbox * 64 * 128);
+          mbar_arrive_expect_tx(&full_bar[s], (uint32_t)nbox * kBoxRows * 128);
           for (int32_t b = 0; b < nbox; ++b)
-            tma_load_2d(act_s + s * kActStageBytes + b * 8192, &tmap_act, c * kBK, ti.row0 + b * 64, &full_bar[s]);
+            tma_load_2d(act_s + s * kActStageBytes + b * kBoxRows * 128, &tmap_act, c * kBK, ti.row0 + b * kBoxRows,
+                        &full_bar[s]);
         }
       }
     }
-  } else if (warp == 6) {
+  } else if (warp == kWWarp) {
     // ---------------------------------------------------- weight producer
     if (elect_one()) {
       uint32_t wit = 0, tl = 0;
@@ -191,15 +208,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             "l"(src), "r"(sbytes), "r"(smem_u32(&scfull_bar[sb]))
             : "memory");
         const int32_t wrow = ti.expert * p.N + ti.f0;
+        bool ok = true;
         for (int32_t c = 0; c < nchunks; ++c, ++wit) {
           const uint32_t s = wit % kWStages, ph = (wit / kWStages) & 1;
-          if (!mbar_wait(&wempty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
+          if (!mbar_wait(&wempty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&wfull_bar[s], kWStageBytes);
           tma_load_2d(w_s + s * kWStageBytes, &tmap_w, c * (kBK / 2), wrow, &wfull_bar[s]);
         }
+        if (!ok) { *abort_s = 1; break; }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // --------------------------------------------------------- MMA issuer
     if (elect_one()) {
       uint32_t it = 0, tl = 0;
@@ -208,8 +227,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!decode_tile(p, t, ftiles, ti)) continue;
         const uint32_t n_mma = (uint32_t)((ti.nrows + 15) & ~15);
         const uint32_t idesc = make_idesc_bf16(kBM, n_mma);
-        if (!mbar_wait(accempty_bar, (tl & 1) ^ 1, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
+        const uint32_t ab = tl & 1, aph = (tl >> 1) & 1;
+        if (!mbar_wait(&accempty_bar[ab], aph ^ 1, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
         tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ab * kAccCols;
         bool ok = true;
         for (int32_t c = 0; c < nchunks; ++c, ++it) {
           const uint32_t s = it % kStages, ph = (it / kStages) & 1;
@@ -218,65 +239,58 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t b_base = smem_u32(act_s + s * kActStageBytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            tc_mma_ts(tmem_base, tmem_base + kAColBase + s * 32 + kk * 8, make_sdesc_sw128(b_base + kk * 32), idesc,
+            tc_mma_ts(d_tmem, tmem_base + kAColBase + s * 32 + kk * 8, make_sdesc_sw128(b_base + kk * 32), idesc,
                       (c > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&empty_bar[s]);
         }
         if (!ok) { *abort_s = 1; break; }
-        tc_commit(accfull_bar);
+        tc_commit(&accfull_bar[ab]);
         ++tl;
       }
     }
-  } else {
-    // ------------------------------------- dequant (weights -> TMEM) + epilogue
-    const int row = threadIdx.x;  // weight row within the tile == TMEM lane
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  } else if (warp < kDequantWarps) {
+    // --------------------------------------------- dequant: weights -> TMEM
+    const int wg = warp >> 2;                   // which MXFP4 group of the chunk
+    const int row = (warp & 3) * 32 + lane;     // weight row within the tile == TMEM lane
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     uint32_t it = 0, wit = 0, tl = 0;
     for (int32_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       TileInfo ti;
       if (!decode_tile(p, t, ftiles, ti)) continue;
       if (*abort_s) break;
       const uint32_t sb = tl & 1, sph = (tl >> 1) & 1;
-      const int32_t frow = ti.f0 + row;
-      const bool row_ok = frow < p.N;
+      ++tl;
+      const bool row_ok = ti.f0 + row < p.N;
       bool ok = mbar_wait(&scfull_bar[sb], sph, p.err, kErrTimeoutFull);
-      const uint8_t* srow = sc_s + sb * kScaleBytes + row * G;
+      const uint8_t* srow = sc_s + sb * kScaleBytes + row * G + wg;
+      const uint32_t nib_off = (uint32_t)(wg ^ ((row >> 2) & 1)) << 4;  // 32-byte swizzle
       for (int32_t c = 0; c < nchunks && ok; ++c, ++it, ++wit) {
         const uint32_t ws = wit % kWStages, wph = (wit / kWStages) & 1;
         const uint32_t s = it % kStages, ph = (it / kStages) & 1;
         ok = mbar_wait(&wfull_bar[ws], wph, p.err, kErrTimeoutFull);
         if (!ok) break;
-        // nibbles of this row: 32 bytes, 32-byte-swizzled rows (16-byte halves
-        // swapped on rows whose bit 2 is set)
-        const uint8_t* wrow = w_s + ws * kWStageBytes + row * 32;
-        const uint32_t sw = (row >> 2) & 1;
-        uint4 n0 = *(const uint4*)(wrow + (sw << 4));
-        uint4 n1 = *(const uint4*)(wrow + ((sw ^ 1) << 4));
+        const uint4 nb = *(const uint4*)(w_s + ws * kWStageBytes + row * 32 + nib_off);
+        const uint32_t sc = srow[2 * c];
         __syncwarp();
         if (lane == 0) mbar_arrive(&wempty_bar[ws]);
-        const uint32_t s0 = srow[2 * c], s1 = srow[2 * c + 1];
-        uint32_t r[32];
+        uint32_t r[16];
         if (row_ok) {
-          const uint32_t sc0 = e8m0_scale_bf16x2(s0), sc1 = e8m0_scale_bf16x2(s1);
+          const uint32_t sc2 = e8m0_scale_bf16x2(sc);
           uint32_t o[4];
-          fp4x8_to_bf16x8(n0.x, sc0, o); r[0] = o[0]; r[1] = o[1]; r[2] = o[2]; r[3] = o[3];
-          fp4x8_to_bf16x8(n0.y, sc0, o); r[4] = o[0]; r[5] = o[1]; r[6] = o[2]; r[7] = o[3];
-          fp4x8_to_bf16x8(n0.z, sc0, o); r[8] = o[0]; r[9] = o[1]; r[10] = o[2]; r[11] = o[3];
-          fp4x8_to_bf16x8(n0.w, sc0, o); r[12] = o[0]; r[13] = o[1]; r[14] = o[2]; r[15] = o[3];
-          fp4x8_to_bf16x8(n1.x, sc1, o); r[16] = o[0]; r[17] = o[1]; r[18] = o[2]; r[19] = o[3];
-          fp4x8_to_bf16x8(n1.y, sc1, o); r[20] = o[0]; r[21] = o[1]; r[22] = o[2]; r[23] = o[3];
-          fp4x8_to_bf16x8(n1.z, sc1, o); r[24] = o[0]; r[25] = o[1]; r[26] = o[2]; r[27] = o[3];
-          fp4x8_to_bf16x8(n1.w, sc1, o); r[28] = o[0]; r[29] = o[1]; r[30] = o[2]; r[31] = o[3];
+          fp4x8_to_bf16x8(nb.x, sc2, o); r[0] = o[0]; r[1] = o[1]; r[2] = o[2]; r[3] = o[3];
+          fp4x8_to_bf16x8(nb.y, sc2, o); r[4] = o[0]; r[5] = o[1]; r[6] = o[2]; r[7] = o[3];
+          fp4x8_to_bf16x8(nb.z, sc2, o); r[8] = o[0]; r[9] = o[1]; r[10] = o[2]; r[11] = o[3];
+          fp4x8_to_bf16x8(nb.w, sc2, o); r[12] = o[0]; r[13] = o[1]; r[14] = o[2]; r[15] = o[3];
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = 0u;
+          for (int j = 0; j < 16; ++j) r[j] = 0u;
         }
         ok = mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty);
         if (!ok) break;
         __syncwarp();
         tc_fence_after();
-        tmem_st_x32(tmem_base + lane_base + kAColBase + s * 32, r);
+        tmem_st_x16(tmem_base + lane_base + kAColBase + s * 32 + wg * 16, r);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -285,32 +299,49 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&scempty_bar[sb]);
       if (!ok) { *abort_s = 1; break; }
-
-      // ---- epilogue: TMEM accumulator -> registers -> global
-      if (!mbar_wait(accfull_bar, tl & 1, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
+    }
+  } else {
+    // ---------------------------------------- epilogue: TMEM -> registers -> global
+    const int q = warp - kEpiWarp0;               // TMEM lane quarter
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint32_t tl = 0;
+    for (int32_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      TileInfo ti;
+      if (!decode_tile(p, t, ftiles, ti)) continue;
+      if (*abort_s) break;
+      const uint32_t ab = tl & 1, aph = (tl >> 1) & 1;
+      ++tl;
+      const int32_t frow = ti.f0 + row;
+      const bool row_ok = frow < p.N;
+      const float bias = row_ok ? bf16_bits_to_f32(__ldg(p.bias + (size_t)ti.expert * p.N + frow)) : 0.0f;
+      if (!mbar_wait(&accfull_bar[ab], aph, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
       __syncwarp();
       tc_fence_after();
-      const float bias = row_ok ? bf16_bits_to_f32(__ldg(p.bias + (size_t)ti.expert * p.N + frow)) : 0.0f;
       const int32_t ncols = (ti.nrows + 31) & ~31;
       for (int32_t c0 = 0; c0 < ncols; c0 += 32) {
         uint32_t v[32];
-        tmem_ld_x32(tmem_base + lane_base + (uint32_t)c0, v);
+        tmem_ld_x32(tmem_base + lane_base + ab * kAccCols + (uint32_t)c0, v);
         tmem_ld_wait();
         if (kMode == 0) {
-          // lanes (2j, 2j+1) hold the glu / linear rows of output column j
+          // lane pair (2j, 2j+1) holds the glu / linear rows of output column j:
+          // the even lane finishes tokens c0..c0+15, the odd lane c0+16..c0+31
+          const bool odd = lane & 1;
+          uint16_t* out = (uint16_t*)p.out;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float h = __uint_as_float(v[j]) + bias;
-            const float partner = __shfl_xor_sync(0xffffffffu, h, 1);
-            const int32_t col = c0 + j;
-            if (!(lane & 1) && row_ok && col < ti.nrows) {
-              const float g = fminf(h, p.limit);
-              const float l = fmaxf(fminf(partner, p.limit), -p.limit);
-              const float sg = 1.0f / (1.0f + expf(-(p.alpha * g)));
-              const float y = (g * sg) * (l + 1.0f);
-              uint16_t* out = (uint16_t*)p.out;
-              out[(size_t)(ti.row0 + col) * p.ldo + (frow >> 1)] = f32_to_bf16_bits(y);
-            }
+          for (int i = 0; i < 16; ++i) {
+            const float mine_lo = __uint_as_float(v[i]) + bias;
+            const float mine_hi = __uint_as_float(v[16 + i]) + bias;
+            const float send = odd ? mine_lo : mine_hi;
+            const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+            const float gl = odd ? recv : mine_lo;
+            const float li = odd ? mine_hi : recv;
+            const int32_t col = c0 + i + (odd ? 16 : 0);
+            const float g = fminf(gl, p.limit);
+            const float l = fmaxf(fminf(li, p.limit), -p.limit);
+            const float sg = 1.0f / (1.0f + expf(-(p.alpha * g)));
+            const float y = (g * sg) * (l + 1.0f);
+            if (row_ok && col < ti.nrows) out[(size_t)(ti.row0 + col) * p.ldo + (frow >> 1)] = f32_to_bf16_bits(y);
           }
         } else {
           float* out = (float*)p.out;
@@ -324,15 +355,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(accempty_bar);
-      ++tl;
+      if (lane == 0) mbar_arrive(&accempty_bar[ab]);
     }
   }
 
   // ---- teardown: everyone drains, then the allocating warp frees TMEM
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
@@ -396,7 +426,7 @@ int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
   }
   CUtensorMap tmap_act, tmap_w;
   int rc = make_tmap_2d(&tmap_act, L.act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)L.act_rows,
-                        (uint64_t)L.K, kBK, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+                        (uint64_t)L.K, kBK, kBoxRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap_2d(&tmap_w, L.blocks, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)L.E * L.N, (uint64_t)L.K / 2,
                     kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_32B);

@@ -5,6 +5,8 @@
 // floating-point steps reproduce the reference's operation order and
 // rounding (no contraction: __fmul_rn/__fadd_rn where the reference has
 // separate multiply and add).
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace gptoss {
@@ -12,45 +14,65 @@ namespace gptoss {
 // ------------------------------------------------------------ RMSNorm --
 // nn.RMSNorm as lowered for model/mlp.py:81-87,375 (and attention.py:84,193):
 // serial fp32 sum of squares in column order, r = 1/sqrtf(sum/H + eps),
-// out = bf16((r*x)*w).  One lane owns one token's serial sum; a warp stages
-// 32 tokens x 64 columns through shared memory so global reads coalesce.
-constexpr int kNormTok = 32;
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
-                                                       int64_t M, int32_t H, float eps, uint16_t* __restrict__ out) {
-  __shared__ uint16_t tile[8][kNormTok][66];
-  __shared__ float rs[8][kNormTok];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tok0 = ((int64_t)blockIdx.x * 8 + warp) * kNormTok;
-  if (tok0 >= M) return;
-  float ss = 0.0f;
-  for (int32_t k0 = 0; k0 < H; k0 += 64) {
-    // load 32 tokens x 64 columns (2 columns per lane per token)
-    for (int t = 0; t < kNormTok; ++t) {
-      const int64_t m = tok0 + t;
-      uint32_t v = 0;
-      const int32_t k = k0 + 2 * lane;
-      if (m < M && k + 1 < H) v = *(const uint32_t*)(x + m * H + k);
-      else if (m < M && k < H) v = x[m * H + k];
-      tile[warp][t][2 * lane] = (uint16_t)(v & 0xFFFF);
-      tile[warp][t][2 * lane + 1] = (uint16_t)(v >> 16);
-    }
-    __syncwarp();
-    const int32_t kn = min(64, H - k0);
-    for (int32_t j = 0; j < kn; ++j) {
-      const float v = bf16_bits_to_f32(tile[warp][lane][j]);
-      ss = __fadd_rn(ss, __fmul_rn(v, v));
-    }
-    __syncwarp();
+// out = bf16((r*x)*w).  A block brings up to 16 whole token rows into shared
+// memory with one bulk copy each; one thread per token runs the serial sum,
+// then the whole block writes the normalised rows.
+constexpr int kNormRows = 16;
+__global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ w,
+                                                       int64_t M, int32_t H, int32_t rows_per_block, float eps,
+                                                       uint16_t* __restrict__ out, uint32_t* err) {
+  extern __shared__ __align__(16) uint8_t norm_smem[];
+  __shared__ uint64_t bar;
+  __shared__ float rs[kNormRows];
+  uint16_t* rowbuf = (uint16_t*)norm_smem;
+  const int64_t m0 = (int64_t)blockIdx.x * rows_per_block;
+  const int64_t left = M - m0;
+  const int nrows = left < rows_per_block ? (int)left : rows_per_block;
+  const uint32_t row_bytes = (uint32_t)H * 2;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
   }
-  rs[warp][lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
-  __syncwarp();
-  for (int t = 0; t < kNormTok; ++t) {
-    const int64_t m = tok0 + t;
-    if (m >= M) break;
-    const float r = rs[warp][t];
-    for (int32_t k = lane; k < H; k += 32) {
-      const float v = __fmul_rn(__fmul_rn(r, bf16_bits_to_f32(x[m * H + k])), bf16_bits_to_f32(w[k]));
-      out[m * H + k] = f32_to_bf16_bits(v);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&bar, row_bytes * (uint32_t)nrows);
+    for (int r = 0; r < nrows; ++r) {
+      asm volatile(
+          "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem_u32(rowbuf + (size_t)r * H)),
+          "l"(x + (m0 + r) * H), "r"(row_bytes), "r"(smem_u32(&bar))
+          : "memory");
+    }
+  }
+  const bool ok = mbar_wait(&bar, 0, err, kErrTimeoutOther);
+  if (ok && threadIdx.x < nrows) {
+    const uint4* row = (const uint4*)(rowbuf + (size_t)threadIdx.x * H);
+    float ss = 0.0f;
+    for (int32_t k8 = 0; k8 < H / 8; ++k8) {
+      const uint4 v = row[k8];
+      const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float a = __uint_as_float(wv[q] << 16), b = __uint_as_float(wv[q] & 0xFFFF0000u);
+        ss = __fadd_rn(ss, __fmul_rn(a, a));
+        ss = __fadd_rn(ss, __fmul_rn(b, b));
+      }
+    }
+    rs[threadIdx.x] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+  }
+  __syncthreads();
+  if (!ok) return;
+  const int32_t h2 = H / 2;
+  for (int r = 0; r < nrows; ++r) {
+    const float rr = rs[r];
+    const uint32_t* src = (const uint32_t*)(rowbuf + (size_t)r * H);
+    uint32_t* dst = (uint32_t*)(out + (m0 + r) * H);
+    for (int32_t j = threadIdx.x; j < h2; j += blockDim.x) {
+      const uint32_t v = src[j];
+      const uint32_t wv = __ldg((const uint32_t*)w + j);
+      const float a = __fmul_rn(__fmul_rn(rr, __uint_as_float(v << 16)), __uint_as_float(wv << 16));
+      const float b = __fmul_rn(__fmul_rn(rr, __uint_as_float(v & 0xFFFF0000u)), __uint_as_float(wv & 0xFFFF0000u));
+      dst[j] = (uint32_t)f32_to_bf16_bits(a) | ((uint32_t)f32_to_bf16_bits(b) << 16);
     }
   }
 }
@@ -59,71 +81,104 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const uint16_t* __restrict
 // logits[m, e] = bf16(float(acc) + float(b[e])) where acc is a bf16 running
 // sum: acc = bf16(float(acc) + t[m,k]*W[e,k]) for k = 0..H-1 in order
 // (nn.Linear at model/mlp.py:88-92,376 lowered with a bf16 accumulator).
-// t*W is exact in fp32, so fma(t, W, acc) == acc + t*W; the bf16 rounding is
-// a cvt.rn.bf16x2 whose other half is zero, which leaves float(bf16(s)) in
-// the register.  Two chains share one packed f32x2 FMA.
-constexpr int kRouterTok = 16;   // tokens per block
-constexpr int kRouterKT = 32;    // k per shared-memory tile
-template <int EPT>  // experts per thread (even)
+// t*W is exact in fp32, so fma(t, W, acc) == acc + t*W (one rounding to
+// fp32, as in the reference), followed by the rounding to bf16.  Each
+// thread owns a 4-token x 8-expert register tile of independent serial
+// chains; two chains share one packed f32x2 FMA.
+constexpr int kRTT = 4;   // tokens per thread
+constexpr int kRTE = 8;   // experts per thread
+constexpr int kRKT = 16;  // k per shared-memory stage
+
+// bf16 rounding of two fp32 accumulators held as a packed pair.
+template <int kRound>
+__device__ __forceinline__ unsigned long long round_pair_bf16(unsigned long long s) {
+  const uint32_t lo = (uint32_t)s, hi = (uint32_t)(s >> 32);
+  if (kRound == 0) {
+    // one cvt per value; the zero half leaves float(bf16(v)) in the register
+    uint32_t a, b;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(a) : "f"(__uint_as_float(lo)), "f"(0.0f));
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(b) : "f"(__uint_as_float(hi)), "f"(0.0f));
+    return ((unsigned long long)b << 32) | a;
+  } else if (kRound == 1) {
+    // one packed cvt for both values, then split the halves back out
+    uint32_t p;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(__uint_as_float(hi)), "f"(__uint_as_float(lo)));
+    return ((unsigned long long)(p & 0xFFFF0000u) << 32) | (p << 16);
+  } else {
+    // integer round-to-nearest-even on the bit patterns
+    const uint32_t a = (lo + 0x7FFFu + ((lo >> 16) & 1u)) & 0xFFFF0000u;
+    const uint32_t b = (hi + 0x7FFFu + ((hi >> 16) & 1u)) & 0xFFFF0000u;
+    return ((unsigned long long)b << 32) | a;
+  }
+}
+
+template <int kRound>
 __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict__ t, const uint16_t* __restrict__ W,
                                                       const uint16_t* __restrict__ b, int64_t M, int32_t E, int32_t H,
-                                                      uint16_t* __restrict__ logits) {
-  // thread = (token slot 0..15, expert group 0..7); expert group g owns
-  // experts [g*EPT, (g+1)*EPT)
-  extern __shared__ float rsm[];
-  constexpr int kTS = kRouterKT + 2;               // padded row: 16 token rows hit distinct banks
-  float* ts = rsm;                                  // [kRouterTok][kTS]
-  float2* ws = (float2*)(ts + kRouterTok * kTS);    // [kRouterKT][E/2] pairs (e, e+1)
-  const int tid = threadIdx.x;
-  const int slot = tid & 15, grp = tid >> 4;
-  const int64_t m = (int64_t)blockIdx.x * kRouterTok + slot;
-  constexpr int P = EPT / 2;
-  unsigned long long acc[P];
+                                                      int32_t block_experts, uint16_t* __restrict__ logits) {
+  extern __shared__ __align__(16) float rsm[];
+  const int egroups = block_experts / kRTE;         // expert groups per block
+  const int tgroups = 128 / egroups;                // token groups per block
+  const int btok = tgroups * kRTT;                  // tokens per block
+  float* ts = rsm;                                  // [kRKT][btok][2]  (each value twice)
+  float* ws = ts + kRKT * btok * 2;                 // [kRKT][block_experts]
+  const int tg = threadIdx.x % tgroups, eg = threadIdx.x / tgroups;
+  const int64_t tok0 = (int64_t)blockIdx.x * btok;
+  const int32_t e0 = blockIdx.y * block_experts;
+  unsigned long long acc[kRTT][kRTE / 2];
 #pragma unroll
-  for (int i = 0; i < P; ++i) acc[i] = 0ull;
-  const int32_t pairs = E / 2;
-  for (int32_t k0 = 0; k0 < H; k0 += kRouterKT) {
+  for (int i = 0; i < kRTT; ++i)
+#pragma unroll
+    for (int j = 0; j < kRTE / 2; ++j) acc[i][j] = 0ull;
+
+  for (int32_t k0 = 0; k0 < H; k0 += kRKT) {
     __syncthreads();
-    for (int i = tid; i < kRouterTok * kRouterKT; i += 128) {
-      const int s = i / kRouterKT, kk = i % kRouterKT;
-      const int64_t mm = (int64_t)blockIdx.x * kRouterTok + s;
-      ts[s * kTS + kk] = (mm < M && k0 + kk < H) ? bf16_bits_to_f32(t[mm * H + k0 + kk]) : 0.0f;
+    for (int i = threadIdx.x; i < btok * kRKT; i += 128) {
+      const int tok = i / kRKT, kk = i % kRKT;
+      const int64_t m = tok0 + tok;
+      const float v = (m < M && k0 + kk < H) ? bf16_bits_to_f32(t[m * H + k0 + kk]) : 0.0f;
+      ts[(kk * btok + tok) * 2] = v;
+      ts[(kk * btok + tok) * 2 + 1] = v;
     }
-    for (int i = tid; i < kRouterKT * pairs; i += 128) {
-      const int kk = i / pairs, pr = i % pairs;
-      float2 v = make_float2(0.0f, 0.0f);
-      if (k0 + kk < H) {
-        v.x = bf16_bits_to_f32(W[(int64_t)(2 * pr) * H + k0 + kk]);
-        v.y = bf16_bits_to_f32(W[(int64_t)(2 * pr + 1) * H + k0 + kk]);
-      }
-      ws[kk * pairs + pr] = v;
+    for (int i = threadIdx.x; i < block_experts * kRKT; i += 128) {
+      const int e = i / kRKT, kk = i % kRKT;
+      ws[kk * block_experts + e] = (e0 + e < E && k0 + kk < H) ? bf16_bits_to_f32(W[(int64_t)(e0 + e) * H + k0 + kk])
+                                                               : 0.0f;
     }
     __syncthreads();
-    const int32_t kn = min(kRouterKT, H - k0);
+    const int32_t kn = min(kRKT, H - k0);
     for (int32_t kk = 0; kk < kn; ++kk) {
-      const float tv = ts[slot * kTS + kk];
-      const unsigned long long tt = ((unsigned long long)__float_as_uint(tv) << 32) | __float_as_uint(tv);
+      const ulonglong2* tp = (const ulonglong2*)(ts + (kk * btok + tg * kRTT) * 2);
+      const ulonglong2 t01 = tp[0], t23 = tp[1];
+      const unsigned long long tv[4] = {t01.x, t01.y, t23.x, t23.y};
+      const ulonglong2* wp = (const ulonglong2*)(ws + kk * block_experts + eg * kRTE);
+      const ulonglong2 w01 = wp[0], w23 = wp[1];
+      const unsigned long long wv[4] = {w01.x, w01.y, w23.x, w23.y};
 #pragma unroll
-      for (int i = 0; i < P; ++i) {
-        const float2 wv = ws[kk * pairs + grp * P + i];
-        const unsigned long long ww = ((unsigned long long)__float_as_uint(wv.y) << 32) | __float_as_uint(wv.x);
-        unsigned long long s = acc[i];
-        asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s) : "l"(tt), "l"(ww));
-        uint32_t lo, hi;
-        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(__uint_as_float((uint32_t)s)), "f"(0.0f));
-        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(__uint_as_float((uint32_t)(s >> 32))), "f"(0.0f));
-        acc[i] = ((unsigned long long)hi << 32) | lo;
+      for (int i = 0; i < kRTT; ++i) {
+#pragma unroll
+        for (int j = 0; j < kRTE / 2; ++j) {
+          unsigned long long s = acc[i][j];
+          asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s) : "l"(tv[i]), "l"(wv[j]));
+          acc[i][j] = round_pair_bf16<kRound>(s);
+        }
       }
     }
   }
-  if (m < M) {
 #pragma unroll
-    for (int i = 0; i < P; ++i) {
-      const int32_t e0 = 2 * (grp * P + i);
-      if (e0 < E) {
-        const float a0 = __uint_as_float((uint32_t)acc[i]), a1 = __uint_as_float((uint32_t)(acc[i] >> 32));
-        logits[m * E + e0] = f32_to_bf16_bits(__fadd_rn(a0, bf16_bits_to_f32(b[e0])));
-        logits[m * E + e0 + 1] = f32_to_bf16_bits(__fadd_rn(a1, bf16_bits_to_f32(b[e0 + 1])));
+  for (int i = 0; i < kRTT; ++i) {
+    const int64_t m = tok0 + tg * kRTT + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < kRTE / 2; ++j) {
+      const int32_t e = e0 + eg * kRTE + 2 * j;
+      if (e + 1 < E + 1 && e < E) {
+        const float a0 = __uint_as_float((uint32_t)acc[i][j]);
+        logits[m * E + e] = f32_to_bf16_bits(__fadd_rn(a0, bf16_bits_to_f32(b[e])));
+      }
+      if (e + 1 < E) {
+        const float a1 = __uint_as_float((uint32_t)(acc[i][j] >> 32));
+        logits[m * E + e + 1] = f32_to_bf16_bits(__fadd_rn(a1, bf16_bits_to_f32(b[e + 1])));
       }
     }
   }
@@ -192,8 +247,8 @@ __global__ void topk_softmax_kernel(const uint16_t* __restrict__ logits, int64_t
 // Expert-major order of the (token, rank) pairs (the layout of the grouped
 // kernels, model/mlp_optimized.py:118-170): rows of expert e occupy
 // [indptr[e], indptr[e+1]) in ascending token order.  Also builds the token
-// tiles the grouped GEMM walks: an expert with c rows gets ceil(c/256)
-// tiles of roundup16(ceil(c/tiles)) rows.
+// tiles the grouped GEMM walks: an expert with c rows gets
+// ceil(c/kMoeTileMaxRows) tiles of roundup16(ceil(c/tiles)) rows.
 // Stage 1 (one block): per-expert counts, exclusive scan, tile plan.
 __global__ void __launch_bounds__(1024) moe_count_scan_kernel(const int32_t* __restrict__ idx, int64_t pairs, int32_t E,
                                                                int32_t* __restrict__ indptr,
@@ -214,7 +269,7 @@ __global__ void __launch_bounds__(1024) moe_count_scan_kernel(const int32_t* __r
       const int32_t c = cnt[e];
       indptr[e] = acc;
       tile_ptr[e] = tacc;
-      const int32_t nt = (c + 255) / 256;
+      const int32_t nt = (c + kMoeTileMaxRows - 1) / kMoeTileMaxRows;
       const int32_t per = nt ? ((((c + nt - 1) / nt) + 15) & ~15) : 0;
       tile_rows[e] = per;
       acc += c;
@@ -319,31 +374,50 @@ __global__ void mxfp4_dequant_kernel(const uint8_t* __restrict__ blocks, const u
 
 // ------------------------------------------------------------- launch --
 int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, float eps, uint16_t* out,
-                   cudaStream_t s) {
+                   uint32_t* err, cudaStream_t s) {
   if (M <= 0) return 0;
-  const int64_t blocks = (M + 8 * kNormTok - 1) / (8 * kNormTok);
-  rmsnorm_kernel<<<(unsigned)blocks, 256, 0, s>>>(x, w, M, H, eps, out);
+  if (H % 8 || ((uintptr_t)x & 15)) return -12;
+  const size_t row = (size_t)H * 2;
+  const size_t fit = (size_t)(100 * 1024) / row;
+  int rows = fit < (size_t)kNormRows ? (int)fit : kNormRows;
+  if (rows < 1) return -12;
+  const size_t smem = row * rows;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024 + 1024);
+    attr = true;
+  }
+  const int64_t blocks = (M + rows - 1) / rows;
+  rmsnorm_kernel<<<(unsigned)blocks, 128, smem, s>>>(x, w, M, H, rows, eps, out, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
 int launch_router(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H,
                   uint16_t* logits, cudaStream_t s) {
   if (M <= 0) return 0;
-  if (E % 16 != 0 || E > 256) return -12;
-  const unsigned blocks = (unsigned)((M + kRouterTok - 1) / kRouterTok);
-  const size_t smem = (size_t)kRouterTok * (kRouterKT + 2) * 4 + (size_t)kRouterKT * E * 4;
-  const int ept = E / 8;
-  switch (ept) {
-    case 2: router_kernel<2><<<blocks, 128, smem, s>>>(t, W, b, M, E, H, logits); break;
-    case 4: router_kernel<4><<<blocks, 128, smem, s>>>(t, W, b, M, E, H, logits); break;
-    case 6: router_kernel<6><<<blocks, 128, smem, s>>>(t, W, b, M, E, H, logits); break;
-    case 8: router_kernel<8><<<blocks, 128, smem, s>>>(t, W, b, M, E, H, logits); break;
-    case 12: router_kernel<12><<<blocks, 128, smem, s>>>(t, W, b, M, E, H, logits); break;
-    case 16: router_kernel<16><<<blocks, 128, smem, s>>>(t, W, b, M, E, H, logits); break;
-    case 24: router_kernel<24><<<blocks, 128, smem, s>>>(t, W, b, M, E, H, logits); break;
-    case 32: router_kernel<32><<<blocks, 128, smem, s>>>(t, W, b, M, E, H, logits); break;
-    default: return -12;
+  if (E % kRTE != 0 || E > 1024) return -12;
+  const int block_experts = E >= 64 ? 64 : E;
+  if (E % block_experts) return -12;
+  const int egroups = block_experts / kRTE;
+  if (128 % egroups) return -12;
+  const int btok = (128 / egroups) * kRTT;
+  const size_t smem = (size_t)kRKT * btok * 2 * 4 + (size_t)kRKT * block_experts * 4;
+  dim3 grid((unsigned)((M + btok - 1) / btok), (unsigned)(E / block_experts));
+  static int round_mode = -1;
+  if (round_mode < 0) {
+    const char* env = getenv("GPTOSS_ROUTER_ROUND");
+    round_mode = env ? atoi(env) : 0;
   }
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(router_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    cudaFuncSetAttribute(router_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    cudaFuncSetAttribute(router_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    attr = true;
+  }
+  if (round_mode == 1) router_kernel<1><<<grid, 128, smem, s>>>(t, W, b, M, E, H, block_experts, logits);
+  else if (round_mode == 2) router_kernel<2><<<grid, 128, smem, s>>>(t, W, b, M, E, H, block_experts, logits);
+  else router_kernel<0><<<grid, 128, smem, s>>>(t, W, b, M, E, H, block_experts, logits);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
