@@ -19,6 +19,9 @@ int launch_gather(const uint16_t*, const int32_t*, int64_t, int32_t, uint16_t*, 
 int launch_combine(const float*, const int32_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t,
                    uint16_t*, cudaStream_t);
 int launch_mxfp4_dequant(const uint8_t*, const uint8_t*, int64_t, uint16_t*, cudaStream_t);
+int launch_plan_tiles(const int32_t*, int32_t, int32_t*, int32_t*, cudaStream_t);
+int launch_segment_copy(const void*, void*, const int32_t*, int32_t, int32_t, int64_t, int32_t, int32_t*,
+                        cudaStream_t);
 // moe_gemm.cu
 struct GemmLaunch {
   const uint16_t* act;
@@ -177,6 +180,22 @@ int gptoss_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t r
   if (((uintptr_t)blocks & 15) || ((uintptr_t)out & 15)) return fail(-1, "gptoss_mxfp4_dequant: 16-byte alignment");
   return check_launch(launch_mxfp4_dequant(blocks, scales, rows * (int64_t)groups, out, GPTOSS_STREAM(stream)),
                       "mxfp4_dequant");
+}
+
+int gptoss_moe_plan_tiles(const int32_t* indptr, int32_t E, int32_t* tile_ptr, int32_t* tile_rows, void* stream) {
+  if (E <= 0) return fail(-1, "gptoss_moe_plan_tiles: bad E");
+  return check_launch(launch_plan_tiles(indptr, E, tile_ptr, tile_rows, GPTOSS_STREAM(stream)), "plan_tiles");
+}
+
+int gptoss_moe_segment_copy(const void* src, void* dst, const int32_t* counts, int32_t num_ranks,
+                            int32_t local_experts, int64_t row_bytes, int32_t direction, int32_t* indptr_local,
+                            void* stream) {
+  if (num_ranks <= 0 || local_experts <= 0 || row_bytes <= 0 || row_bytes % 16 || (direction != 0 && direction != 1))
+    return fail(-1, "gptoss_moe_segment_copy: bad arguments");
+  if (local_experts + 1 > 256 && indptr_local) return fail(-1, "gptoss_moe_segment_copy: at most 255 local experts");
+  return check_launch(launch_segment_copy(src, dst, counts, num_ranks, local_experts, row_bytes, direction,
+                                          indptr_local, GPTOSS_STREAM(stream)),
+                      "segment_copy");
 }
 
 }  // extern "C"

@@ -372,6 +372,56 @@ __global__ void mxfp4_dequant_kernel(const uint8_t* __restrict__ blocks, const u
   }
 }
 
+// ------------------------------------------------ expert parallelism --
+// Token tiles of the grouped GEMMs from an expert-row index (indptr): the
+// same plan moe_count_scan_kernel builds, for rows that arrived from other
+// ranks.
+__global__ void moe_plan_tiles_kernel(const int32_t* __restrict__ indptr, int32_t E, int32_t* __restrict__ tile_ptr,
+                                      int32_t* __restrict__ tile_rows) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int32_t tacc = 0;
+  for (int32_t e = 0; e < E; ++e) {
+    const int32_t c = indptr[e + 1] - indptr[e];
+    const int32_t nt = (c + kMoeTileMaxRows - 1) / kMoeTileMaxRows;
+    tile_ptr[e] = tacc;
+    tile_rows[e] = nt ? ((((c + nt - 1) / nt) + 15) & ~15) : 0;
+    tacc += nt;
+  }
+  tile_ptr[E] = tacc;
+}
+
+// Rows exchanged between ranks arrive source-major: for each source rank s,
+// the rows of local expert 0, 1, ... (counts[s][e] rows each).  The grouped
+// GEMMs want them expert-major (for each expert, the rows of source 0, 1,
+// ...).  One block per (s, e) segment moves its rows; dir 0 = source-major
+// -> expert-major, dir 1 = back.  Block 0 also writes the expert-major
+// indptr_local[E+1] when asked.
+__global__ void segment_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                    const int32_t* __restrict__ counts, int32_t P, int32_t El, int64_t row_bytes,
+                                    int32_t dir, int32_t* __restrict__ indptr_local) {
+  const int32_t s = blockIdx.x / El, e = blockIdx.x % El;
+  int64_t src_off = 0, dst_off = 0;
+  for (int32_t i = 0; i < P * El; ++i) {
+    const int32_t si = i / El, ei = i % El;
+    const int32_t c = counts[i];
+    if (si < s || (si == s && ei < e)) src_off += c;        // source-major position
+    if (ei < e || (ei == e && si < s)) dst_off += c;        // expert-major position
+  }
+  if (blockIdx.x == 0 && indptr_local != nullptr && threadIdx.x <= El) {
+    int32_t acc = 0;
+    for (int32_t ei = 0; ei < (int32_t)threadIdx.x; ++ei)
+      for (int32_t si = 0; si < P; ++si) acc += counts[si * El + ei];
+    indptr_local[threadIdx.x] = acc;
+  }
+  const int64_t rows = counts[s * El + e];
+  const int64_t a = dir == 0 ? src_off : dst_off;  // read position
+  const int64_t b = dir == 0 ? dst_off : src_off;  // write position
+  const int64_t vec = row_bytes / 16;
+  const uint4* in = (const uint4*)(src + a * row_bytes);
+  uint4* out = (uint4*)(dst + b * row_bytes);
+  for (int64_t i = threadIdx.x; i < rows * vec; i += blockDim.x) out[i] = in[i];
+}
+
 // ------------------------------------------------------------- launch --
 int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, float eps, uint16_t* out,
                    uint32_t* err, cudaStream_t s) {
@@ -462,4 +512,18 @@ int launch_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t g
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+}  // namespace gptoss
+
+namespace gptoss {
+int launch_plan_tiles(const int32_t* indptr, int32_t E, int32_t* tile_ptr, int32_t* tile_rows, cudaStream_t s) {
+  moe_plan_tiles_kernel<<<1, 32, 0, s>>>(indptr, E, tile_ptr, tile_rows);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+int launch_segment_copy(const void* src, void* dst, const int32_t* counts, int32_t P, int32_t El, int64_t row_bytes,
+                        int32_t dir, int32_t* indptr_local, cudaStream_t s) {
+  if (P <= 0 || El <= 0 || row_bytes % 16) return -12;
+  segment_copy_kernel<<<(unsigned)(P * El), 256, 0, s>>>((const uint8_t*)src, (uint8_t*)dst, counts, P, El, row_bytes,
+                                                          dir, indptr_local);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
 }  // namespace gptoss

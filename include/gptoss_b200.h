@@ -133,6 +133,26 @@ int gptoss_moe_combine(const float* h2, const int32_t* row_of_pair, const uint16
 int gptoss_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t rows, int32_t groups,
                          uint16_t* out, void* stream);
 
+/* --------------------------------------------- expert-parallel helpers
+ * The reference runs the MoE block on one device (world_size = 1,
+ * model/mlp.py:79); expert parallelism is new here.  Each rank owns
+ * num_experts / num_ranks experts; token rows travel between ranks with one
+ * NCCL all-to-all each way (host code).  These two calls prepare the rows
+ * that arrive for the grouped GEMMs and send the results back. */
+
+/* Token tiles of gptoss_moe_mlp1/mlp2 for rows already grouped by expert
+ * (indptr [E+1], device): tile_ptr [E+1], tile_rows [E]. */
+int gptoss_moe_plan_tiles(const int32_t* indptr, int32_t E, int32_t* tile_ptr, int32_t* tile_rows, void* stream);
+
+/* Reorders rows between source-major order (for each source rank s, the rows
+ * of local experts 0..El-1, counts[s*El + e] rows each) and expert-major order
+ * (for each expert, the rows of sources 0..P-1).  direction 0: src -> expert
+ * major (also writes indptr_local [El+1] when non-NULL); 1: the reverse.
+ * row_bytes must be a multiple of 16.  counts is device memory. */
+int gptoss_moe_segment_copy(const void* src, void* dst, const int32_t* counts, int32_t num_ranks,
+                            int32_t local_experts, int64_t row_bytes, int32_t direction, int32_t* indptr_local,
+                            void* stream);
+
 #ifdef __cplusplus
 }
 #endif
