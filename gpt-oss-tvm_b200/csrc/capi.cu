@@ -55,6 +55,11 @@ static int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+namespace gptoss {
+// Records a message for gptoss_last_error() (used by entry points defined in other files).
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace gptoss
+
 static int check_launch(int rc, const char* what) {
   if (rc == 0) return 0;
   cudaError_t e = cudaGetLastError();

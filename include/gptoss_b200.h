@@ -133,6 +133,24 @@ int gptoss_moe_combine(const float* h2, const int32_t* row_of_pair, const uint16
 int gptoss_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t rows, int32_t groups,
                          uint16_t* out, void* stream);
 
+/* MLPBlock.forward like gptoss_moe_forward, but allocating nothing: no
+ * cudaMalloc, no cudaFree, no workspace.  It has no counterpart in the
+ * reference.  It is for callers that cannot allocate device memory when the
+ * block runs -- a serving loop whose device memory is planned before the
+ * first request, code that must not call cudaMalloc because it synchronises
+ * the device, or a host without a CUDA allocator of its own.
+ * Its scratch is one fixed device array inside this library (about 6.3 MB,
+ * held on every GPU that loads the library until the process exits), sized
+ * for M <= 64 tokens, <= 128 experts, top_k <= 4 and hidden, intermediate
+ * <= 2880; larger sizes are rejected with an error.  All experts must be on
+ * this device.  The first call on each device looks up the array's device
+ * address (with that device current); make that first call before any
+ * stream capture.  Every call shares the array: calls that overlap on the
+ * GPU (two streams, or two host threads) race on it, and the array keeps
+ * the last call's contents.  x, out: [M, H] bf16 device memory. */
+int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gptoss_moe_weights* w, uint16_t* out,
+                               void* stream);
+
 /* --------------------------------------------- expert-parallel helpers
  * The reference runs the MoE block on one device (world_size = 1,
  * model/mlp.py:79); expert parallelism is new here.  Each rank owns
