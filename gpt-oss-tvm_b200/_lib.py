@@ -25,7 +25,11 @@ class gptoss_moe_weights(ctypes.Structure):
         ("norm_weight", ctypes.c_void_p), ("gate_weight", ctypes.c_void_p), ("gate_bias", ctypes.c_void_p),
         ("mlp1_blocks", ctypes.c_void_p), ("mlp1_scales", ctypes.c_void_p), ("mlp1_bias", ctypes.c_void_p),
         ("mlp2_blocks", ctypes.c_void_p), ("mlp2_scales", ctypes.c_void_p), ("mlp2_bias", ctypes.c_void_p),
+        ("flags", ctypes.c_uint32),
     ]
+
+
+MOE_F16 = 1  # GPTOSS_MOE_F16
 
 
 _P, _I64, _I32, _F = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_float
@@ -42,12 +46,22 @@ SIGNATURES = {
     "gptoss_moe_router": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P]),
     "gptoss_moe_topk_softmax": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _P, _P, _P]),
     "gptoss_moe_permute": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P]),
-    "gptoss_moe_gather": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _P]),
-    "gptoss_moe_mlp1": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _F, _F, _P, _P, _P]),
-    "gptoss_moe_mlp2": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
+    "gptoss_moe_gather": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P, _P]),
+    "gptoss_moe_mlp1": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _F, _F, _I32, _P, _P, _P]),
+    "gptoss_moe_mlp2": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P]),
+    "gptoss_moe_weights_prepare": (ctypes.c_int, [ctypes.POINTER(gptoss_moe_weights), _P]),
     "gptoss_moe_combine": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P]),
     "gptoss_mxfp4_dequant": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _P]),
     "gptoss_moe_forward_noalloc": (ctypes.c_int, [_P, _I64, ctypes.POINTER(gptoss_moe_weights), _P, _P]),
+    "gptoss_yarn_inv_freq": (ctypes.c_int, [_I32, _F, _F, _F, _F, _I32, _P, _P]),
+    "gptoss_rope_yarn": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P, _F, _P, _P]),
+    "gptoss_qkv_rope_append": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _F, _P, _P, _P, _P]),
+    "gptoss_attn_prefill": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I32, _F, _P, _P, _P]),
+    "gptoss_attn_decode_scratch_bytes": (ctypes.c_int64, [_I64, _I32, _I64, _I32]),
+    "gptoss_attn_decode": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I32, _F, _P, _P, _I64, _P,
+                                          _P, _P]),
+    "gptoss_attn_merge": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P, _P]),
+    "gptoss_attn_sink_rescale": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P]),
     "gptoss_moe_plan_tiles": (ctypes.c_int, [_P, _I32, _P, _P, _P]),
     "gptoss_moe_segment_copy": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I64, _I32, _P, _P]),
 }

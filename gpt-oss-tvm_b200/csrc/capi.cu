@@ -1,4 +1,6 @@
 // capi.cu -- the extern "C" boundary of libgptoss_b200.so (see include/gptoss_b200.h).
+#include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -7,39 +9,7 @@
 #include "../../include/gptoss_b200.h"
 #include "common.cuh"
 
-namespace gptoss {
-// moe_route.cu
-int launch_rmsnorm(const uint16_t*, const uint16_t*, int64_t, int32_t, float, uint16_t*, uint32_t*, cudaStream_t);
-int launch_router(const uint16_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t, uint16_t*,
-                  cudaStream_t);
-int launch_topk_softmax(const uint16_t*, int64_t, int32_t, int32_t, uint16_t*, int32_t*, uint32_t*, cudaStream_t);
-int launch_permute(const int32_t*, int64_t, int32_t, int32_t, int32_t*, int32_t*, int32_t*, int32_t*, int32_t*,
-                   int32_t*, uint32_t*, cudaStream_t);
-int launch_gather(const uint16_t*, const int32_t*, int64_t, int32_t, uint16_t*, cudaStream_t);
-int launch_combine(const float*, const int32_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t,
-                   uint16_t*, cudaStream_t);
-int launch_mxfp4_dequant(const uint8_t*, const uint8_t*, int64_t, uint16_t*, cudaStream_t);
-int launch_plan_tiles(const int32_t*, int32_t, int32_t*, int32_t*, cudaStream_t);
-int launch_segment_copy(const void*, void*, const int32_t*, int32_t, int32_t, int64_t, int32_t, int32_t*,
-                        cudaStream_t);
-// moe_gemm.cu
-struct GemmLaunch {
-  const uint16_t* act;
-  int64_t act_rows;
-  const uint8_t* blocks;
-  const uint8_t* scales;
-  const uint16_t* bias;
-  const int32_t* indptr;
-  const int32_t* tile_ptr;
-  const int32_t* tile_rows;
-  void* out;
-  int32_t E, N, K, ldo;
-  float alpha, limit;
-  uint32_t* err;
-  int grid;
-};
-int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream);
-}  // namespace gptoss
+#include "launch.h"
 
 using namespace gptoss;
 
@@ -121,16 +91,16 @@ int gptoss_moe_permute(const int32_t* topk_indices, int64_t M, int32_t K, int32_
                       "permute");
 }
 
-int gptoss_moe_gather(const uint16_t* t, const int32_t* token_of_row, int64_t rows, int32_t H, uint16_t* act,
-                      void* stream) {
+int gptoss_moe_gather(const uint16_t* t, const int32_t* token_of_row, int64_t rows, int32_t H, int32_t act_f16,
+                      uint16_t* act, void* stream) {
   if (rows < 0 || H <= 0 || H % 8) return fail(-1, "gptoss_moe_gather: H must be a multiple of 8");
-  return check_launch(launch_gather(t, token_of_row, rows, H, act, GPTOSS_STREAM(stream)), "gather");
+  return check_launch(launch_gather(t, token_of_row, rows, H, act, act_f16, GPTOSS_STREAM(stream)), "gather");
 }
 
 static int gemm_common(int mode, const uint16_t* act, int64_t act_rows, const int32_t* indptr,
                        const int32_t* tile_ptr, const int32_t* tile_rows, int32_t E, int32_t N, int32_t K,
                        const uint8_t* blocks, const uint8_t* scales, const uint16_t* bias, float alpha, float limit,
-                       void* out, int32_t ldo, uint32_t* err, void* stream) {
+                       void* out, int32_t ldo, int32_t act_f16, uint32_t* err, void* stream) {
   if (act_rows <= 0) return 0;
   if (E <= 0 || N <= 0 || K <= 0 || K % 64)
     return fail(-1, "moe gemm: K must be a positive multiple of 64 (got %d)", K);
@@ -154,22 +124,52 @@ static int gemm_common(int mode, const uint16_t* act, int64_t act_rows, const in
   L.limit = limit;
   L.err = err;
   L.grid = num_sms();
+  L.f16 = act_f16 ? 1 : 0;
   return check_launch(launch_moe_gemm(mode, L, GPTOSS_STREAM(stream)), mode == 0 ? "moe_mlp1" : "moe_mlp2");
 }
 
 int gptoss_moe_mlp1(const uint16_t* act, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
                     const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
-                    const uint8_t* scales, const uint16_t* bias, float alpha, float limit, uint16_t* y,
-                    uint32_t* err, void* stream) {
+                    const uint8_t* scales, const uint16_t* bias, float alpha, float limit, int32_t act_f16,
+                    uint16_t* y, uint32_t* err, void* stream) {
   return gemm_common(0, act, act_rows, indptr, tile_ptr, tile_rows, E, 2 * I, H, blocks, scales, bias, alpha, limit,
-                     y, I, err, stream);
+                     y, I, act_f16, err, stream);
 }
 
 int gptoss_moe_mlp2(const uint16_t* y, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
                     const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
-                    const uint8_t* scales, const uint16_t* bias, float* h2, uint32_t* err, void* stream) {
+                    const uint8_t* scales, const uint16_t* bias, int32_t act_f16, float* h2, uint32_t* err,
+                    void* stream) {
   return gemm_common(1, y, act_rows, indptr, tile_ptr, tile_rows, E, H, I, blocks, scales, bias, 0.f, 0.f, h2, H,
-                     err, stream);
+                     act_f16, err, stream);
+}
+
+int gptoss_moe_weights_prepare(gptoss_moe_weights* w, void* stream) {
+  if (!w) return fail(-1, "gptoss_moe_weights_prepare: null weights");
+  const int64_t El = w->num_local_experts;
+  const int64_t n1 = El * 2 * w->intermediate * (w->hidden / 32);
+  const int64_t n2 = El * w->hidden * (w->intermediate / 32);
+  uint32_t* d = nullptr;
+  if (cudaMalloc(&d, 16) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(-4, "gptoss_moe_weights_prepare: cudaMalloc failed");
+  }
+  const uint32_t init[4] = {255u, 0u, 0u, 0u};
+  cudaStream_t s = GPTOSS_STREAM(stream);
+  cudaMemcpyAsync(d, init, 16, cudaMemcpyHostToDevice, s);
+  int rc = launch_weight_ranges(w->mlp1_scales, n1, w->mlp2_scales, n2, w->norm_weight, w->hidden, d, s);
+  uint32_t h[4] = {0, 0, 0, 0};
+  if (rc == 0) cudaMemcpyAsync(h, d, 16, cudaMemcpyDeviceToHost, s);
+  cudaStreamSynchronize(s);
+  cudaFree(d);
+  if (rc) return check_launch(rc, "weights_prepare");
+  float max_norm;
+  memcpy(&max_norm, &h[2], 4);
+  // f16 path: every e2m1 x 2^(s-127) is an exact f16 for s in 104..140, and the
+  // RMSNorm output stays below sqrt(H) * max|norm weight| < 32768
+  const bool f16_ok = h[0] >= 104u && h[1] <= 140u && max_norm * sqrtf((float)w->hidden) < 32768.0f;
+  w->flags = (w->flags & ~(uint32_t)GPTOSS_MOE_F16) | (f16_ok ? (uint32_t)GPTOSS_MOE_F16 : 0u);
+  return 0;
 }
 
 int gptoss_moe_combine(const float* h2, const int32_t* row_of_pair, const uint16_t* topk_weights,
@@ -201,6 +201,92 @@ int gptoss_moe_segment_copy(const void* src, void* dst, const int32_t* counts, i
   return check_launch(launch_segment_copy(src, dst, counts, num_ranks, local_experts, row_bytes, direction,
                                           indptr_local, GPTOSS_STREAM(stream)),
                       "segment_copy");
+}
+
+// -------------------------------------------------------------- attention --
+int gptoss_yarn_inv_freq(int32_t D, float theta, float factor, float beta_fast, float beta_slow,
+                         int32_t original_max_position, float* inv_freq, float* concentration) {
+  if (D <= 0 || D % 2 || D > 256 || !inv_freq) return fail(-1, "gptoss_yarn_inv_freq: bad arguments");
+  // correction range in double precision (model/attention.py:15-36), then the
+  // per-dimension blend in fp32 (attention.py:39-61)
+  const double pi = 3.14159265358979323846;
+  auto corr_dim = [&](double rot) {
+    return (D * std::log((double)original_max_position / (rot * 2 * pi))) / (2 * std::log((double)theta));
+  };
+  double low = std::max(corr_dim(beta_fast), 0.0);
+  double high = std::min(corr_dim(beta_slow), (double)(D - 1));
+  if (low == high) high += 0.001;
+  const float lo_f = (float)low, hmlo_f = (float)(high - low);
+  for (int32_t f = 0; f < D / 2; ++f) {
+    const float e = (float)(f * 2 % D) / (float)D;
+    const float fp = powf(theta, e);
+    const float extra = 1.0f / fp;
+    const float inter = 1.0f / (factor * fp);
+    float v = ((float)f - lo_f) / hmlo_f;
+    v = v < 1.0f ? v : 1.0f;
+    const float ramp = 1.0f - (v > 0.0f ? v : 0.0f);
+    inv_freq[f] = inter * (1.0f - ramp) + extra * ramp;
+  }
+  if (concentration) concentration[0] = factor > 1.0f ? (float)(0.1 * std::log((double)factor) + 1.0) : 1.0f;
+  return 0;
+}
+
+int gptoss_rope_yarn(const uint16_t* x, const int32_t* positions, int64_t S, int32_t heads, int32_t D,
+                     const float* inv_freq, float concentration, uint16_t* out, void* stream) {
+  if (S < 0 || heads <= 0 || D <= 0 || D % 2 || D > 256 || !inv_freq) return fail(-1, "gptoss_rope_yarn: bad shape");
+  return check_launch(launch_rope(x, positions, S, heads, D, inv_freq, concentration, out, GPTOSS_STREAM(stream)),
+                      "rope_yarn");
+}
+
+int gptoss_qkv_rope_append(const uint16_t* qkv, const int32_t* positions, const int32_t* slots, int64_t S,
+                           int32_t Hq, int32_t Hkv, int32_t D, const float* inv_freq, float concentration,
+                           uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, void* stream) {
+  if (S < 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || D % 2 || D > 256 || !inv_freq)
+    return fail(-1, "gptoss_qkv_rope_append: bad shape");
+  return check_launch(launch_qkv_rope(qkv, positions, slots, S, Hq, Hkv, D, inv_freq, concentration, q_out, k_cache,
+                                      v_cache, GPTOSS_STREAM(stream)),
+                      "qkv_rope_append");
+}
+
+int gptoss_attn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* sinks, int64_t Sq,
+                        int64_t Skv, int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale, uint16_t* o,
+                        float* lse, void* stream) {
+  if (D != 64) return fail(-1, "gptoss_attn_prefill: head_dim must be 64");
+  if (Sq < 0 || Skv < Sq || Hq <= 0 || Hkv <= 0 || Hq % Hkv)
+    return fail(-1, "gptoss_attn_prefill: need 0 <= Sq <= Skv and Hq a multiple of Hkv");
+  return check_launch(launch_attn_prefill(q, k, v, sinks, Sq, Skv, Hq, Hkv, D, window, sm_scale, o, lse,
+                                          GPTOSS_STREAM(stream)),
+                      "attn_prefill");
+}
+
+int64_t gptoss_attn_decode_scratch_bytes(int64_t B, int32_t Hq, int64_t max_len, int32_t window) {
+  return (int64_t)attn_decode_scratch_bytes(B, Hq, max_len, attn_decode_splits(max_len, window));
+}
+
+int gptoss_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* kv_len,
+                       int64_t B, int64_t max_len, int32_t Hq, int32_t Hkv, int32_t D, int32_t window,
+                       float sm_scale, const uint16_t* sinks, float* scratch, int64_t scratch_bytes, uint16_t* o,
+                       float* lse, void* stream) {
+  if (D != 64) return fail(-1, "gptoss_attn_decode: head_dim must be 64");
+  if (B < 0 || max_len <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Hq / Hkv > 8)
+    return fail(-1, "gptoss_attn_decode: bad shape (Hq/Hkv must be <= 8)");
+  if (scratch_bytes < gptoss_attn_decode_scratch_bytes(B, Hq, max_len, window))
+    return fail(-1, "gptoss_attn_decode: scratch smaller than gptoss_attn_decode_scratch_bytes()");
+  return check_launch(launch_attn_decode(q, k_cache, v_cache, kv_len, B, max_len, Hq, Hkv, D, window, sm_scale, sinks,
+                                         scratch, o, lse, GPTOSS_STREAM(stream)),
+                      "attn_decode");
+}
+
+int gptoss_attn_merge(const uint16_t* o1, const float* lse1, const uint16_t* o2, const float* lse2, int64_t T,
+                      int32_t Hq, int32_t D, uint16_t* o, float* lse, void* stream) {
+  if (T < 0 || Hq <= 0 || D <= 0) return fail(-1, "gptoss_attn_merge: bad shape");
+  return check_launch(launch_attn_merge(o1, lse1, o2, lse2, T, Hq, D, o, lse, GPTOSS_STREAM(stream)), "attn_merge");
+}
+
+int gptoss_attn_sink_rescale(uint16_t* o, const float* lse, const uint16_t* sinks, int64_t T, int32_t Hq, int32_t D,
+                             void* stream) {
+  if (T < 0 || Hq <= 0 || D <= 0) return fail(-1, "gptoss_attn_sink_rescale: bad shape");
+  return check_launch(launch_sink_rescale(o, lse, sinks, T, Hq, D, GPTOSS_STREAM(stream)), "sink_rescale");
 }
 
 }  // extern "C"
@@ -314,6 +400,7 @@ int gptoss_moe_forward(const uint16_t* x, int64_t M, const gptoss_moe_weights* w
     return fail(-1, "gptoss_moe_forward: expert-parallel weights need the dispatch/combine path");
   if (M == 0) return 0;
   const int32_t E = w->num_experts, K = w->top_k, H = w->hidden, I = w->intermediate;
+  const int32_t f16 = (w->flags & GPTOSS_MOE_F16) ? 1 : 0;
   const int64_t R = M * K;
   int rc;
   if ((rc = gptoss_rms_norm(x, w->norm_weight, M, H, w->rms_eps, ws->t, stream))) return rc;
@@ -323,12 +410,13 @@ int gptoss_moe_forward(const uint16_t* x, int64_t M, const gptoss_moe_weights* w
   if ((rc = gptoss_moe_permute(ws->topk_idx, M, K, E, ws->indptr, ws->token_of_row, ws->row_of_pair,
                                ws->expert_of_row, ws->tile_ptr, ws->tile_rows, ws->err, stream)))
     return rc;
-  if ((rc = gptoss_moe_gather(ws->t, ws->token_of_row, R, H, ws->act, stream))) return rc;
+  if ((rc = gptoss_moe_gather(ws->t, ws->token_of_row, R, H, f16, ws->act, stream))) return rc;
   if ((rc = gptoss_moe_mlp1(ws->act, R, ws->indptr, ws->tile_ptr, ws->tile_rows, E, H, I, w->mlp1_blocks,
-                            w->mlp1_scales, w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, ws->y, ws->err, stream)))
+                            w->mlp1_scales, w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, f16, ws->y, ws->err,
+                            stream)))
     return rc;
   if ((rc = gptoss_moe_mlp2(ws->y, R, ws->indptr, ws->tile_ptr, ws->tile_rows, E, H, I, w->mlp2_blocks,
-                            w->mlp2_scales, w->mlp2_bias, ws->h2, ws->err, stream)))
+                            w->mlp2_scales, w->mlp2_bias, f16, ws->h2, ws->err, stream)))
     return rc;
   return gptoss_moe_combine(ws->h2, ws->row_of_pair, ws->topk_w, x, M, K, H, out, stream);
 }

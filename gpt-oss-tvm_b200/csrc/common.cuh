@@ -10,6 +10,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -49,6 +50,9 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return (uint16_t)(u >> 16);
 }
 __device__ __forceinline__ float round_bf16(float f) { return bf16_bits_to_f32(f32_to_bf16_bits(f)); }
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
 // ------------------------------------------------------------- smem addr --
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -158,6 +162,11 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(uint32_t M, uint32_t N) {
          | (1u << 10)         // B format bf16
          | ((N >> 3) << 17)   // N / 8
          | ((M >> 4) << 24);  // M / 16
+}
+
+// Instruction descriptor for kind::f16: f16 A/B, fp32 D, both K-major.
+__host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t M, uint32_t N) {
+  return (1u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle,

@@ -1,0 +1,67 @@
+// launch.h -- host-side launch helpers shared between the kernel files and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gptoss {
+
+// Arguments of one grouped expert GEMM (moe_gemm.cu).
+struct GemmLaunch {
+  const uint16_t* act;   // [act_rows, K] bf16 or f16, expert-major rows
+  int64_t act_rows;
+  const uint8_t* blocks;  // [E, N, K/32, 16]
+  const uint8_t* scales;  // [E, N, K/32]
+  const uint16_t* bias;   // [E, N] bf16
+  const int32_t* indptr;
+  const int32_t* tile_ptr;
+  const int32_t* tile_rows;
+  void* out;  // mode 0: [act_rows, N/2] (bf16, or f16 when f16); mode 1: [act_rows, N] f32
+  int32_t E, N, K, ldo;
+  float alpha, limit;
+  uint32_t* err;
+  int grid;
+  int f16;  // 1: f16 activations and hardware e2m1 -> f16 weight decode
+};
+int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream);
+
+// moe_route.cu
+int launch_rmsnorm(const uint16_t*, const uint16_t*, int64_t, int32_t, float, uint16_t*, uint32_t*, cudaStream_t);
+int launch_router(const uint16_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t, uint16_t*,
+                  cudaStream_t);
+int launch_topk_softmax(const uint16_t*, int64_t, int32_t, int32_t, uint16_t*, int32_t*, uint32_t*, cudaStream_t);
+int launch_permute(const int32_t*, int64_t, int32_t, int32_t, int32_t*, int32_t*, int32_t*, int32_t*, int32_t*,
+                   int32_t*, uint32_t*, cudaStream_t);
+int launch_gather(const uint16_t*, const int32_t*, int64_t, int32_t, uint16_t*, int32_t to_f16, cudaStream_t);
+int launch_combine(const float*, const int32_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t,
+                   uint16_t*, cudaStream_t);
+int launch_mxfp4_dequant(const uint8_t*, const uint8_t*, int64_t, uint16_t*, cudaStream_t);
+int launch_plan_tiles(const int32_t*, int32_t, int32_t*, int32_t*, cudaStream_t);
+int launch_segment_copy(const void*, void*, const int32_t*, int32_t, int32_t, int64_t, int32_t, int32_t*,
+                        cudaStream_t);
+int launch_weight_ranges(const uint8_t* s1, int64_t n1, const uint8_t* s2, int64_t n2, const uint16_t* norm_w,
+                         int32_t H, uint32_t* out4, cudaStream_t);
+
+// attention.cu
+int launch_qkv_rope(const uint16_t* qkv, const int32_t* pos, const int32_t* slot, int64_t S, int32_t Hq, int32_t Hkv,
+                    int32_t D, const float* inv_freq, float conc, uint16_t* q_out, uint16_t* k_cache,
+                    uint16_t* v_cache, cudaStream_t s);
+int launch_rope(const uint16_t* x, const int32_t* pos, int64_t S, int32_t Hh, int32_t D, const float* inv_freq,
+                float conc, uint16_t* out, cudaStream_t s);
+int launch_attn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* sinks, int64_t Sq,
+                        int64_t Skv, int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale, uint16_t* o,
+                        float* lse, cudaStream_t s);
+size_t attn_decode_scratch_bytes(int64_t B, int32_t Hq, int64_t max_len, int32_t splits);
+int attn_decode_splits(int64_t max_len, int32_t window);
+int launch_attn_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* kv_len, int64_t B,
+                       int64_t max_len, int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale,
+                       const uint16_t* sinks, float* scratch, uint16_t* o, float* lse, cudaStream_t s);
+int launch_attn_merge(const uint16_t* o1, const float* l1, const uint16_t* o2, const float* l2, int64_t T, int32_t Hq,
+                      int32_t D, uint16_t* o, float* lse, cudaStream_t s);
+int launch_sink_rescale(uint16_t* o, const float* lse, const uint16_t* sinks, int64_t T, int32_t Hq, int32_t D,
+                        cudaStream_t s);
+
+// capi.cu: records a message for gptoss_last_error()
+int set_last_error(int code, const char* msg);
+
+}  // namespace gptoss

@@ -27,6 +27,7 @@
 // the epilogue of tile i overlaps the main loop of tile i+1), 12 activation
 // TMA, 13 MMA issuer (also owns TMEM), 14 weight TMA.
 #include "common.cuh"
+#include "launch.h"
 
 namespace gptoss {
 
@@ -110,7 +111,35 @@ __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[
       : "memory");
 }
 
-template <int kMode>
+// e2m1 -> f16 decode of 8 nibbles with the hardware converter, scaled by the
+// E8M0 power of two as packed f16 (exact for scale codes 104..140: every
+// product is an f16 normal or subnormal number).
+__device__ __forceinline__ void fp4x8_to_f16x8(uint32_t w, uint32_t scale2, uint32_t& o0, uint32_t& o1, uint32_t& o2,
+                                               uint32_t& o3) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(o0), "=r"(o1), "=r"(o2), "=r"(o3)
+      : "r"(w));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o0) : "r"(scale2));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o1) : "r"(scale2));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o2) : "r"(scale2));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o3) : "r"(scale2));
+}
+
+// 2^(s-127) as an f16 pair (normal for s >= 113, subnormal for 103..112).
+__device__ __forceinline__ uint32_t e8m0_scale_f16x2(uint32_t s) {
+  const uint32_t h = s >= 113u ? ((s - 112u) << 10) : (1u << (s - 103u));
+  return h | (h << 16);
+}
+
+// kF16: weights decoded to f16 by the hardware converter and activations in
+// f16 (the fast path, valid when every scale code is in 104..140); otherwise
+// exact bf16 decode and bf16 activations.
+template <int kMode, bool kF16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_w,
                        const GemmParams p) {
@@ -226,7 +255,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         TileInfo ti;
         if (!decode_tile(p, t, ftiles, ti)) continue;
         const uint32_t n_mma = (uint32_t)((ti.nrows + 15) & ~15);
-        const uint32_t idesc = make_idesc_bf16(kBM, n_mma);
+        const uint32_t idesc = kF16 ? make_idesc_f16(kBM, n_mma) : make_idesc_bf16(kBM, n_mma);
         const uint32_t ab = tl & 1, aph = (tl >> 1) & 1;
         if (!mbar_wait(&accempty_bar[ab], aph ^ 1, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
         tc_fence_after();
@@ -276,12 +305,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) mbar_arrive(&wempty_bar[ws]);
         uint32_t r[16];
         if (row_ok) {
-          const uint32_t sc2 = e8m0_scale_bf16x2(sc);
-          uint32_t o[4];
-          fp4x8_to_bf16x8(nb.x, sc2, o); r[0] = o[0]; r[1] = o[1]; r[2] = o[2]; r[3] = o[3];
-          fp4x8_to_bf16x8(nb.y, sc2, o); r[4] = o[0]; r[5] = o[1]; r[6] = o[2]; r[7] = o[3];
-          fp4x8_to_bf16x8(nb.z, sc2, o); r[8] = o[0]; r[9] = o[1]; r[10] = o[2]; r[11] = o[3];
-          fp4x8_to_bf16x8(nb.w, sc2, o); r[12] = o[0]; r[13] = o[1]; r[14] = o[2]; r[15] = o[3];
+          if (kF16) {
+            const uint32_t sc2 = e8m0_scale_f16x2(sc);
+            fp4x8_to_f16x8(nb.x, sc2, r[0], r[1], r[2], r[3]);
+            fp4x8_to_f16x8(nb.y, sc2, r[4], r[5], r[6], r[7]);
+            fp4x8_to_f16x8(nb.z, sc2, r[8], r[9], r[10], r[11]);
+            fp4x8_to_f16x8(nb.w, sc2, r[12], r[13], r[14], r[15]);
+          } else {
+            const uint32_t sc2 = e8m0_scale_bf16x2(sc);
+            uint32_t o[4];
+            fp4x8_to_bf16x8(nb.x, sc2, o); r[0] = o[0]; r[1] = o[1]; r[2] = o[2]; r[3] = o[3];
+            fp4x8_to_bf16x8(nb.y, sc2, o); r[4] = o[0]; r[5] = o[1]; r[6] = o[2]; r[7] = o[3];
+            fp4x8_to_bf16x8(nb.z, sc2, o); r[8] = o[0]; r[9] = o[1]; r[10] = o[2]; r[11] = o[3];
+            fp4x8_to_bf16x8(nb.w, sc2, o); r[12] = o[0]; r[13] = o[1]; r[14] = o[2]; r[15] = o[3];
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) r[j] = 0u;
@@ -341,7 +378,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const float l = fmaxf(fminf(li, p.limit), -p.limit);
             const float sg = 1.0f / (1.0f + expf(-(p.alpha * g)));
             const float y = (g * sg) * (l + 1.0f);
-            if (row_ok && col < ti.nrows) out[(size_t)(ti.row0 + col) * p.ldo + (frow >> 1)] = f32_to_bf16_bits(y);
+            if (row_ok && col < ti.nrows)
+              out[(size_t)(ti.row0 + col) * p.ldo + (frow >> 1)] =
+                  kF16 ? __half_as_ushort(__float2half_rn(y)) : f32_to_bf16_bits(y);
           }
         } else {
           float* out = (float*)p.out;
@@ -400,21 +439,18 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-struct GemmLaunch {
-  const uint16_t* act;       // [R_alloc, K] bf16
-  int64_t act_rows;          // R_alloc
-  const uint8_t* blocks;     // [E, N, G, 16]
-  const uint8_t* scales;     // [E, N, G]
-  const uint16_t* bias;      // [E, N]
-  const int32_t* indptr;
-  const int32_t* tile_ptr;
-  const int32_t* tile_rows;
-  void* out;
-  int32_t E, N, K, ldo;
-  float alpha, limit;
-  uint32_t* err;
-  int grid;
-};
+
+
+template <int kMode, bool kF16>
+static void launch_variant(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, int grid, int smem,
+                           cudaStream_t stream) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(moe_gemm_tc_kernel<kMode, kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr = true;
+  }
+  moe_gemm_tc_kernel<kMode, kF16><<<grid, kGemmThreads, smem, stream>>>(ta, tw, p);
+}
 
 int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
   if (L.K % kBK != 0 || L.K / 32 > kMaxGroups) return -10;
@@ -425,8 +461,8 @@ int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
     if (((int64_t)kBM * G) % 16 || ((int64_t)last * G) % 16 || ((int64_t)L.N * G) % 16) return -11;
   }
   CUtensorMap tmap_act, tmap_w;
-  int rc = make_tmap_2d(&tmap_act, L.act, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)L.act_rows,
-                        (uint64_t)L.K, kBK, kBoxRows, CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = make_tmap_2d(&tmap_act, L.act, L.f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                        (uint64_t)L.act_rows, (uint64_t)L.K, kBK, kBoxRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap_2d(&tmap_w, L.blocks, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)L.E * L.N, (uint64_t)L.K / 2,
                     kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_32B);
@@ -447,19 +483,11 @@ int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
   p.err = L.err;
   const int smem = GemmSmem::kAlloc;
   if (mode == 0) {
-    static bool attr0 = false;
-    if (!attr0) {
-      cudaFuncSetAttribute(moe_gemm_tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      attr0 = true;
-    }
-    moe_gemm_tc_kernel<0><<<L.grid, kGemmThreads, smem, stream>>>(tmap_act, tmap_w, p);
+    if (L.f16) launch_variant<0, true>(tmap_act, tmap_w, p, L.grid, smem, stream);
+    else launch_variant<0, false>(tmap_act, tmap_w, p, L.grid, smem, stream);
   } else {
-    static bool attr1 = false;
-    if (!attr1) {
-      cudaFuncSetAttribute(moe_gemm_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      attr1 = true;
-    }
-    moe_gemm_tc_kernel<1><<<L.grid, kGemmThreads, smem, stream>>>(tmap_act, tmap_w, p);
+    if (L.f16) launch_variant<1, true>(tmap_act, tmap_w, p, L.grid, smem, stream);
+    else launch_variant<1, false>(tmap_act, tmap_w, p, L.grid, smem, stream);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -113,6 +113,7 @@ extern "C" int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gp
   float* h2 = (float*)(base + kOffH2);
 
   const int32_t E = w->num_experts, K = w->top_k, H = w->hidden, I = w->intermediate;
+  const int32_t f16 = (w->flags & GPTOSS_MOE_F16) ? 1 : 0;
   const int64_t R = M * K;
   int rc;
   if ((rc = gptoss_rms_norm(x, w->norm_weight, M, H, w->rms_eps, t, stream))) return rc;
@@ -121,12 +122,12 @@ extern "C" int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gp
     return rc;
   if ((rc = gptoss_moe_permute(topk_idx, M, K, E, indptr, tok, rev, exr, tile_ptr, tile_rows, nullptr, stream)))
     return rc;
-  if ((rc = gptoss_moe_gather(t, tok, R, H, act, stream))) return rc;
+  if ((rc = gptoss_moe_gather(t, tok, R, H, f16, act, stream))) return rc;
   if ((rc = gptoss_moe_mlp1(act, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp1_blocks, w->mlp1_scales,
-                            w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, y, nullptr, stream)))
+                            w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, f16, y, nullptr, stream)))
     return rc;
   if ((rc = gptoss_moe_mlp2(y, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp2_blocks, w->mlp2_scales, w->mlp2_bias,
-                            h2, nullptr, stream)))
+                            f16, h2, nullptr, stream)))
     return rc;
   return gptoss_moe_combine(h2, rev, topk_w, x, M, K, H, out, stream);
 }

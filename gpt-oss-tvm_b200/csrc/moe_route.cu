@@ -25,6 +25,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
   __shared__ uint64_t bar;
   __shared__ float rs[kNormRows];
   uint16_t* rowbuf = (uint16_t*)norm_smem;
+  const int32_t pitch = H + 8;  // padded row pitch (elements): rows start on different banks
   const int64_t m0 = (int64_t)blockIdx.x * rows_per_block;
   const int64_t left = M - m0;
   const int nrows = left < rows_per_block ? (int)left : rows_per_block;
@@ -39,14 +40,14 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
     for (int r = 0; r < nrows; ++r) {
       asm volatile(
           "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-              smem_u32(rowbuf + (size_t)r * H)),
+              smem_u32(rowbuf + (size_t)r * pitch)),
           "l"(x + (m0 + r) * H), "r"(row_bytes), "r"(smem_u32(&bar))
           : "memory");
     }
   }
   const bool ok = mbar_wait(&bar, 0, err, kErrTimeoutOther);
   if (ok && threadIdx.x < nrows) {
-    const uint4* row = (const uint4*)(rowbuf + (size_t)threadIdx.x * H);
+    const uint4* row = (const uint4*)(rowbuf + (size_t)threadIdx.x * pitch);
     float ss = 0.0f;
     for (int32_t k8 = 0; k8 < H / 8; ++k8) {
       const uint4 v = row[k8];
@@ -65,7 +66,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
   const int32_t h2 = H / 2;
   for (int r = 0; r < nrows; ++r) {
     const float rr = rs[r];
-    const uint32_t* src = (const uint32_t*)(rowbuf + (size_t)r * H);
+    const uint32_t* src = (const uint32_t*)(rowbuf + (size_t)r * pitch);
     uint32_t* dst = (uint32_t*)(out + (m0 + r) * H);
     for (int32_t j = threadIdx.x; j < h2; j += blockDim.x) {
       const uint32_t v = src[j];
@@ -87,7 +88,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
 // chains; two chains share one packed f32x2 FMA.
 constexpr int kRTT = 4;   // tokens per thread
 constexpr int kRTE = 8;   // experts per thread
-constexpr int kRKT = 16;  // k per shared-memory stage
+constexpr int kRKT = 32;  // k per shared-memory stage (multiple of 8)
 
 // bf16 rounding of two fp32 accumulators held as a packed pair.
 template <int kRound>
@@ -125,27 +126,72 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
   const int tg = threadIdx.x % tgroups, eg = threadIdx.x / tgroups;
   const int64_t tok0 = (int64_t)blockIdx.x * btok;
   const int32_t e0 = blockIdx.y * block_experts;
+  constexpr int kParts = kRKT / 8;                  // 16-byte pieces per row per stage
+  constexpr int kMaxTQ = 16, kMaxWQ = 4;
+  const int ntq = (btok * kParts + 127) / 128, nwq = (block_experts * kParts + 127) / 128;
+  uint4 tq[kMaxTQ], wq[kMaxWQ];
+  auto load_stage = [&](int32_t k0) {
+#pragma unroll
+    for (int q = 0; q < kMaxTQ; ++q) {
+      if (q >= ntq) break;
+      const int j = threadIdx.x + 128 * q;
+      const int tok = j / kParts, part = j % kParts;
+      const int64_t m = tok0 + tok;
+      tq[q] = make_uint4(0, 0, 0, 0);
+      if (tok < btok && m < M && k0 + part * 8 < H) tq[q] = *(const uint4*)(t + m * H + k0 + part * 8);
+    }
+#pragma unroll
+    for (int q = 0; q < kMaxWQ; ++q) {
+      if (q >= nwq) break;
+      const int j = threadIdx.x + 128 * q;
+      const int e = j / kParts, part = j % kParts;
+      wq[q] = make_uint4(0, 0, 0, 0);
+      if (e < block_experts && e0 + e < E && k0 + part * 8 < H)
+        wq[q] = *(const uint4*)(W + (int64_t)(e0 + e) * H + k0 + part * 8);
+    }
+  };
+  auto store_stage = [&]() {
+#pragma unroll
+    for (int q = 0; q < kMaxTQ; ++q) {
+      if (q >= ntq) break;
+      const int j = threadIdx.x + 128 * q;
+      const int tok = j / kParts, part = j % kParts;
+      if (tok >= btok) continue;
+      const uint32_t v[4] = {tq[q].x, tq[q].y, tq[q].z, tq[q].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float lo = __uint_as_float(v[i] << 16), hi = __uint_as_float(v[i] & 0xFFFF0000u);
+        *(float2*)(ts + ((part * 8 + 2 * i) * btok + tok) * 2) = make_float2(lo, lo);
+        *(float2*)(ts + ((part * 8 + 2 * i + 1) * btok + tok) * 2) = make_float2(hi, hi);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < kMaxWQ; ++q) {
+      if (q >= nwq) break;
+      const int j = threadIdx.x + 128 * q;
+      const int e = j / kParts, part = j % kParts;
+      if (e >= block_experts) continue;
+      const uint32_t v[4] = {wq[q].x, wq[q].y, wq[q].z, wq[q].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        ws[(part * 8 + 2 * i) * block_experts + e] = __uint_as_float(v[i] << 16);
+        ws[(part * 8 + 2 * i + 1) * block_experts + e] = __uint_as_float(v[i] & 0xFFFF0000u);
+      }
+    }
+  };
+
   unsigned long long acc[kRTT][kRTE / 2];
 #pragma unroll
   for (int i = 0; i < kRTT; ++i)
 #pragma unroll
     for (int j = 0; j < kRTE / 2; ++j) acc[i][j] = 0ull;
 
+  load_stage(0);
   for (int32_t k0 = 0; k0 < H; k0 += kRKT) {
     __syncthreads();
-    for (int i = threadIdx.x; i < btok * kRKT; i += 128) {
-      const int tok = i / kRKT, kk = i % kRKT;
-      const int64_t m = tok0 + tok;
-      const float v = (m < M && k0 + kk < H) ? bf16_bits_to_f32(t[m * H + k0 + kk]) : 0.0f;
-      ts[(kk * btok + tok) * 2] = v;
-      ts[(kk * btok + tok) * 2 + 1] = v;
-    }
-    for (int i = threadIdx.x; i < block_experts * kRKT; i += 128) {
-      const int e = i / kRKT, kk = i % kRKT;
-      ws[kk * block_experts + e] = (e0 + e < E && k0 + kk < H) ? bf16_bits_to_f32(W[(int64_t)(e0 + e) * H + k0 + kk])
-                                                               : 0.0f;
-    }
+    store_stage();
     __syncthreads();
+    if (k0 + kRKT < H) load_stage(k0 + kRKT);  // next stage's loads overlap this stage's chains
     const int32_t kn = min(kRKT, H - k0);
     for (int32_t kk = 0; kk < kn; ++kk) {
       const ulonglong2* tp = (const ulonglong2*)(ts + (kk * btok + tg * kRTT) * 2);
@@ -158,9 +204,9 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
       for (int i = 0; i < kRTT; ++i) {
 #pragma unroll
         for (int j = 0; j < kRTE / 2; ++j) {
-          unsigned long long s = acc[i][j];
-          asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(s) : "l"(tv[i]), "l"(wv[j]));
-          acc[i][j] = round_pair_bf16<kRound>(s);
+          unsigned long long sacc = acc[i][j];
+          asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(sacc) : "l"(tv[i]), "l"(wv[j]));
+          acc[i][j] = round_pair_bf16<kRound>(sacc);
         }
       }
     }
@@ -172,7 +218,7 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
 #pragma unroll
     for (int j = 0; j < kRTE / 2; ++j) {
       const int32_t e = e0 + eg * kRTE + 2 * j;
-      if (e + 1 < E + 1 && e < E) {
+      if (e < E) {
         const float a0 = __uint_as_float((uint32_t)acc[i][j]);
         logits[m * E + e] = f32_to_bf16_bits(__fadd_rn(a0, bf16_bits_to_f32(b[e])));
       }
@@ -318,7 +364,11 @@ __global__ void __launch_bounds__(1024) moe_place_kernel(const int32_t* __restri
 }
 
 // ------------------------------------------------------------- gather --
-// act[row] = t[token_of_row[row]]  (nn.op.take at model/mlp_optimized.py:150)
+// act[row] = t[token_of_row[row]]  (nn.op.take at model/mlp_optimized.py:150),
+// optionally converted from bf16 to f16 for the f16 GEMM path (exact for
+// |v| in the f16 normal range, which RMSNorm output stays in when the norm
+// weights pass gptoss_moe_weights_prepare's check).
+template <bool kToF16>
 __global__ void gather_rows_kernel(const uint16_t* __restrict__ t, const int32_t* __restrict__ token_of_row,
                                    int64_t rows, int32_t H, uint16_t* __restrict__ act) {
   const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -327,7 +377,18 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ t, const int32_t
   const int64_t src = token_of_row[r];
   const uint4* s = (const uint4*)(t + src * H);
   uint4* d = (uint4*)(act + r * H);
-  for (int32_t i = lane; i < H / 8; i += 32) d[i] = s[i];
+  for (int32_t i = lane; i < H / 8; i += 32) {
+    uint4 v = s[i];
+    if (kToF16) {
+      uint32_t* w = (uint32_t*)&v;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __half2 h = __floats2half2_rn(__uint_as_float(w[q] << 16), __uint_as_float(w[q] & 0xFFFF0000u));
+        w[q] = *(const uint32_t*)&h;
+      }
+    }
+    d[i] = v;
+  }
 }
 
 // ------------------------------------------------------------ combine --
@@ -369,6 +430,36 @@ __global__ void mxfp4_dequant_kernel(const uint8_t* __restrict__ blocks, const u
   for (int q = 0; q < 4; ++q) {
     fp4x8_to_bf16x8(words[q], sc, o);
     dst[q] = make_uint4(bf16x2_mul(o[0], fix), bf16x2_mul(o[1], fix), bf16x2_mul(o[2], fix), bf16x2_mul(o[3], fix));
+  }
+}
+
+// ------------------------------------------------------ weight ranges --
+// min / max of the E8M0 scale codes of both projections and the largest
+// |norm weight| (as fp32 bits), for choosing the f16 GEMM path.
+// out4 = {min scale, max scale, max |norm weight| bits, unused}.
+__global__ void weight_ranges_kernel(const uint8_t* __restrict__ s1, int64_t n1, const uint8_t* __restrict__ s2,
+                                     int64_t n2, const uint16_t* __restrict__ norm_w, int32_t H,
+                                     uint32_t* __restrict__ out4) {
+  uint32_t lo = 255, hi = 0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n1 + n2; i += stride) {
+    const uint32_t v = i < n1 ? s1[i] : s2[i - n1];
+    lo = min(lo, v);
+    hi = max(hi, v);
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, off));
+    hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, off));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMin(&out4[0], lo);
+    atomicMax(&out4[1], hi);
+  }
+  if (blockIdx.x == 0) {
+    uint32_t m = 0;
+    for (int32_t k = threadIdx.x; k < H; k += blockDim.x) m = max(m, (uint32_t)(norm_w[k] & 0x7FFFu) << 16);
+    for (int off = 16; off > 0; off >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if ((threadIdx.x & 31) == 0) atomicMax(&out4[2], m);  // positive floats order like their bits
   }
 }
 
@@ -427,7 +518,7 @@ int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, f
                    uint32_t* err, cudaStream_t s) {
   if (M <= 0) return 0;
   if (H % 8 || ((uintptr_t)x & 15)) return -12;
-  const size_t row = (size_t)H * 2;
+  const size_t row = (size_t)(H + 8) * 2;
   const size_t fit = (size_t)(100 * 1024) / row;
   int rows = fit < (size_t)kNormRows ? (int)fit : kNormRows;
   if (rows < 1) return -12;
@@ -445,13 +536,14 @@ int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, f
 int launch_router(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H,
                   uint16_t* logits, cudaStream_t s) {
   if (M <= 0) return 0;
-  if (E % kRTE != 0 || E > 1024) return -12;
+  if (E % kRTE != 0 || E > 1024 || H % 8 || ((uintptr_t)t & 15) || ((uintptr_t)W & 15)) return -12;
   const int block_experts = E >= 64 ? 64 : E;
   if (E % block_experts) return -12;
   const int egroups = block_experts / kRTE;
   if (128 % egroups) return -12;
   const int btok = (128 / egroups) * kRTT;
   const size_t smem = (size_t)kRKT * btok * 2 * 4 + (size_t)kRKT * block_experts * 4;
+  if (smem > 200 * 1024) return -12;
   dim3 grid((unsigned)((M + btok - 1) / btok), (unsigned)(E / block_experts));
   static int round_mode = -1;
   if (round_mode < 0) {
@@ -460,9 +552,9 @@ int launch_router(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64
   }
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(router_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    cudaFuncSetAttribute(router_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    cudaFuncSetAttribute(router_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    cudaFuncSetAttribute(router_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(router_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(router_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr = true;
   }
   if (round_mode == 1) router_kernel<1><<<grid, 128, smem, s>>>(t, W, b, M, E, H, block_experts, logits);
@@ -490,10 +582,11 @@ int launch_permute(const int32_t* idx, int64_t M, int32_t K, int32_t E, int32_t*
 }
 
 int launch_gather(const uint16_t* t, const int32_t* token_of_row, int64_t rows, int32_t H, uint16_t* act,
-                  cudaStream_t s) {
+                  int32_t to_f16, cudaStream_t s) {
   if (rows <= 0) return 0;
   if (H % 8) return -12;
-  gather_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(t, token_of_row, rows, H, act);
+  if (to_f16) gather_rows_kernel<true><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(t, token_of_row, rows, H, act);
+  else gather_rows_kernel<false><<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(t, token_of_row, rows, H, act);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -515,6 +608,11 @@ int launch_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t g
 }  // namespace gptoss
 
 namespace gptoss {
+int launch_weight_ranges(const uint8_t* s1, int64_t n1, const uint8_t* s2, int64_t n2, const uint16_t* norm_w,
+                         int32_t H, uint32_t* out4, cudaStream_t s) {
+  weight_ranges_kernel<<<592, 256, 0, s>>>(s1, n1, s2, n2, norm_w, H, out4);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
 int launch_plan_tiles(const int32_t* indptr, int32_t E, int32_t* tile_ptr, int32_t* tile_rows, cudaStream_t s) {
   moe_plan_tiles_kernel<<<1, 32, 0, s>>>(indptr, E, tile_ptr, tile_rows);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;

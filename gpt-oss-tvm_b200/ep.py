@@ -67,6 +67,7 @@ class CudaBackend:
         self.tile_ptr = torch.empty(El + 1, **i32)
         self.tile_rows = torch.empty(El, **i32)
         self.err = torch.zeros(4, **i32)
+        self.f16 = 1 if blk.f16_path else 0  # rows travel in the GEMM's activation type
         self._recv_cap = 0
         self.h2_back = torch.empty(R, H, dtype=torch.float32, device=dev)
 
@@ -92,7 +93,7 @@ class CudaBackend:
                   _ptr(self.logits), _ptr(self.w), _ptr(self.idx), _ptr(self.err), S)
         _lib.call("gptoss_moe_permute", _ptr(self.idx), M, k, E, _ptr(self.indptr), _ptr(self.tok), _ptr(self.rev),
                   _ptr(self.exr), _ptr(self.tile_ptr_g), _ptr(self.tile_rows_g), _ptr(self.err), S)
-        _lib.call("gptoss_moe_gather", _ptr(self.t), _ptr(self.tok), M * k, H, _ptr(self.send), S)
+        _lib.call("gptoss_moe_gather", _ptr(self.t), _ptr(self.tok), M * k, H, self.f16, _ptr(self.send), S)
         counts = self.indptr[1:] - self.indptr[:-1]
         return self.send[: M * k], counts.view(self.world, self.El)
 
@@ -109,10 +110,10 @@ class CudaBackend:
         _lib.call("gptoss_moe_mlp1", _ptr(self.act), recv_rows, _ptr(self.indptr_local), _ptr(self.tile_ptr),
                   _ptr(self.tile_rows), El, H, I, _ptr(blk.mlp1_weight_blocks), _ptr(blk.mlp1_weight_scales),
                   _ptr(blk.mlp1_bias), ctypes.c_float(blk.swiglu_alpha), ctypes.c_float(blk.swiglu_limit),
-                  _ptr(self.y), _ptr(self.err), S)
+                  self.f16, _ptr(self.y), _ptr(self.err), S)
         _lib.call("gptoss_moe_mlp2", _ptr(self.y), recv_rows, _ptr(self.indptr_local), _ptr(self.tile_ptr),
                   _ptr(self.tile_rows), El, H, I, _ptr(blk.mlp2_weight_blocks), _ptr(blk.mlp2_weight_scales),
-                  _ptr(blk.mlp2_bias), _ptr(self.h2_local), _ptr(self.err), S)
+                  _ptr(blk.mlp2_bias), self.f16, _ptr(self.h2_local), _ptr(self.err), S)
         _lib.call("gptoss_moe_segment_copy", _ptr(self.h2_local), _ptr(self.h2_src), _ptr(recv_counts), self.world, El,
                   H * 4, 1, None, S)
         return self.h2_src[:recv_rows]
@@ -149,6 +150,11 @@ class ExpertParallelMoE:
             raise ValueError("num_experts must equal num_local_experts * world size")
         if blk.expert_offset != self.rank * blk.num_local_experts:
             raise ValueError("rank r must own experts [r*El, (r+1)*El)")
+        if hasattr(blk, "flags") and backend is None:
+            # every rank must run the same GEMM path (the rows travel in its activation type)
+            f = torch.tensor([int(blk.flags)], dtype=torch.int32, device=blk.device)
+            dist.all_reduce(f, op=dist.ReduceOp.MIN, group=group)
+            blk.flags = int(f.item())
         self.backend = backend or CudaBackend(blk, max_tokens, self.world)
         self.last_splits = None
 
@@ -213,11 +219,11 @@ class ExpertParallelMoE:
             _lib.call("gptoss_moe_mlp1", _ptr(b.act), recv_rows, _ptr(b.indptr_local), _ptr(b.tile_ptr),
                       _ptr(b.tile_rows), El, H, I, _ptr(blk.mlp1_weight_blocks), _ptr(blk.mlp1_weight_scales),
                       _ptr(blk.mlp1_bias), ctypes.c_float(blk.swiglu_alpha), ctypes.c_float(blk.swiglu_limit),
-                      _ptr(b.y), _ptr(b.err), S)
+                      b.f16, _ptr(b.y), _ptr(b.err), S)
             ev[5].record()
             _lib.call("gptoss_moe_mlp2", _ptr(b.y), recv_rows, _ptr(b.indptr_local), _ptr(b.tile_ptr),
                       _ptr(b.tile_rows), El, H, I, _ptr(blk.mlp2_weight_blocks), _ptr(blk.mlp2_weight_scales),
-                      _ptr(blk.mlp2_bias), _ptr(b.h2_local), _ptr(b.err), S)
+                      _ptr(blk.mlp2_bias), b.f16, _ptr(b.h2_local), _ptr(b.err), S)
             _lib.call("gptoss_moe_segment_copy", _ptr(b.h2_local), _ptr(b.h2_src), _ptr(recv_counts), b.world, El,
                       H * 4, 1, None, S)
             ev[6].record()

@@ -61,6 +61,8 @@ class MLPBlock:
         self.mlp2_bias = torch.zeros(El, H, dtype=torch.bfloat16, device=dev)
         self._ws = None
         self._ws_tokens = 0
+        self.flags = 0            # GPTOSS_MOE_* bits (set by prepare())
+        self.allow_f16 = True     # let prepare() enable the f16 GEMM path when it is exact
 
     # reference-style parameter names ------------------------------------
     PARAM_NAMES = {
@@ -92,7 +94,20 @@ class MLPBlock:
             if tuple(t.shape) != tuple(dst.shape):
                 raise ValueError(f"{key}: shape {tuple(t.shape)} != {tuple(dst.shape)}")
             dst.copy_(t.to(dst.dtype) if t.dtype != dst.dtype else t)
+        return self.prepare()
+
+    def prepare(self) -> "MLPBlock":
+        """One-time weight check: enables the f16 GEMM path when every E8M0
+        scale code lies in 104..140 (then e2m1 x 2^k is an exact f16)."""
+        w = self.c_weights()
+        w.flags = 0
+        _lib.call("gptoss_moe_weights_prepare", ctypes.byref(w), _stream())
+        self.flags = int(w.flags) if self.allow_f16 else 0
         return self
+
+    @property
+    def f16_path(self) -> bool:
+        return bool(self.flags & _lib.MOE_F16)
 
     def c_weights(self) -> _lib.gptoss_moe_weights:
         w = _lib.gptoss_moe_weights()
@@ -113,6 +128,7 @@ class MLPBlock:
         w.mlp2_blocks = self.mlp2_weight_blocks.data_ptr()
         w.mlp2_scales = self.mlp2_weight_scales.data_ptr()
         w.mlp2_bias = self.mlp2_bias.data_ptr()
+        w.flags = self.flags
         return w
 
     def workspace(self, tokens: int):
@@ -170,6 +186,7 @@ def profile_moe_stages(blk: "MLPBlock", x: torch.Tensor, repeats: int = 3) -> di
     E, El, k, H, I = blk.num_experts, blk.num_local_experts, blk.experts_per_token, blk.hidden_size, blk.intermediate_size
     R = M * k
     dev = x2.device
+    f16 = 1 if blk.f16_path else 0
     i32 = dict(dtype=torch.int32, device=dev)
     t = torch.empty_like(x2)
     logits = torch.empty(M, E, dtype=torch.bfloat16, device=dev)
@@ -196,14 +213,14 @@ def profile_moe_stages(blk: "MLPBlock", x: torch.Tensor, repeats: int = 3) -> di
         _lib.call("gptoss_moe_permute", _ptr(idx), M, k, E, _ptr(indptr), _ptr(tok), _ptr(rev), _ptr(exr),
                   _ptr(tile_ptr), _ptr(tile_rows), _ptr(err), S)
         ev[3].record()
-        _lib.call("gptoss_moe_gather", _ptr(t), _ptr(tok), R, H, _ptr(act), S)
+        _lib.call("gptoss_moe_gather", _ptr(t), _ptr(tok), R, H, f16, _ptr(act), S)
         ev[4].record()
         _lib.call("gptoss_moe_mlp1", _ptr(act), R, _ptr(indptr), _ptr(tile_ptr), _ptr(tile_rows), E, H, I,
                   _ptr(blk.mlp1_weight_blocks), _ptr(blk.mlp1_weight_scales), _ptr(blk.mlp1_bias),
-                  ctypes.c_float(blk.swiglu_alpha), ctypes.c_float(blk.swiglu_limit), _ptr(y), _ptr(err), S)
+                  ctypes.c_float(blk.swiglu_alpha), ctypes.c_float(blk.swiglu_limit), f16, _ptr(y), _ptr(err), S)
         ev[5].record()
         _lib.call("gptoss_moe_mlp2", _ptr(y), R, _ptr(indptr), _ptr(tile_ptr), _ptr(tile_rows), E, H, I,
-                  _ptr(blk.mlp2_weight_blocks), _ptr(blk.mlp2_weight_scales), _ptr(blk.mlp2_bias), _ptr(h2),
+                  _ptr(blk.mlp2_weight_blocks), _ptr(blk.mlp2_weight_scales), _ptr(blk.mlp2_bias), f16, _ptr(h2),
                   _ptr(err), S)
         ev[6].record()
         _lib.call("gptoss_moe_combine", _ptr(h2), _ptr(rev), _ptr(w), _ptr(x2), M, k, H, _ptr(out), S)

@@ -60,7 +60,18 @@ typedef struct gptoss_moe_weights {
   const uint8_t* mlp2_blocks;
   const uint8_t* mlp2_scales;
   const uint16_t* mlp2_bias;
+  uint32_t flags;        /* GPTOSS_MOE_* bits, set by gptoss_moe_weights_prepare */
 } gptoss_moe_weights;
+
+/* flags bit: every E8M0 scale code is in 104..140 and RMSNorm outputs stay in
+ * the f16 range, so the grouped GEMMs may decode the e2m1 weights to f16 with
+ * the hardware converter and run on f16 activations (exact weights either way). */
+#define GPTOSS_MOE_F16 1u
+
+/* One-time weight check (synchronises `stream`): sets or clears GPTOSS_MOE_F16
+ * in w->flags from the scale codes and the norm weight.  Call after loading
+ * weights (the reference loads them once, weights.py:102-122). */
+int gptoss_moe_weights_prepare(gptoss_moe_weights* w, void* stream);
 
 /* Scratch for gptoss_moe_forward (device memory owned by the library). */
 typedef struct gptoss_moe_workspace gptoss_moe_workspace;
@@ -104,24 +115,26 @@ int gptoss_moe_permute(const int32_t* topk_indices, int64_t M, int32_t K, int32_
                        int32_t* token_of_row, int32_t* row_of_pair, int32_t* expert_of_row, int32_t* tile_ptr,
                        int32_t* tile_rows, uint32_t* err, void* stream);
 
-/* nn.op.take(t, token_indices) (model/mlp_optimized.py:150): act[r] = t[token_of_row[r]]. */
-int gptoss_moe_gather(const uint16_t* t, const int32_t* token_of_row, int64_t rows, int32_t H, uint16_t* act,
-                      void* stream);
+/* nn.op.take(t, token_indices) (model/mlp_optimized.py:150): act[r] = t[token_of_row[r]],
+ * converted to f16 when act_f16 (the f16 GEMM path). */
+int gptoss_moe_gather(const uint16_t* t, const int32_t* token_of_row, int64_t rows, int32_t H, int32_t act_f16,
+                      uint16_t* act, void* stream);
 
 /* run_einsum(mlp1) + swiglu (model/mlp.py:238-326, :29-60, :387-390;
  * grouped form mxfp4_moe_mlp1_prefill, model/mlp_optimized.py:214-351).
- * act [act_rows, H] bf16 expert-major; weights of E experts;
- * y [act_rows, I] bf16.  Tolerance (bf16) vs. the reference. */
+ * act [act_rows, H] expert-major (bf16, or f16 when act_f16); weights of E experts;
+ * y [act_rows, I] (same type as act).  Tolerance (bf16) vs. the reference. */
 int gptoss_moe_mlp1(const uint16_t* act, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
                     const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
-                    const uint8_t* scales, const uint16_t* bias, float alpha, float limit, uint16_t* y,
-                    uint32_t* err, void* stream);
+                    const uint8_t* scales, const uint16_t* bias, float alpha, float limit, int32_t act_f16,
+                    uint16_t* y, uint32_t* err, void* stream);
 
 /* run_einsum(mlp2) (model/mlp.py:395; grouped form mxfp4_moe_mlp2_prefill,
- * model/mlp_optimized.py:353-460).  y [rows, I] bf16 -> h2 [rows, H] fp32. */
+ * model/mlp_optimized.py:353-460).  y [rows, I] (bf16, or f16 when act_f16) -> h2 [rows, H] fp32. */
 int gptoss_moe_mlp2(const uint16_t* y, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
                     const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
-                    const uint8_t* scales, const uint16_t* bias, float* h2, uint32_t* err, void* stream);
+                    const uint8_t* scales, const uint16_t* bias, int32_t act_f16, float* h2, uint32_t* err,
+                    void* stream);
 
 /* run_gating + residual (model/mlp.py:328-369, :398-402):
  * out[m] = bf16(x[m] + bf16(sum_r h2[row_of_pair[m,r]] * w[m,r])). */
@@ -132,6 +145,62 @@ int gptoss_moe_combine(const float* h2, const int32_t* row_of_pair, const uint16
  * MXFP4 blocks [rows, G, 16] + scales [rows, G] to bf16 [rows, G*32]. */
 int gptoss_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t rows, int32_t groups,
                          uint16_t* out, void* stream);
+
+/* -------------------------------------------------------------- attention
+ * AttentionBlock (model/attention.py:70-256): head_dim 64, GQA (Hq a multiple
+ * of Hkv), learned per-head sinks, alternating sliding-window / full causal
+ * masks, YaRN RoPE.  Layouts: q [T, Hq, D], k / v [T, Hkv, D] bf16; lse
+ * [T, Hq] fp32 in base 2 of the scaled scores (q.k * sm_scale * log2 e),
+ * the convention of the reference's TVM kernels (attention.py:237-240). */
+
+/* YaRN inverse frequencies inv_freq [D/2] and the attention concentration
+ * (rope_freq_yarn, model/attention.py:15-67, :148-153), computed on the host
+ * in fp32 like the reference.  Host memory in and out. */
+int gptoss_yarn_inv_freq(int32_t D, float theta, float factor, float beta_fast, float beta_slow,
+                         int32_t original_max_position, float* inv_freq, float* concentration);
+
+/* AttentionBlock._rope (model/attention.py:96-169): x [S, heads, D] -> out,
+ * rotate-half pairs (d, d + D/2), positions [S] int32 (device), inv_freq host. */
+int gptoss_rope_yarn(const uint16_t* x, const int32_t* positions, int64_t S, int32_t heads, int32_t D,
+                     const float* inv_freq, float concentration, uint16_t* out, void* stream);
+
+/* qkv split + RoPE on q and k + append_mha_kv (model/attention.py:206-214):
+ * qkv [S, (Hq + 2 Hkv) D] -> q_out [S, Hq, D]; k (rotated) and v written to
+ * row slots[s] of k_cache / v_cache [num_slots, Hkv, D] (slots NULL: row s). */
+int gptoss_qkv_rope_append(const uint16_t* qkv, const int32_t* positions, const int32_t* slots, int64_t S,
+                           int32_t Hq, int32_t Hkv, int32_t D, const float* inv_freq, float concentration,
+                           uint16_t* q_out, uint16_t* k_cache, uint16_t* v_cache, void* stream);
+
+/* paged_kv_cache.self_attention + the sink rescale (model/attention.py:218-247):
+ * Sq queries that are the last Sq of Skv keys, causal, window W > 0 keeps
+ * keys >= pos - W + 1 (tvm_fix.patch:35-47), W <= 0 = full.  sinks [Hq]
+ * bf16 or NULL (NULL: no rescale, o is the plain attention output).
+ * o [Sq, Hq, D] bf16; lse [Sq, Hq] fp32 or NULL. */
+int gptoss_attn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* sinks, int64_t Sq,
+                        int64_t Skv, int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale, uint16_t* o,
+                        float* lse, void* stream);
+
+/* paged_kv_cache.cross_attention for one new token per sequence
+ * (model/attention.py:221-224) + sink rescale: q [B, Hq, D]; caches
+ * [B, max_len, Hkv, D] with kv_len[b] valid rows (device), the query being
+ * the token at kv_len[b] - 1; window as above (decode on windowed layers
+ * reads the last W keys, tvm_fix.patch:194-281).  scratch: device memory of
+ * gptoss_attn_decode_scratch_bytes() bytes.  o [B, Hq, D]; lse [B, Hq]. */
+int64_t gptoss_attn_decode_scratch_bytes(int64_t B, int32_t Hq, int64_t max_len, int32_t window);
+int gptoss_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* kv_len,
+                       int64_t B, int64_t max_len, int32_t Hq, int32_t Hkv, int32_t D, int32_t window,
+                       float sm_scale, const uint16_t* sinks, float* scratch, int64_t scratch_bytes, uint16_t* o,
+                       float* lse, void* stream);
+
+/* merge_attn_output_inplace (model/attention.py:231-233): two partial
+ * attention states over disjoint keys -> one (o bf16 [T, Hq, D], lse). */
+int gptoss_attn_merge(const uint16_t* o1, const float* lse1, const uint16_t* o2, const float* lse2, int64_t T,
+                      int32_t Hq, int32_t D, uint16_t* o, float* lse, void* stream);
+
+/* Sink rescale alone (model/attention.py:240-247), in place:
+ * o *= bf16(sigmoid(ln2 * lse - sink[h])). */
+int gptoss_attn_sink_rescale(uint16_t* o, const float* lse, const uint16_t* sinks, int64_t T, int32_t Hq, int32_t D,
+                             void* stream);
 
 /* MLPBlock.forward like gptoss_moe_forward, but allocating nothing: no
  * cudaMalloc, no cudaFree, no workspace.  It has no counterpart in the

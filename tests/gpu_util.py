@@ -55,13 +55,23 @@ class MoEPieces:
     """Runs the MoE block step by step through the C ABI (device buffers
     allocated here with torch) so each stage can be compared with the oracle."""
 
-    def __init__(self, p: dict, k: int = 4):
+    def __init__(self, p: dict, k: int = 4, f16: bool | None = None):
+        """f16: GEMM path (None = what gptoss_moe_weights_prepare allows)."""
         self.p = {kk: dev(v) for kk, v in p.items()}
         self.E = p["gate_weight"].shape[0]
         self.H = p["gate_weight"].shape[1]
         self.I = p["mlp2_weight_blocks"].shape[2] * 32
         self.k = k
         self.err = torch.zeros(4, dtype=torch.int32, device="cuda")
+        w = _lib.gptoss_moe_weights()
+        w.num_experts = w.num_local_experts = self.E
+        w.hidden, w.intermediate, w.top_k = self.H, self.I, k
+        w.norm_weight = self.p["norm_weight"].data_ptr()
+        w.mlp1_scales = self.p["mlp1_weight_scales"].data_ptr()
+        w.mlp2_scales = self.p["mlp2_weight_scales"].data_ptr()
+        call("gptoss_moe_weights_prepare", ctypes.byref(w), S())
+        allowed = bool(w.flags & _lib.MOE_F16)
+        self.f16 = allowed if f16 is None else (f16 and allowed)
 
     def run(self, x_bits: np.ndarray, routing=None):
         """routing: optional (weights bf16 bits [M,k], indices int32 [M,k])
@@ -81,8 +91,10 @@ class MoEPieces:
         tok = torch.empty(R, **i32)
         rev = torch.empty(R, **i32)
         exp_ = torch.empty(R, **i32)
-        act = torch.empty(R, H, dtype=torch.bfloat16, device="cuda")
-        y = torch.empty(R, I, dtype=torch.bfloat16, device="cuda")
+        adt = torch.float16 if self.f16 else torch.bfloat16
+        act = torch.empty(R, H, dtype=adt, device="cuda")
+        y = torch.empty(R, I, dtype=adt, device="cuda")
+        f16 = 1 if self.f16 else 0
         h2 = torch.empty(R, H, dtype=torch.float32, device="cuda")
         out = torch.empty_like(x)
         p = self.p
@@ -94,15 +106,16 @@ class MoEPieces:
             idx.copy_(dev(routing[1]))
         call("gptoss_moe_permute", P(idx), M, k, E, P(indptr), P(tok), P(rev), P(exp_), P(tile_ptr), P(tile_rows),
              P(self.err), S())
-        call("gptoss_moe_gather", P(t), P(tok), R, H, P(act), S())
+        call("gptoss_moe_gather", P(t), P(tok), R, H, f16, P(act), S())
         call("gptoss_moe_mlp1", P(act), R, P(indptr), P(tile_ptr), P(tile_rows), E, H, I, P(p["mlp1_weight_blocks"]),
-             P(p["mlp1_weight_scales"]), P(p["mlp1_bias"]), ctypes.c_float(1.702), ctypes.c_float(7.0), P(y),
+             P(p["mlp1_weight_scales"]), P(p["mlp1_bias"]), ctypes.c_float(1.702), ctypes.c_float(7.0), f16, P(y),
              P(self.err), S())
         call("gptoss_moe_mlp2", P(y), R, P(indptr), P(tile_ptr), P(tile_rows), E, H, I, P(p["mlp2_weight_blocks"]),
-             P(p["mlp2_weight_scales"]), P(p["mlp2_bias"]), P(h2), P(self.err), S())
+             P(p["mlp2_weight_scales"]), P(p["mlp2_bias"]), f16, P(h2), P(self.err), S())
         call("gptoss_moe_combine", P(h2), P(rev), P(w), P(x), M, k, H, P(out), S())
         torch.cuda.synchronize()
         assert int(self.err.cpu()[0]) == 0, f"device error word {int(self.err.cpu()[0]):#x}"
+        y_f32 = y.float().cpu().numpy()
         return dict(t=host(t), logits=host(logits), weights=host(w), indices=host(idx), indptr=host(indptr),
-                    token_of_row=host(tok), row_of_pair=host(rev), expert_of_row=host(exp_), y=host(y), h2=host(h2),
+                    token_of_row=host(tok), row_of_pair=host(rev), expert_of_row=host(exp_), y=y_f32, h2=host(h2),
                     out=host(out), tile_ptr=host(tile_ptr), tile_rows=host(tile_rows))

@@ -44,7 +44,7 @@ def _check_experts(oracle, r, ref, rows=None):
     M, k = r["indices"].shape
     rows = np.arange(M) if rows is None else rows
     rev = r["row_of_pair"].reshape(M, k)
-    y_gpu = G.f32(r["y"])[rev[rows].ravel()]
+    y_gpu = r["y"][rev[rows].ravel()]
     y_ref = ref["y"][rows].reshape(-1, ref["y"].shape[-1])
     G.tol_check(y_gpu, y_ref, what="mlp1+swiglu")
     h2_gpu = r["h2"][rev[rows].ravel()]
@@ -54,8 +54,9 @@ def _check_experts(oracle, r, ref, rows=None):
     G.tol_check(G.f32(r["out"][rows]), G.f32(ref["out"][rows]), what="block output")
 
 
+@pytest.mark.parametrize("f16", [True, False], ids=["f16-path", "bf16-path"])
 @pytest.mark.parametrize("M", [1, 5, 37, 300])
-def test_moe_block_e8(oracle, params_e8, M):
+def test_moe_block_e8(oracle, params_e8, M, f16):
     x = synth().activations(M, seed=100 + M)
     rows = None if M <= 40 else np.sort(np.random.default_rng(M).choice(M, 24, replace=False))
     mask = None
@@ -64,7 +65,9 @@ def test_moe_block_e8(oracle, params_e8, M):
         mask[rows] = 1
     ref = oracle.moe_forward(x, params_e8, rows_mask=mask, return_all=True)
     ref["x"] = x
-    r = G.MoEPieces(params_e8).run(x)
+    pieces = G.MoEPieces(params_e8, f16=f16)
+    assert pieces.f16 == f16, "the synthetic weights (scale codes 118..124) must allow the f16 path"
+    r = pieces.run(x)
     _check_routing(r, ref, M, 8)
     _check_permutation(oracle, r, 8)
     _check_experts(oracle, r, ref, rows)
@@ -147,14 +150,15 @@ def test_config3_scale_routing_bit_exact_and_sampled_experts(oracle):
     _check_experts(oracle, r, ref, rows)
 
 
-def test_forced_routing_multi_tile_and_empty_experts(oracle, params_e8):
+@pytest.mark.parametrize("f16", [True, False], ids=["f16-path", "bf16-path"])
+def test_forced_routing_multi_tile_and_empty_experts(oracle, params_e8, f16):
     """Every token routed to experts 0..3 (600 rows each -> 3 token tiles per
     expert, 4 empty experts)."""
     M = 600
     x = synth().activations(M, seed=9)
     idx = np.tile(np.array([[2, 0, 3, 1]], np.int32), (M, 1))
     wts = synth().bf16_bits(np.tile(np.array([[0.4, 0.3, 0.2, 0.1]], np.float32), (M, 1)))
-    r = G.MoEPieces(params_e8).run(x, routing=(wts, idx))
+    r = G.MoEPieces(params_e8, f16=f16).run(x, routing=(wts, idx))
     indptr, tok, rev, _ = oracle.moe_permute(idx, 8)
     np.testing.assert_array_equal(r["indptr"], indptr)
     np.testing.assert_array_equal(r["tile_ptr"], [0, 3, 6, 9, 12, 12, 12, 12, 12])
@@ -166,10 +170,23 @@ def test_forced_routing_multi_tile_and_empty_experts(oracle, params_e8):
     h2 = oracle.moe_einsum(y, idx[rows], params_e8["mlp2_weight_blocks"], params_e8["mlp2_weight_scales"],
                            params_e8["mlp2_bias"])
     revm = r["row_of_pair"].reshape(M, 4)
-    G.tol_check(G.f32(r["y"])[revm[rows].ravel()], y.reshape(-1, 2880), what="forced mlp1")
+    G.tol_check(r["y"][revm[rows].ravel()], y.reshape(-1, 2880), what="forced mlp1")
     G.tol_check(r["h2"][revm[rows].ravel()], h2.reshape(-1, 2880), what="forced mlp2")
     _, out = oracle.gating_residual(h2, wts[rows], x[rows])
     G.tol_check(G.f32(r["out"][rows]), G.f32(out), what="forced output")
+
+
+def test_f16_path_disabled_for_out_of_range_scales():
+    """A scale code outside 104..140 makes gptoss_moe_weights_prepare clear the
+    f16 flag; the exact bf16 path then matches the oracle."""
+    p = dict(synth().moe_params(8, seed=10))
+    p["mlp2_weight_scales"] = p["mlp2_weight_scales"].copy()
+    p["mlp2_weight_scales"][3, 5, 7] = 141
+    assert not G.MoEPieces(p).f16
+    p["mlp2_weight_scales"][3, 5, 7] = 103
+    assert not G.MoEPieces(p).f16
+    p["mlp2_weight_scales"][3, 5, 7] = 104
+    assert G.MoEPieces(p).f16
 
 
 def test_topk_ties_golden():
