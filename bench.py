@@ -53,57 +53,52 @@ def measured_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """Samples SM clocks and clock-event (throttle) reasons through NVML while
+    the timed region runs (read-only queries)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, gpu_index: int, period_s: float = 0.02):
+        self.gpu, self.period = gpu_index, period_s
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
         except Exception:
-            self.proc = None
+            self._nv = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv, h = self._nv, self._h
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                bits = get_reasons(h)
+                for bit, name in self.REASONS.items():
+                    if bits & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self.period)
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self._nv is not None:
+            self._t.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
 
 
 def dist_env():
@@ -278,27 +273,55 @@ def cpu_baseline(args):
 
 
 def run_reference(args):
+    """The reference's own CPU implementation of the path, on the host cores:
+    model/mlp.py compiled by TVM (oracle/_ref, one process per core) when it
+    was built, else the C restatement of the oracle (OpenMP)."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    cb = importlib.import_module("oracle.cpu_baseline")
-    vals = []
-    info = None
-    for i in range(args.warmup + args.steps):
-        info = cb.measure(tokens=args.cpu_tokens, num_experts=NUM_EXPERTS)
-        if i >= args.warmup:
-            vals.append(info["value"])
-    value = statistics.mean(vals)
-    ms = TOKENS / value * 1e3
+    rr = importlib.import_module("oracle.ref_runner")
+    if rr.available(NUM_EXPERTS):
+        pool = rr.RefPool(NUM_EXPERTS)
+        kind, cores = "reference", pool.procs
+        sample = (f"{pool.procs} tokens per step (1 per process) of the {NUM_EXPERTS}-expert MoE block, "
+                  f"the reference's model/mlp.py compiled by TVM (C target), one process per core")
+
+        def step():
+            return pool.step(1)
+    else:
+        import oracle
+        oracle.build()
+        synth = importlib.import_module("gpt-oss-tvm_b200.synthetic")
+        p = synth.moe_params(NUM_EXPERTS, seed=0)
+        cores = len(os.sched_getaffinity(0))
+        kind, pool = "port", None
+        sample = f"{cores} tokens per step of the {NUM_EXPERTS}-expert MoE block, C restatement (OpenMP)"
+
+        def step():
+            x = synth.activations(cores, seed=1)
+            t0 = time.perf_counter()
+            oracle.moe_forward(x, p)
+            return time.perf_counter() - t0, cores
+    for _ in range(args.warmup):
+        step()
+    tot_t, tot_n = 0.0, 0
+    for _ in range(args.steps):
+        dt, n = step()
+        tot_t += dt
+        tot_n += n
+    if pool is not None:
+        pool.close()
+    value = tot_n / tot_t
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 accumulate over bf16 / MXFP4 (reference CPU path)",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(TOKENS / value * 1e3, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32 accumulate over bf16 activations and MXFP4 weights (reference CPU path)",
         "data": "synthetic (seeded; BASELINE configs[3] distributions)",
         "config": {"workload": "gpt-oss-120b MoE layer prefill (configs[3])", "tokens_per_gpu": TOKENS,
                    "num_experts": NUM_EXPERTS, "top_k": TOP_K, "hidden": HIDDEN, "intermediate": INTER,
                    "parallelism": "host cores"},
-        "cpu_baseline": {k: info[k] for k in ("kind", "cores", "sample", "unit")} | {"value": round(value, 3)},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -308,7 +331,7 @@ def main():
     global TOKENS
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=32, help="token sample of the CPU baseline")

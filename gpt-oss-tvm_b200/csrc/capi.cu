@@ -174,7 +174,7 @@ int gptoss_moe_weights_prepare(gptoss_moe_weights* w, void* stream) {
 
 int gptoss_moe_combine(const float* h2, const int32_t* row_of_pair, const uint16_t* topk_weights,
                        const uint16_t* x, int64_t M, int32_t K, int32_t H, uint16_t* out, void* stream) {
-  if (M < 0 || K < 1 || H <= 0) return fail(-1, "gptoss_moe_combine: bad shape");
+  if (M < 0 || K < 1 || K > 8 || H <= 0 || H % 4) return fail(-1, "gptoss_moe_combine: bad shape");
   return check_launch(launch_combine(h2, row_of_pair, topk_weights, x, M, K, H, out, GPTOSS_STREAM(stream)),
                       "combine");
 }

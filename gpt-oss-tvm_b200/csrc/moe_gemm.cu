@@ -22,23 +22,24 @@
 //     token rows, K = 16 per instruction) accumulates fp32 in TMEM.
 //   * Nibbles are streamed by TMA (32-byte swizzle) through an 8-deep ring;
 //     each tile's 128 x K/32 scale bytes arrive with one bulk copy.
-// Warp roles: 0-7 dequant (two warpgroups, one 32-element MXFP4 group of each
-// 64-wide K chunk each), 8-11 epilogue (double-buffered TMEM accumulator, so
-// the epilogue of tile i overlaps the main loop of tile i+1), 12 activation
-// TMA, 13 MMA issuer (also owns TMEM), 14 weight TMA.
+// Warp roles: 0-15 dequant (four warpgroups: even / odd K chunks x the two
+// 32-element MXFP4 groups of a 64-wide chunk), 16-19 epilogue (double-buffered
+// TMEM accumulator, so the epilogue of tile i overlaps the main loop of tile
+// i+1), 20 activation TMA, 21 MMA issuer (also owns TMEM), 22 weight TMA.
 #include "common.cuh"
 #include "launch.h"
 
 namespace gptoss {
 
-constexpr int kGemmThreads = 480;
+constexpr int kGemmThreads = 736;
 constexpr int kBM = 128;            // weight rows per tile (MMA M)
 constexpr int kMaxBN = kMoeTileMaxRows;  // token rows per tile (MMA N, max)
-constexpr int kBoxRows = 64;        // activation TMA box height
+constexpr int kBoxRows = 16;        // activation TMA box height (up to 13 boxes per stage)
 constexpr int kBK = 64;             // K per pipeline chunk (one 128 B swizzle row of bf16)
-constexpr int kStages = 3;          // activation + TMEM A stages
+constexpr int kStages = 3;          // TMEM A stages (dequantised weights)
+constexpr int kBStages = 6;         // shared-memory activation stages
 constexpr int kWStages = 8;         // nibble ring depth
-constexpr int kActStageBytes = 256 * kBK * 2;      // 32 KB (room for 4 boxes of 64 rows)
+constexpr int kActStageBytes = kMaxBN * kBK * 2;   // 26 KB (208 rows of 128 B)
 constexpr int kWStageBytes = kBM * (kBK / 2);      // 4 KB (128 rows x 32 nibble bytes)
 constexpr int kMaxGroups = 96;                     // K/32 upper bound (K <= 3072)
 constexpr int kScaleBytes = kBM * kMaxGroups;      // per-tile scale buffer (row stride = G)
@@ -46,9 +47,10 @@ constexpr int kAccCols = kMaxBN;                   // columns of one accumulator
 constexpr int kTmemCols = 512;
 constexpr int kAColBase = 2 * kAccCols;            // A stage s at columns 416 + 32 s
 static_assert(kAColBase + kStages * 32 <= kTmemCols, "TMEM budget");
-constexpr int kDequantWarps = 8;
-constexpr int kEpiWarp0 = 8;
-constexpr int kActWarp = 12, kMmaWarp = 13, kWWarp = 14;
+constexpr int kDequantWarps = 16;  // 4 warpgroups: (chunk parity, MXFP4 group of the chunk)
+constexpr int kDequantPerChunk = 8; // warps that fill one chunk's A stage
+constexpr int kEpiWarp0 = 16;
+constexpr int kActWarp = 20, kMmaWarp = 21, kWWarp = 22;
 
 struct GemmParams {
   const uint8_t* scales;     // [E, N, G]
@@ -68,10 +70,10 @@ struct GemmParams {
 struct GemmSmem {
   // offsets from the 1024-aligned base
   static constexpr int kAct = 0;
-  static constexpr int kW = kAct + kStages * kActStageBytes;
+  static constexpr int kW = kAct + kBStages * kActStageBytes;
   static constexpr int kScale = kW + kWStages * kWStageBytes;
   static constexpr int kBar = kScale + 2 * kScaleBytes;
-  static constexpr int kNumBars = 2 * kStages + 2 * kWStages + 4 + 4;
+  static constexpr int kNumBars = 2 * kStages + 2 * kBStages + 2 * kWStages + 4 + 4;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kTotal = kMisc + 64;
   static constexpr int kAlloc = kTotal + 1024;  // slack for manual 1024 B alignment
@@ -149,12 +151,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* w_s = smem + GemmSmem::kW;
   uint8_t* sc_s = smem + GemmSmem::kScale;
   uint64_t* bars = (uint64_t*)(smem + GemmSmem::kBar);
-  uint64_t* full_bar = bars;                      // [kStages] act TMA tx + 8 dequant warps
+  uint64_t* full_bar = bars;                      // [kStages] TMEM A stage: 8 dequant warps
   uint64_t* empty_bar = full_bar + kStages;       // [kStages] MMA commit
-  uint64_t* wfull_bar = empty_bar + kStages;      // [kWStages] nibble TMA tx
+  uint64_t* bfull_bar = empty_bar + kStages;      // [kBStages] activation TMA tx
+  uint64_t* bempty_bar = bfull_bar + kBStages;    // [kBStages] MMA commit
+  uint64_t* wfull_bar = bempty_bar + kBStages;    // [kWStages] nibble TMA tx
   uint64_t* wempty_bar = wfull_bar + kWStages;    // [kWStages] 8 dequant warps
   uint64_t* scfull_bar = wempty_bar + kWStages;   // [2] scale bulk copy tx
-  uint64_t* scempty_bar = scfull_bar + 2;         // [2] 8 dequant warps
+  uint64_t* scempty_bar = scfull_bar + 2;         // [2] all 16 dequant warps
   uint64_t* accfull_bar = scempty_bar + 2;        // [2] MMA commit
   uint64_t* accempty_bar = accfull_bar + 2;       // [2] 4 epilogue warps
   uint32_t* misc = (uint32_t*)(smem + GemmSmem::kMisc);
@@ -170,12 +174,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], 1 + kDequantWarps);
+      mbar_init(&full_bar[s], kDequantPerChunk);
       mbar_init(&empty_bar[s], 1);
+    }
+    for (int s = 0; s < kBStages; ++s) {
+      mbar_init(&bfull_bar[s], 1);
+      mbar_init(&bempty_bar[s], 1);
     }
     for (int s = 0; s < kWStages; ++s) {
       mbar_init(&wfull_bar[s], 1);
-      mbar_init(&wempty_bar[s], kDequantWarps);
+      mbar_init(&wempty_bar[s], kDequantPerChunk);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&scfull_bar[s], 1);
@@ -208,12 +216,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (!decode_tile(p, t, ftiles, ti)) continue;
         const int32_t nbox = (ti.nrows + kBoxRows - 1) / kBoxRows;
         for (int32_t c = 0; c < nchunks; ++c, ++it) {
-          const uint32_t s = it % kStages, ph = (it / kStages) & 1;
-          if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
-          mbar_arrive_expect_tx(&full_bar[s], (uint32_t)nbox * kBoxRows * 128);
+          const uint32_t s = it % kBStages, ph = (it / kBStages) & 1;
+          if (!mbar_wait(&bempty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
+          mbar_arrive_expect_tx(&bfull_bar[s], (uint32_t)nbox * kBoxRows * 128);
           for (int32_t b = 0; b < nbox; ++b)
             tma_load_2d(act_s + s * kActStageBytes + b * kBoxRows * 128, &tmap_act, c * kBK, ti.row0 + b * kBoxRows,
-                        &full_bar[s]);
+                        &bfull_bar[s]);
         }
       }
     }
@@ -263,15 +271,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         bool ok = true;
         for (int32_t c = 0; c < nchunks; ++c, ++it) {
           const uint32_t s = it % kStages, ph = (it / kStages) & 1;
+          const uint32_t sb = it % kBStages, phb = (it / kBStages) & 1;
+          if (!mbar_wait(&bfull_bar[sb], phb, p.err, kErrTimeoutFull)) { ok = false; break; }
           if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t b_base = smem_u32(act_s + s * kActStageBytes);
+          const uint32_t b_base = smem_u32(act_s + sb * kActStageBytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             tc_mma_ts(d_tmem, tmem_base + kAColBase + s * 32 + kk * 8, make_sdesc_sw128(b_base + kk * 32), idesc,
                       (c > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(&empty_bar[s]);
+          tc_commit(&bempty_bar[sb]);
         }
         if (!ok) { *abort_s = 1; break; }
         tc_commit(&accfull_bar[ab]);
@@ -280,7 +291,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp < kDequantWarps) {
     // --------------------------------------------- dequant: weights -> TMEM
-    const int wg = warp >> 2;                   // which MXFP4 group of the chunk
+    const int wg = (warp >> 2) & 1;             // which MXFP4 group of the chunk
+    const int parity = warp >> 3;               // even or odd chunks
     const int row = (warp & 3) * 32 + lane;     // weight row within the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     uint32_t it = 0, wit = 0, tl = 0;
@@ -294,9 +306,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       bool ok = mbar_wait(&scfull_bar[sb], sph, p.err, kErrTimeoutFull);
       const uint8_t* srow = sc_s + sb * kScaleBytes + row * G + wg;
       const uint32_t nib_off = (uint32_t)(wg ^ ((row >> 2) & 1)) << 4;  // 32-byte swizzle
-      for (int32_t c = 0; c < nchunks && ok; ++c, ++it, ++wit) {
-        const uint32_t ws = wit % kWStages, wph = (wit / kWStages) & 1;
-        const uint32_t s = it % kStages, ph = (it / kStages) & 1;
+      for (int32_t c = parity; c < nchunks && ok; c += 2) {
+        const uint32_t witc = wit + (uint32_t)c, itc = it + (uint32_t)c;
+        const uint32_t ws = witc % kWStages, wph = (witc / kWStages) & 1;
+        const uint32_t s = itc % kStages, ph = (itc / kStages) & 1;
         ok = mbar_wait(&wfull_bar[ws], wph, p.err, kErrTimeoutFull);
         if (!ok) break;
         const uint4 nb = *(const uint4*)(w_s + ws * kWStageBytes + row * 32 + nib_off);
@@ -333,6 +346,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&full_bar[s]);
       }
+      it += (uint32_t)nchunks;
+      wit += (uint32_t)nchunks;
       __syncwarp();
       if (lane == 0) mbar_arrive(&scempty_bar[sb]);
       if (!ok) { *abort_s = 1; break; }

@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
   if (ok && threadIdx.x < nrows) {
     const uint4* row = (const uint4*)(rowbuf + (size_t)threadIdx.x * pitch);
     float ss = 0.0f;
+#pragma unroll 4
     for (int32_t k8 = 0; k8 < H / 8; ++k8) {
       const uint4 v = row[k8];
       const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
@@ -86,7 +87,7 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
 // fp32, as in the reference), followed by the rounding to bf16.  Each
 // thread owns a 4-token x 8-expert register tile of independent serial
 // chains; two chains share one packed f32x2 FMA.
-constexpr int kRTT = 4;   // tokens per thread
+constexpr int kRTT = 2;   // tokens per thread
 constexpr int kRTE = 8;   // experts per thread
 constexpr int kRKT = 32;  // k per shared-memory stage (multiple of 8)
 
@@ -113,7 +114,7 @@ __device__ __forceinline__ unsigned long long round_pair_bf16(unsigned long long
   }
 }
 
-template <int kRound>
+template <int kRound, int kMaxTQ, int kMaxWQ>
 __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict__ t, const uint16_t* __restrict__ W,
                                                       const uint16_t* __restrict__ b, int64_t M, int32_t E, int32_t H,
                                                       int32_t block_experts, uint16_t* __restrict__ logits) {
@@ -127,7 +128,6 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
   const int64_t tok0 = (int64_t)blockIdx.x * btok;
   const int32_t e0 = blockIdx.y * block_experts;
   constexpr int kParts = kRKT / 8;                  // 16-byte pieces per row per stage
-  constexpr int kMaxTQ = 16, kMaxWQ = 4;
   const int ntq = (btok * kParts + 127) / 128, nwq = (block_experts * kParts + 127) / 128;
   uint4 tq[kMaxTQ], wq[kMaxWQ];
   auto load_stage = [&](int32_t k0) {
@@ -194,9 +194,8 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
     if (k0 + kRKT < H) load_stage(k0 + kRKT);  // next stage's loads overlap this stage's chains
     const int32_t kn = min(kRKT, H - k0);
     for (int32_t kk = 0; kk < kn; ++kk) {
-      const ulonglong2* tp = (const ulonglong2*)(ts + (kk * btok + tg * kRTT) * 2);
-      const ulonglong2 t01 = tp[0], t23 = tp[1];
-      const unsigned long long tv[4] = {t01.x, t01.y, t23.x, t23.y};
+      const ulonglong2 t01 = *(const ulonglong2*)(ts + (kk * btok + tg * kRTT) * 2);
+      const unsigned long long tv[2] = {t01.x, t01.y};
       const ulonglong2* wp = (const ulonglong2*)(ws + kk * block_experts + eg * kRTE);
       const ulonglong2 w01 = wp[0], w23 = wp[1];
       const unsigned long long wv[4] = {w01.x, w01.y, w23.x, w23.y};
@@ -394,21 +393,38 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ t, const int32_t
 // ------------------------------------------------------------ combine --
 // out[m, c] = bf16(float(x[m,c]) + float(bf16(sum_r h2[row(m,r), c] * w[m,r])))
 // with the serial fp32 sum over r of run_gating (model/mlp.py:328-369) and
-// the residual of model/mlp.py:399-402.
-__global__ void combine_kernel(const float* __restrict__ h2, const int32_t* __restrict__ row_of_pair,
-                               const uint16_t* __restrict__ w, const uint16_t* __restrict__ x, int64_t M, int32_t K,
-                               int32_t H, uint16_t* __restrict__ out) {
-  const int32_t cblocks = (H + blockDim.x - 1) / blockDim.x;
-  const int64_t m = blockIdx.x / cblocks;
-  const int32_t c = (int32_t)(blockIdx.x % cblocks) * blockDim.x + threadIdx.x;
-  if (m >= M || c >= H) return;
-  float acc = 0.0f;
+// the residual of model/mlp.py:399-402.  One block per token, 4 columns per
+// thread (16-byte loads of the fp32 expert rows).
+__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ h2, const int32_t* __restrict__ row_of_pair,
+                                                      const uint16_t* __restrict__ w, const uint16_t* __restrict__ x,
+                                                      int64_t M, int32_t K, int32_t H, uint16_t* __restrict__ out) {
+  const int64_t m = blockIdx.x;
+  if (m >= M) return;
+  const float* rows[8];
+  float wr[8];
   for (int32_t r = 0; r < K; ++r) {
-    const int32_t row = row_of_pair[m * K + r];
-    acc = __fadd_rn(acc, __fmul_rn(h2[(int64_t)row * H + c], bf16_bits_to_f32(w[m * K + r])));
+    rows[r] = h2 + (int64_t)__ldg(row_of_pair + m * K + r) * H;
+    wr[r] = bf16_bits_to_f32(__ldg(w + m * K + r));
   }
-  const float o = round_bf16(acc);
-  out[m * H + c] = f32_to_bf16_bits(__fadd_rn(bf16_bits_to_f32(x[m * H + c]), o));
+  for (int32_t c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int32_t r = 0; r < K; ++r) {
+      const float4 v = __ldg((const float4*)rows[r] + c4);
+      acc[0] = __fadd_rn(acc[0], __fmul_rn(v.x, wr[r]));
+      acc[1] = __fadd_rn(acc[1], __fmul_rn(v.y, wr[r]));
+      acc[2] = __fadd_rn(acc[2], __fmul_rn(v.z, wr[r]));
+      acc[3] = __fadd_rn(acc[3], __fmul_rn(v.w, wr[r]));
+    }
+    const uint2 xv = __ldg((const uint2*)(x + m * H) + c4);
+    const float x0 = __uint_as_float(xv.x << 16), x1 = __uint_as_float(xv.x & 0xFFFF0000u);
+    const float x2 = __uint_as_float(xv.y << 16), x3 = __uint_as_float(xv.y & 0xFFFF0000u);
+    uint2 o;
+    o.x = (uint32_t)f32_to_bf16_bits(__fadd_rn(x0, round_bf16(acc[0]))) |
+          ((uint32_t)f32_to_bf16_bits(__fadd_rn(x1, round_bf16(acc[1]))) << 16);
+    o.y = (uint32_t)f32_to_bf16_bits(__fadd_rn(x2, round_bf16(acc[2]))) |
+          ((uint32_t)f32_to_bf16_bits(__fadd_rn(x3, round_bf16(acc[3]))) << 16);
+    ((uint2*)(out + m * H))[c4] = o;
+  }
 }
 
 // ------------------------------------------------------- MXFP4 decode --
@@ -533,6 +549,32 @@ int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, f
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+template <int kRound, int kTQ, int kWQ>
+static void launch_router_variant(dim3 grid, size_t smem, cudaStream_t s, const uint16_t* t, const uint16_t* W,
+                                  const uint16_t* b, int64_t M, int32_t E, int32_t H, int32_t be, uint16_t* logits) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(router_kernel<kRound, kTQ, kWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr = true;
+  }
+  router_kernel<kRound, kTQ, kWQ><<<grid, 128, smem, s>>>(t, W, b, M, E, H, be, logits);
+}
+
+template <int kRound>
+static int launch_router_round(int egroups, dim3 grid, size_t smem, cudaStream_t s, const uint16_t* t,
+                               const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H, int32_t be,
+                               uint16_t* logits) {
+  // prefetch registers per thread: token tile (btok rows x 4 pieces) and expert tile (be rows x 4 pieces)
+  switch (egroups) {
+    case 8: launch_router_variant<kRound, 1, 2>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
+    case 4: launch_router_variant<kRound, 2, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
+    case 2: launch_router_variant<kRound, 4, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
+    case 1: launch_router_variant<kRound, 8, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
+    default: return -12;
+  }
+  return 0;
+}
+
 int launch_router(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H,
                   uint16_t* logits, cudaStream_t s) {
   if (M <= 0) return 0;
@@ -550,16 +592,11 @@ int launch_router(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64
     const char* env = getenv("GPTOSS_ROUTER_ROUND");
     round_mode = env ? atoi(env) : 0;
   }
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(router_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(router_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    cudaFuncSetAttribute(router_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
-  if (round_mode == 1) router_kernel<1><<<grid, 128, smem, s>>>(t, W, b, M, E, H, block_experts, logits);
-  else if (round_mode == 2) router_kernel<2><<<grid, 128, smem, s>>>(t, W, b, M, E, H, block_experts, logits);
-  else router_kernel<0><<<grid, 128, smem, s>>>(t, W, b, M, E, H, block_experts, logits);
+  int rc;
+  if (round_mode == 1) rc = launch_router_round<1>(egroups, grid, smem, s, t, W, b, M, E, H, block_experts, logits);
+  else if (round_mode == 2) rc = launch_router_round<2>(egroups, grid, smem, s, t, W, b, M, E, H, block_experts, logits);
+  else rc = launch_router_round<0>(egroups, grid, smem, s, t, W, b, M, E, H, block_experts, logits);
+  if (rc) return rc;
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
@@ -593,7 +630,8 @@ int launch_gather(const uint16_t* t, const int32_t* token_of_row, int64_t rows, 
 int launch_combine(const float* h2, const int32_t* row_of_pair, const uint16_t* w, const uint16_t* x, int64_t M,
                    int32_t K, int32_t H, uint16_t* out, cudaStream_t s) {
   if (M <= 0) return 0;
-  const int64_t blocks = (int64_t)((H + 255) / 256) * M;
+  if (H % 4 || K > 8) return -12;
+  const int64_t blocks = M;
   combine_kernel<<<(unsigned)blocks, 256, 0, s>>>(h2, row_of_pair, w, x, M, K, H, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
