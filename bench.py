@@ -256,6 +256,11 @@ def run_b200(args):
             "stages_ms": {k: round(v, 4) for k, v in prof.items() if k.endswith("_ms")},
             "clocks": sampler.summary(),
         }
+        if args.decode and world == 1:
+            line["decode"] = {
+                "gpt-oss-20b (configs[0]) 1 token": decode_bench(dev, 32, 1, 20, peaks),
+                "gpt-oss-120b batched decode (configs[4]) 256 tokens": decode_bench(dev, 128, 256, 20, peaks),
+            }
         if args.cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args)
         print(json.dumps(line), flush=True)
@@ -264,6 +269,93 @@ def run_b200(args):
     blk.free_workspace()
     if world > 1:
         dist.destroy_process_group()
+
+
+def _random_block(mlp, cfgm, E, dev, seed):
+    cfg = cfgm.GPTOssConfig(num_experts=E)
+    blk = mlp.MLPBlock(cfg, device=dev)
+    g = torch_gen(dev, seed)
+    import torch
+    with torch.no_grad():
+        blk.gate_weight.copy_((torch.randn(E, HIDDEN, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+        blk.gate_bias.copy_((torch.randn(E, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+        for name in ("mlp1_weight_blocks", "mlp2_weight_blocks"):
+            t = getattr(blk, name)
+            t.copy_(torch.randint(0, 256, t.shape, generator=g, device=dev, dtype=torch.int32).to(torch.uint8))
+        for name in ("mlp1_weight_scales", "mlp2_weight_scales"):
+            t = getattr(blk, name)
+            t.copy_(torch.randint(118, 125, t.shape, generator=g, device=dev, dtype=torch.int32).to(torch.uint8))
+        for name in ("mlp1_bias", "mlp2_bias"):
+            t = getattr(blk, name)
+            t.copy_((torch.randn(t.shape, generator=g, device=dev) * 0.02).to(torch.bfloat16))
+    return blk.prepare()
+
+
+def torch_gen(dev, seed):
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    return g
+
+
+def decode_bench(dev, E, M, steps, peaks):
+    """MoE decode: M tokens through MLPBlock.forward replayed from a CUDA
+    graph, L2 flushed (a 256 MB write) before every timed step.  Bytes =
+    13,236,480 per distinct expert the step routes to (MXFP4 blocks, scales and
+    biases of both projections) + router weights + activations."""
+    import torch
+    mlp = importlib.import_module("gpt-oss-tvm_b200.mlp")
+    cfgm = importlib.import_module("gpt-oss-tvm_b200.config")
+    blk = _random_block(mlp, cfgm, E, dev, 7 + E)
+    g = torch_gen(dev, 11 + M)
+    xs = [torch.randn(M, HIDDEN, generator=g, device=dev).to(torch.bfloat16) for _ in range(4)]
+    x = torch.empty_like(xs[0])
+    out = torch.empty_like(x)
+    x.copy_(xs[0])
+    for _ in range(3):
+        blk.forward(x, out)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        blk.forward(x, out)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    times, bytes_ = [], []
+    per_expert = 2 * (INTER * HIDDEN // 2 + INTER * HIDDEN // 32 + INTER) + \
+        (HIDDEN * INTER // 2 + HIDDEN * INTER // 32 + HIDDEN)  # 13,236,480 B
+    for i in range(steps + 3):
+        x.copy_(xs[i % len(xs)])
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        if i >= 3:
+            times.append(e0.elapsed_time(e1))
+    # distinct experts per input (routing of each of the inputs)
+    distinct = []
+    for xi in xs:
+        logits = torch.empty(M, E, dtype=torch.bfloat16, device=dev)
+        w = torch.empty(M, 4, dtype=torch.bfloat16, device=dev)
+        idx = torch.empty(M, 4, dtype=torch.int32, device=dev)
+        t = torch.empty_like(xi)
+        lib = importlib.import_module("gpt-oss-tvm_b200._lib")
+        S = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        P = lambda a: ctypes.c_void_p(a.data_ptr())  # noqa: E731
+        lib.call("gptoss_rms_norm", P(xi), P(blk.norm_weight), M, HIDDEN, ctypes.c_float(1e-5), P(t), S)
+        lib.call("gptoss_moe_router", P(t), P(blk.gate_weight), P(blk.gate_bias), M, E, HIDDEN, 4, P(logits), P(w),
+                 P(idx), None, S)
+        distinct.append(int(torch.unique(idx).numel()))
+    nbytes = statistics.mean(distinct) * per_expert + E * HIDDEN * 2 + E * 2 + HIDDEN * 2 + 2 * M * HIDDEN * 2
+    ms = statistics.median(times)
+    gbs = nbytes / (ms / 1e3) / 1e9
+    del graph
+    blk.free_workspace()
+    return {"tokens": M, "experts": E, "ms_per_step": round(ms, 4), "tokens_per_s": round(M / (ms / 1e3), 1),
+            "distinct_experts": statistics.mean(distinct), "bytes_per_step": int(nbytes),
+            "achieved_gbs": round(gbs, 1), "hbm_peak_gbs": peaks.get("hbm_gbs"),
+            "hbm_frac": round(gbs / float(peaks.get("hbm_gbs", 6650.0)), 4),
+            "l2": "flushed before every step (256 MB write)", "cuda_graph": True}
 
 
 def cpu_baseline(args):
@@ -337,6 +429,7 @@ def main():
     ap.add_argument("--cpu-tokens", type=int, default=32, help="token sample of the CPU baseline")
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU (default: the configs[3] 8192)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-decode", dest="decode", action="store_false", help="skip the MoE decode measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
