@@ -41,6 +41,9 @@ HIDDEN = 2880
 INTER = 2880
 METRIC = "MoE-layer tokens/s (gpt-oss-120b MoE layer, 8192-token prefill)"
 FP4_DENSE_PEAK_TFLOPS = 9000.0  # nominal dense e2m1 tensor peak of one B200
+# DRAM bytes (read + write) of one gate/up GEMM launch at the 8192-token workload, from the
+# ncu capture summarised in profiles/moe_gemm_config3_prefill.md
+MLP1_DRAM_TRAFFIC_BYTES = 1.319099e9 + 0.184780e9
 
 
 def measured_peaks():
@@ -249,7 +252,9 @@ def run_b200(args):
             "roofline": {"bound": "tensor", "kernel": "moe_gemm_tc_kernel<0> (gate/up + SwiGLU)",
                          "achieved": round(achieved_tflops, 1), "peak": peak_tflops, "unit": "TFLOP/s",
                          "frac": round(achieved_tflops / peak_tflops, 4), "peak_source": f"{peak_kind} bf16 dense (cuBLAS)",
-                         "traffic": None,
+                         "traffic": (MLP1_DRAM_TRAFFIC_BYTES if TOKENS == 8192 and world == 1 else None),
+                         "traffic_unit": "bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+                         "algorithmic_bytes": 128 * (8294400 + 518400 + 11520) + 2 * TOKENS * TOP_K * HIDDEN * 2,
                          "mma_kind": "tcgen05.mma kind::f16 (" + ("f16" if blk.f16_path else "bf16") + " x same -> fp32)",
                          "frac_of_fp4_dense_peak": round(achieved_tflops / FP4_DENSE_PEAK_TFLOPS, 4),
                          "all_gemm_tflops": round(total_gemm_tflops, 1)},

@@ -29,7 +29,7 @@ enum DeviceError : uint32_t {
 
 // Token rows of one grouped-GEMM tile (the MMA N dimension); the permutation
 // plans its token tiles with this bound.
-constexpr int kMoeTileMaxRows = 208;
+constexpr int kMoeTileMaxRows = 192;
 
 // Poll budget for one mbarrier wait.  try_wait itself blocks for a bounded,
 // hardware-defined window, so this is several seconds of waiting at most.

@@ -18,7 +18,7 @@
 //     the activation operand only.
 //   * The activations (expert-major rows, bf16, K-major) are the "B" operand,
 //     brought into 128-byte-swizzled shared memory by TMA.
-//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 208
+//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 192
 //     token rows, K = 16 per instruction) accumulates fp32 in TMEM.
 //   * Nibbles are streamed by TMA (32-byte swizzle) through an 8-deep ring;
 //     each tile's 128 x K/32 scale bytes arrive with one bulk copy.
@@ -36,16 +36,16 @@ constexpr int kBM = 128;            // weight rows per tile (MMA M)
 constexpr int kMaxBN = kMoeTileMaxRows;  // token rows per tile (MMA N, max)
 constexpr int kBoxRows = 16;        // activation TMA box height (up to 13 boxes per stage)
 constexpr int kBK = 64;             // K per pipeline chunk (one 128 B swizzle row of bf16)
-constexpr int kStages = 3;          // TMEM A stages (dequantised weights)
+constexpr int kStages = 4;          // TMEM A stages (dequantised weights)
 constexpr int kBStages = 6;         // shared-memory activation stages
 constexpr int kWStages = 8;         // nibble ring depth
-constexpr int kActStageBytes = kMaxBN * kBK * 2;   // 26 KB (208 rows of 128 B)
+constexpr int kActStageBytes = kMaxBN * kBK * 2;   // 24 KB (192 rows of 128 B)
 constexpr int kWStageBytes = kBM * (kBK / 2);      // 4 KB (128 rows x 32 nibble bytes)
 constexpr int kMaxGroups = 96;                     // K/32 upper bound (K <= 3072)
 constexpr int kScaleBytes = kBM * kMaxGroups;      // per-tile scale buffer (row stride = G)
 constexpr int kAccCols = kMaxBN;                   // columns of one accumulator buffer
 constexpr int kTmemCols = 512;
-constexpr int kAColBase = 2 * kAccCols;            // A stage s at columns 416 + 32 s
+constexpr int kAColBase = 2 * kAccCols;            // A stage s at columns 384 + 32 s
 static_assert(kAColBase + kStages * 32 <= kTmemCols, "TMEM budget");
 constexpr int kDequantWarps = 16;  // 4 warpgroups: (chunk parity, MXFP4 group of the chunk)
 constexpr int kDequantPerChunk = 8; // warps that fill one chunk's A stage
