@@ -262,10 +262,7 @@ def run_b200(args):
             "clocks": sampler.summary(),
         }
         if args.decode and world == 1:
-            line["decode"] = {
-                "gpt-oss-20b (configs[0]) 1 token": decode_bench(dev, 32, 1, 20, peaks),
-                "gpt-oss-120b batched decode (configs[4]) 256 tokens": decode_bench(dev, 128, 256, 20, peaks),
-            }
+            line["decode"] = {name: decode_bench(dev, E, M, 20, peaks) for name, (E, M) in DECODE_CASES.items()}
         if args.cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args)
         print(json.dumps(line), flush=True)
@@ -301,6 +298,22 @@ def torch_gen(dev, seed):
     g = torch.Generator(device=dev)
     g.manual_seed(seed)
     return g
+
+
+DECODE_CASES = {
+    "gpt-oss-20b (configs[0]) 1 token": (32, 1),
+    "gpt-oss-120b batched decode (configs[4]) 256 tokens": (128, 256),
+}
+
+
+def decode_only(args):
+    """--decode-only I: just decode case I on cuda:0 (a small, self-contained
+    command for kernel profiles)."""
+    import torch
+    name = list(DECODE_CASES)[args.decode_only]
+    E, M = DECODE_CASES[name]
+    peaks, _ = measured_peaks()
+    print(json.dumps({name: decode_bench(torch.device("cuda", 0), E, M, args.steps, peaks)}), flush=True)
 
 
 def decode_bench(dev, E, M, steps, peaks):
@@ -353,6 +366,8 @@ def decode_bench(dev, E, M, steps, peaks):
         distinct.append(int(torch.unique(idx).numel()))
     nbytes = statistics.mean(distinct) * per_expert + E * HIDDEN * 2 + E * 2 + HIDDEN * 2 + 2 * M * HIDDEN * 2
     ms = statistics.median(times)
+    st = blk.profile_stages(xs[0], repeats=5, flush=flush)
+    stages = {k: round(v, 4) for k, v in st.items() if k.endswith("_ms")}
     gbs = nbytes / (ms / 1e3) / 1e9
     del graph
     blk.free_workspace()
@@ -360,7 +375,8 @@ def decode_bench(dev, E, M, steps, peaks):
             "distinct_experts": statistics.mean(distinct), "bytes_per_step": int(nbytes),
             "achieved_gbs": round(gbs, 1), "hbm_peak_gbs": peaks.get("hbm_gbs"),
             "hbm_frac": round(gbs / float(peaks.get("hbm_gbs", 6650.0)), 4),
-            "l2": "flushed before every step (256 MB write)", "cuda_graph": True}
+            "l2": "flushed before every step (256 MB write)", "cuda_graph": True,
+            "stages_ms": stages, "stages_note": "kernels launched one by one (not graph-replayed), L2 flushed"}
 
 
 def cpu_baseline(args):
@@ -435,11 +451,15 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU (default: the configs[3] 8192)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-decode", dest="decode", action="store_false", help="skip the MoE decode measurements")
+    ap.add_argument("--decode-only", type=int, default=None, choices=range(len(DECODE_CASES)),
+                    help="run only this decode case (index into DECODE_CASES) and print its measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     TOKENS = args.tokens
-    if args.impl == "reference":
+    if args.decode_only is not None:
+        decode_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

@@ -25,11 +25,18 @@ enum DeviceError : uint32_t {
   kErrBadRouting = 1u << 3,      // expert index outside [0, E)
   kErrTimeoutOther = 1u << 4,
   kErrTimeoutFlag = 1u << 5,     // generic bounded flag wait ran out
+  kErrBadTilePlan = 1u << 6,     // a token tile larger than the GEMM variant holds
 };
 
-// Token rows of one grouped-GEMM tile (the MMA N dimension); the permutation
-// plans its token tiles with this bound.
+// Token rows of one grouped-GEMM tile (the MMA N dimension).  With few rows
+// per expert (decode) the tiles are at most 32 rows and the GEMM runs its
+// weight-streaming variant; otherwise at most 192.  The permutation plans its
+// token tiles with the same rule as the GEMM launch.
 constexpr int kMoeTileMaxRows = 192;
+constexpr int kMoeTileRowsSmall = 32;
+__host__ __device__ __forceinline__ int moe_tile_rows_max(int64_t rows, int32_t num_experts) {
+  return rows <= 8 * (int64_t)num_experts ? kMoeTileRowsSmall : kMoeTileMaxRows;
+}
 
 // Poll budget for one mbarrier wait.  try_wait itself blocks for a bounded,
 // hardware-defined window, so this is several seconds of waiting at most.
@@ -137,6 +144,25 @@ __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// One 64-wide K chunk: four K=16 steps, A columns a_tmem + 0/8/16/24 and B
+// 32 bytes further along the 128-byte swizzled rows per step (descriptor start
+// address + 2).  `accumulate` == 0 only for the first chunk of a tile.  One asm
+// block keeps the per-instruction issue cost (descriptor arithmetic,
+// predicates) off the single issuing thread's critical path.
+__device__ __forceinline__ void tc_mma4_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %6, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %8, %3, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], %10, %3, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(a_tmem + 8), "l"(b_desc + 2), "r"(a_tmem + 16),
+      "l"(b_desc + 4), "r"(a_tmem + 24), "l"(b_desc + 6)
       : "memory");
 }
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16.

@@ -19,11 +19,12 @@
 //   * The activations (expert-major rows, bf16, K-major) are the "B" operand,
 //     brought into 128-byte-swizzled shared memory by TMA.
 //   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 192
-//     token rows, K = 16 per instruction) accumulates fp32 in TMEM.
-//   * Nibbles are streamed by TMA (32-byte swizzle) through an 8-deep ring;
-//     each tile's 128 x K/32 scale bytes arrive with one bulk copy.
-// Warp roles: 0-15 dequant (four warpgroups: even / odd K chunks x the two
-// 32-element MXFP4 groups of a 64-wide chunk), 16-19 epilogue (double-buffered
+//     token rows, or 32 in the decode variant, K = 16 per instruction)
+//     accumulates fp32 in TMEM.
+//   * Nibbles are streamed by TMA (32-byte swizzle) through an 8-deep ring
+//     (32-deep in the decode variant); each tile's 128 x K/32 scale bytes
+//     arrive with one bulk copy.
+// Warp roles: 0-15 dequant (four warpgroups), 16-19 epilogue (double-buffered
 // TMEM accumulator, so the epilogue of tile i overlaps the main loop of tile
 // i+1), 20 activation TMA, 21 MMA issuer (also owns TMEM), 22 weight TMA.
 #include "common.cuh"
@@ -33,24 +34,55 @@ namespace gptoss {
 
 constexpr int kGemmThreads = 736;
 constexpr int kBM = 128;            // weight rows per tile (MMA M)
-constexpr int kMaxBN = kMoeTileMaxRows;  // token rows per tile (MMA N, max)
-constexpr int kBoxRows = 16;        // activation TMA box height (up to 13 boxes per stage)
+constexpr int kBoxRows = 16;        // activation TMA box heights: 16 rows, and 64 rows for the
+constexpr int kBigBoxRows = 64;     // bulk of large tiles (fewer, larger TMA requests)
 constexpr int kBK = 64;             // K per pipeline chunk (one 128 B swizzle row of bf16)
-constexpr int kStages = 4;          // TMEM A stages (dequantised weights)
-constexpr int kBStages = 6;         // shared-memory activation stages
-constexpr int kWStages = 8;         // nibble ring depth
-constexpr int kActStageBytes = kMaxBN * kBK * 2;   // 24 KB (192 rows of 128 B)
-constexpr int kWStageBytes = kBM * (kBK / 2);      // 4 KB (128 rows x 32 nibble bytes)
+constexpr int kWChunks = 4;                        // K chunks per nibble stage
+constexpr int kWRowBytes = kWChunks * kBK / 2;     // 128 nibble bytes of a weight row per stage
+constexpr int kWStageBytes = kBM * kWRowBytes;     // 16 KB (128 rows x 128 B, 128-byte swizzle)
 constexpr int kMaxGroups = 96;                     // K/32 upper bound (K <= 3072)
 constexpr int kScaleBytes = kBM * kMaxGroups;      // per-tile scale buffer (row stride = G)
-constexpr int kAccCols = kMaxBN;                   // columns of one accumulator buffer
 constexpr int kTmemCols = 512;
-constexpr int kAColBase = 2 * kAccCols;            // A stage s at columns 384 + 32 s
-static_assert(kAColBase + kStages * 32 <= kTmemCols, "TMEM budget");
-constexpr int kDequantWarps = 16;  // 4 warpgroups: (chunk parity, MXFP4 group of the chunk)
-constexpr int kDequantPerChunk = 8; // warps that fill one chunk's A stage
+constexpr int kASlots = 4;                         // TMEM A slots: slot w is written by warpgroup w only
+constexpr int kDequantWarps = 16;  // 4 warpgroups
 constexpr int kEpiWarp0 = 16;
 constexpr int kActWarp = 20, kMmaWarp = 21, kWWarp = 22;
+
+// Two shapes of the same pipeline.
+//   Large tiles (prefill): up to 192 token rows, 6 activation stages, 3
+//   nibble stages (48 KB) and 2 TMEM A slots (the accumulators take the rest).
+//   Small tiles (decode, few rows per expert): up to 32 token rows, the MMA
+//   is nearly free and the weights must stream at HBM speed: 6 nibble stages
+//   and 6 activation stages of 4 chunks each (96 KB + up to 96 KB in flight
+//   per SM; an activation stream only a few chunks deep would queue behind
+//   the weights in the SM's TMA unit and pace the MMA) and 6 TMEM A slots.
+// A nibble stage is one TMA box of 128 weight rows x 128 bytes (4 K chunks):
+// wide rows keep the TMA request rate, not HBM, from bounding the stream.
+template <bool kSmall>
+struct GemmCfg {
+  static constexpr int kMaxBN = kSmall ? kMoeTileRowsSmall : kMoeTileMaxRows;
+  static constexpr int kBStages = 6;
+  static constexpr int kBChunks = kSmall ? kWChunks : 1;  // K chunks per activation stage
+  static constexpr int kAChunks = kSmall ? 2 : 1;      // K chunks per TMEM A stage (one warpgroup's round)
+  static constexpr int kASlotCols = kAChunks * kBK / 2;  // TMEM columns of an A slot (f16/bf16 pairs)
+  static constexpr int kAPerW = kWChunks / kAChunks;    // A stages per nibble stage = its reader warpgroups
+  static constexpr int kWStages = kSmall ? 6 : 3;
+  static constexpr int kActChunkBytes = kMaxBN * kBK * 2;  // one chunk of the token rows
+  static constexpr int kActStageBytes = kBChunks * kActChunkBytes;
+  static constexpr int kAccCols = kMaxBN;
+  static constexpr int kAColBase = 2 * kAccCols;
+  static_assert(kAColBase + kASlots * kASlotCols <= kTmemCols, "TMEM budget");
+  static_assert(kASlots == 4 && kDequantWarps == 16, "one A slot per dequant warpgroup");
+  // shared memory offsets from the 1024-aligned base
+  static constexpr int kAct = 0;
+  static constexpr int kW = kAct + kBStages * kActStageBytes;
+  static constexpr int kScale = kW + kWStages * kWStageBytes;
+  static constexpr int kBar = kScale + 2 * kScaleBytes;
+  static constexpr int kNumBars = 2 * kASlots + 2 * kBStages + 2 * kWStages + 4 + 4;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kAlloc = kMisc + 64 + 1024;  // + slack for manual 1024 B alignment
+  static_assert(kAlloc <= 227 * 1024, "shared memory budget");
+};
 
 struct GemmParams {
   const uint8_t* scales;     // [E, N, G]
@@ -67,23 +99,14 @@ struct GemmParams {
   uint32_t* err;
 };
 
-struct GemmSmem {
-  // offsets from the 1024-aligned base
-  static constexpr int kAct = 0;
-  static constexpr int kW = kAct + kBStages * kActStageBytes;
-  static constexpr int kScale = kW + kWStages * kWStageBytes;
-  static constexpr int kBar = kScale + 2 * kScaleBytes;
-  static constexpr int kNumBars = 2 * kStages + 2 * kBStages + 2 * kWStages + 4 + 4;
-  static constexpr int kMisc = kBar + kNumBars * 8;
-  static constexpr int kTotal = kMisc + 64;
-  static constexpr int kAlloc = kTotal + 1024;  // slack for manual 1024 B alignment
-};
-
 struct TileInfo {
   int32_t expert, row0, nrows, f0;
 };
 
-// Tile t -> (expert, first permuted row, rows, first feature row).
+// Tile t -> (expert, first permuted row, rows, first feature row).  A tile
+// plan made for larger tiles than this variant holds is reported and skipped
+// by every role alike.
+template <int kMaxBN>
 __device__ __forceinline__ bool decode_tile(const GemmParams& p, int32_t t, int32_t ftiles, TileInfo& ti) {
   const int32_t g = t / ftiles;
   const int32_t f = t - g * ftiles;
@@ -101,6 +124,10 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& p, int32_t t, int3
   ti.row0 = base + tt * per;
   ti.nrows = min(per, cnt - tt * per);
   ti.f0 = f * kBM;
+  if (per > kMaxBN) {
+    if (f == 0 && threadIdx.x == 0) raise_error(p.err, kErrBadTilePlan);
+    return false;
+  }
   return ti.nrows > 0;
 }
 
@@ -138,30 +165,56 @@ __device__ __forceinline__ uint32_t e8m0_scale_f16x2(uint32_t s) {
   return h | (h << 16);
 }
 
+// 16 words (32 elements, one MXFP4 group) of decoded weights.
+template <bool kF16>
+__device__ __forceinline__ void decode_group(const uint4 nb, uint32_t sc, bool row_ok, uint32_t (&r)[16]) {
+  if (!row_ok) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) r[j] = 0u;
+    return;
+  }
+  if (kF16) {
+    const uint32_t sc2 = e8m0_scale_f16x2(sc);
+    fp4x8_to_f16x8(nb.x, sc2, r[0], r[1], r[2], r[3]);
+    fp4x8_to_f16x8(nb.y, sc2, r[4], r[5], r[6], r[7]);
+    fp4x8_to_f16x8(nb.z, sc2, r[8], r[9], r[10], r[11]);
+    fp4x8_to_f16x8(nb.w, sc2, r[12], r[13], r[14], r[15]);
+  } else {
+    const uint32_t sc2 = e8m0_scale_bf16x2(sc);
+    uint32_t o[4];
+    fp4x8_to_bf16x8(nb.x, sc2, o); r[0] = o[0]; r[1] = o[1]; r[2] = o[2]; r[3] = o[3];
+    fp4x8_to_bf16x8(nb.y, sc2, o); r[4] = o[0]; r[5] = o[1]; r[6] = o[2]; r[7] = o[3];
+    fp4x8_to_bf16x8(nb.z, sc2, o); r[8] = o[0]; r[9] = o[1]; r[10] = o[2]; r[11] = o[3];
+    fp4x8_to_bf16x8(nb.w, sc2, o); r[12] = o[0]; r[13] = o[1]; r[14] = o[2]; r[15] = o[3];
+  }
+}
+
 // kF16: weights decoded to f16 by the hardware converter and activations in
 // f16 (the fast path, valid when every scale code is in 104..140); otherwise
 // exact bf16 decode and bf16 activations.
-template <int kMode, bool kF16>
+template <int kMode, bool kF16, bool kSmall>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_w,
+    moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_act64,
+                       const __grid_constant__ CUtensorMap tmap_w,
                        const GemmParams p) {
+  using C = GemmCfg<kSmall>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* act_s = smem + GemmSmem::kAct;
-  uint8_t* w_s = smem + GemmSmem::kW;
-  uint8_t* sc_s = smem + GemmSmem::kScale;
-  uint64_t* bars = (uint64_t*)(smem + GemmSmem::kBar);
-  uint64_t* full_bar = bars;                      // [kStages] TMEM A stage: 8 dequant warps
-  uint64_t* empty_bar = full_bar + kStages;       // [kStages] MMA commit
-  uint64_t* bfull_bar = empty_bar + kStages;      // [kBStages] activation TMA tx
-  uint64_t* bempty_bar = bfull_bar + kBStages;    // [kBStages] MMA commit
-  uint64_t* wfull_bar = bempty_bar + kBStages;    // [kWStages] nibble TMA tx
-  uint64_t* wempty_bar = wfull_bar + kWStages;    // [kWStages] 8 dequant warps
-  uint64_t* scfull_bar = wempty_bar + kWStages;   // [2] scale bulk copy tx
-  uint64_t* scempty_bar = scfull_bar + 2;         // [2] all 16 dequant warps
-  uint64_t* accfull_bar = scempty_bar + 2;        // [2] MMA commit
-  uint64_t* accempty_bar = accfull_bar + 2;       // [2] 4 epilogue warps
-  uint32_t* misc = (uint32_t*)(smem + GemmSmem::kMisc);
+  uint8_t* act_s = smem + C::kAct;
+  uint8_t* w_s = smem + C::kW;
+  uint8_t* sc_s = smem + C::kScale;
+  uint64_t* bars = (uint64_t*)(smem + C::kBar);
+  uint64_t* full_bar = bars;                       // [kASlots] TMEM A slot written: the owning warpgroup
+  uint64_t* empty_bar = full_bar + kASlots;        // [kASlots] MMA commit
+  uint64_t* bfull_bar = empty_bar + kASlots;       // [kBStages] activation TMA tx
+  uint64_t* bempty_bar = bfull_bar + C::kBStages;  // [kBStages] MMA commit
+  uint64_t* wfull_bar = bempty_bar + C::kBStages;  // [kWStages] nibble TMA tx
+  uint64_t* wempty_bar = wfull_bar + C::kWStages;  // [kWStages] the dequant warps that read it
+  uint64_t* scfull_bar = wempty_bar + C::kWStages; // [2] scale bulk copy tx
+  uint64_t* scempty_bar = scfull_bar + 2;          // [2] all 16 dequant warps
+  uint64_t* accfull_bar = scempty_bar + 2;         // [2] MMA commit
+  uint64_t* accempty_bar = accfull_bar + 2;        // [2] 4 epilogue warps
+  uint32_t* misc = (uint32_t*)(smem + C::kMisc);
   volatile uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_s = misc + 1;
 
@@ -169,21 +222,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int lane = threadIdx.x & 31;
   const int32_t G = p.K >> 5;
   const int32_t nchunks = p.K / kBK;
+  const int32_t nstages = (nchunks + kWChunks - 1) / kWChunks;  // nibble stages per tile
+  const int32_t nastages = (nchunks + C::kAChunks - 1) / C::kAChunks;  // TMEM A stages per tile
   const int32_t ftiles = (p.N + kBM - 1) / kBM;
   const int32_t total_tiles = __ldg(p.tile_ptr + p.num_experts) * ftiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], kDequantPerChunk);
+    for (int s = 0; s < kASlots; ++s) {
+      mbar_init(&full_bar[s], 4);
       mbar_init(&empty_bar[s], 1);
     }
-    for (int s = 0; s < kBStages; ++s) {
+    for (int s = 0; s < C::kBStages; ++s) {
       mbar_init(&bfull_bar[s], 1);
       mbar_init(&bempty_bar[s], 1);
     }
-    for (int s = 0; s < kWStages; ++s) {
+    for (int s = 0; s < C::kWStages; ++s) {
       mbar_init(&wfull_bar[s], 1);
-      mbar_init(&wempty_bar[s], kDequantPerChunk);
+      mbar_init(&wempty_bar[s], 4 * C::kAPerW);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&scfull_bar[s], 1);
@@ -200,6 +255,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   if (warp == kActWarp && lane == 0) {
     tma_prefetch_desc(&tmap_act);
+    tma_prefetch_desc(&tmap_act64);
     tma_prefetch_desc(&tmap_w);
   }
   tc_fence_before();
@@ -210,18 +266,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == kActWarp) {
     // ------------------------------------------------ activation producer
     if (elect_one()) {
-      uint32_t it = 0;
+      uint32_t bit = 0;
       for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
         TileInfo ti;
-        if (!decode_tile(p, t, ftiles, ti)) continue;
-        const int32_t nbox = (ti.nrows + kBoxRows - 1) / kBoxRows;
-        for (int32_t c = 0; c < nchunks; ++c, ++it) {
-          const uint32_t s = it % kBStages, ph = (it / kBStages) & 1;
+        if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
+        const int32_t nbig = kSmall ? 0 : ti.nrows / kBigBoxRows;
+        const int32_t nbox = (ti.nrows - nbig * kBigBoxRows + kBoxRows - 1) / kBoxRows;
+        const int32_t brows = nbig * kBigBoxRows + nbox * kBoxRows;  // rows landed per chunk
+        for (int32_t c0 = 0; c0 < nchunks; c0 += C::kBChunks, ++bit) {
+          const uint32_t s = bit % C::kBStages, ph = (bit / C::kBStages) & 1;
+          const int32_t nq = min(C::kBChunks, nchunks - c0);
           if (!mbar_wait(&bempty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
-          mbar_arrive_expect_tx(&bfull_bar[s], (uint32_t)nbox * kBoxRows * 128);
-          for (int32_t b = 0; b < nbox; ++b)
-            tma_load_2d(act_s + s * kActStageBytes + b * kBoxRows * 128, &tmap_act, c * kBK, ti.row0 + b * kBoxRows,
-                        &bfull_bar[s]);
+          mbar_arrive_expect_tx(&bfull_bar[s], (uint32_t)(nq * brows * 128));
+          for (int32_t q = 0; q < nq; ++q) {
+            uint8_t* dst = act_s + s * C::kActStageBytes + q * C::kActChunkBytes;
+            for (int32_t b = 0; b < nbig; ++b)
+              tma_load_2d(dst + b * kBigBoxRows * 128, &tmap_act64, (c0 + q) * kBK, ti.row0 + b * kBigBoxRows,
+                          &bfull_bar[s]);
+            for (int32_t b = 0; b < nbox; ++b)
+              tma_load_2d(dst + (nbig * kBigBoxRows + b * kBoxRows) * 128, &tmap_act, (c0 + q) * kBK,
+                          ti.row0 + nbig * kBigBoxRows + b * kBoxRows, &bfull_bar[s]);
+          }
         }
       }
     }
@@ -231,7 +296,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t wit = 0, tl = 0;
       for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
         TileInfo ti;
-        if (!decode_tile(p, t, ftiles, ti)) continue;
+        if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
         const uint32_t sb = tl & 1, sph = (tl >> 1) & 1;
         ++tl;
         if (!mbar_wait(&scempty_bar[sb], sph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
@@ -246,11 +311,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             : "memory");
         const int32_t wrow = ti.expert * p.N + ti.f0;
         bool ok = true;
-        for (int32_t c = 0; c < nchunks; ++c, ++wit) {
-          const uint32_t s = wit % kWStages, ph = (wit / kWStages) & 1;
+        for (int32_t j = 0; j < nstages; ++j, ++wit) {
+          const uint32_t s = wit % C::kWStages, ph = (wit / C::kWStages) & 1;
           if (!mbar_wait(&wempty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&wfull_bar[s], kWStageBytes);
-          tma_load_2d(w_s + s * kWStageBytes, &tmap_w, c * (kBK / 2), wrow, &wfull_bar[s]);
+          mbar_arrive_expect_tx(&wfull_bar[s], kWStageBytes);  // the zero-filled tail counts too
+          tma_load_2d(w_s + s * kWStageBytes, &tmap_w, j * kWRowBytes, wrow, &wfull_bar[s]);
         }
         if (!ok) { *abort_s = 1; break; }
       }
@@ -258,31 +323,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == kMmaWarp) {
     // --------------------------------------------------------- MMA issuer
     if (elect_one()) {
-      uint32_t it = 0, tl = 0;
+      // slot / activation-stage cursors run on across tiles, in step with the
+      // dequant warpgroups (A stages) and the activation producer (stages)
+      uint32_t s = 0, ph = 0, sb = 0, phb = 0, tl = 0;
+      const uint64_t bdesc0 = make_sdesc_sw128(smem_u32(act_s));
       for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
         TileInfo ti;
-        if (!decode_tile(p, t, ftiles, ti)) continue;
+        if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
         const uint32_t n_mma = (uint32_t)((ti.nrows + 15) & ~15);
         const uint32_t idesc = kF16 ? make_idesc_f16(kBM, n_mma) : make_idesc_bf16(kBM, n_mma);
         const uint32_t ab = tl & 1, aph = (tl >> 1) & 1;
         if (!mbar_wait(&accempty_bar[ab], aph ^ 1, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + ab * kAccCols;
+        const uint32_t d_tmem = tmem_base + ab * C::kAccCols;
         bool ok = true;
-        for (int32_t c = 0; c < nchunks; ++c, ++it) {
-          const uint32_t s = it % kStages, ph = (it / kStages) & 1;
-          const uint32_t sb = it % kBStages, phb = (it / kBStages) & 1;
-          if (!mbar_wait(&bfull_bar[sb], phb, p.err, kErrTimeoutFull)) { ok = false; break; }
-          if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t b_base = smem_u32(act_s + sb * kActStageBytes);
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            tc_mma_ts(d_tmem, tmem_base + kAColBase + s * 32 + kk * 8, make_sdesc_sw128(b_base + kk * 32), idesc,
-                      (c > 0 || kk > 0) ? 1u : 0u);
+        int32_t sub = 0, q = 0;
+        for (int32_t c = 0; c < nchunks; ++c) {
+          if (q == 0) {
+            if (!mbar_wait(&bfull_bar[sb], phb, p.err, kErrTimeoutFull)) { ok = false; break; }
+            tc_fence_after();
           }
-          tc_commit(&empty_bar[s]);
-          tc_commit(&bempty_bar[sb]);
+          if (sub == 0) {
+            if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) { ok = false; break; }
+            tc_fence_after();
+          }
+          // start-address field of the descriptor: (byte offset >> 4), no carry out of its 14 bits
+          const uint64_t bdesc = bdesc0 + (uint64_t)((uint32_t)(sb * C::kActStageBytes + q * C::kActChunkBytes) >> 4);
+          tc_mma4_ts(d_tmem, tmem_base + C::kAColBase + s * C::kASlotCols + sub * 32, bdesc, idesc, c > 0 ? 1u : 0u);
+          const bool last = c == nchunks - 1;
+          if (++sub == C::kAChunks || last) {
+            tc_commit(&empty_bar[s]);
+            sub = 0;
+            s = (s + 1) & (kASlots - 1);
+            ph ^= s == 0 ? 1u : 0u;
+          }
+          if (++q == C::kBChunks || last) {
+            tc_commit(&bempty_bar[sb]);
+            q = 0;
+            if (++sb == C::kBStages) { sb = 0; phb ^= 1u; }
+          }
         }
         if (!ok) { *abort_s = 1; break; }
         tc_commit(&accfull_bar[ab]);
@@ -291,63 +370,70 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp < kDequantWarps) {
     // --------------------------------------------- dequant: weights -> TMEM
-    const int wg = (warp >> 2) & 1;             // which MXFP4 group of the chunk
-    const int parity = warp >> 3;               // even or odd chunks
+    // The A stages of all tiles are numbered consecutively (gai); stage gai
+    // (kAChunks chunks, both MXFP4 groups of each) is decoded by warpgroup
+    // gai % 4 into TMEM slot gai % 4, so each slot has a single writer and its
+    // empty/full phases advance in that warpgroup's program order.  A nibble
+    // stage holds kAPerW A stages and is read (and released) by their
+    // kAPerW warpgroups: all four for large tiles; for small tiles two, the
+    // two pairs alternating stages so that one pair's barrier waits overlap
+    // the other pair's decode.
+    const int wgi = warp >> 2;
     const int row = (warp & 3) * 32 + lane;     // weight row within the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    uint32_t it = 0, wit = 0, tl = 0;
+    const uint32_t swz = (uint32_t)(row & 7);   // 128-byte swizzle of the nibble rows
+    const uint32_t ta = tmem_base + lane_base + C::kAColBase + (uint32_t)wgi * C::kASlotCols;
+    uint32_t ait = 0, wit = 0, tl = 0, uses = 0;
     for (int32_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       TileInfo ti;
-      if (!decode_tile(p, t, ftiles, ti)) continue;
+      if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
       if (*abort_s) break;
       const uint32_t sb = tl & 1, sph = (tl >> 1) & 1;
       ++tl;
       const bool row_ok = ti.f0 + row < p.N;
       bool ok = mbar_wait(&scfull_bar[sb], sph, p.err, kErrTimeoutFull);
-      const uint8_t* srow = sc_s + sb * kScaleBytes + row * G + wg;
-      const uint32_t nib_off = (uint32_t)(wg ^ ((row >> 2) & 1)) << 4;  // 32-byte swizzle
-      for (int32_t c = parity; c < nchunks && ok; c += 2) {
-        const uint32_t witc = wit + (uint32_t)c, itc = it + (uint32_t)c;
-        const uint32_t ws = witc % kWStages, wph = (witc / kWStages) & 1;
-        const uint32_t s = itc % kStages, ph = (itc / kStages) & 1;
+      const uint8_t* srow = sc_s + sb * kScaleBytes + row * G;
+      for (int32_t j = 0; j < nstages && ok; ++j) {
+        // this warpgroup's A stage in nibble stage j, if it reads the stage
+        const int r = (wgi - (int)((ait + (uint32_t)(j * C::kAPerW)) & 3u)) & 3;
+        if (r >= C::kAPerW) continue;
+        const uint32_t wsi = wit + (uint32_t)j;
+        const uint32_t ws = wsi % C::kWStages, wph = (wsi / C::kWStages) & 1;
         ok = mbar_wait(&wfull_bar[ws], wph, p.err, kErrTimeoutFull);
         if (!ok) break;
-        const uint4 nb = *(const uint4*)(w_s + ws * kWStageBytes + row * 32 + nib_off);
-        const uint32_t sc = srow[2 * c];
+        // pieces 2q + g of the stage row, q = r * kAChunks + u (chunk), g = group
+        const uint8_t* wrow = w_s + ws * kWStageBytes + row * kWRowBytes;
+        uint4 nb[2 * C::kAChunks];
+#pragma unroll
+        for (int k = 0; k < 2 * C::kAChunks; ++k)
+          nb[k] = *(const uint4*)(wrow + (((uint32_t)(2 * C::kAChunks * r + k) ^ swz) << 4));
         __syncwarp();
         if (lane == 0) mbar_arrive(&wempty_bar[ws]);
-        uint32_t r[16];
-        if (row_ok) {
-          if (kF16) {
-            const uint32_t sc2 = e8m0_scale_f16x2(sc);
-            fp4x8_to_f16x8(nb.x, sc2, r[0], r[1], r[2], r[3]);
-            fp4x8_to_f16x8(nb.y, sc2, r[4], r[5], r[6], r[7]);
-            fp4x8_to_f16x8(nb.z, sc2, r[8], r[9], r[10], r[11]);
-            fp4x8_to_f16x8(nb.w, sc2, r[12], r[13], r[14], r[15]);
-          } else {
-            const uint32_t sc2 = e8m0_scale_bf16x2(sc);
-            uint32_t o[4];
-            fp4x8_to_bf16x8(nb.x, sc2, o); r[0] = o[0]; r[1] = o[1]; r[2] = o[2]; r[3] = o[3];
-            fp4x8_to_bf16x8(nb.y, sc2, o); r[4] = o[0]; r[5] = o[1]; r[6] = o[2]; r[7] = o[3];
-            fp4x8_to_bf16x8(nb.z, sc2, o); r[8] = o[0]; r[9] = o[1]; r[10] = o[2]; r[11] = o[3];
-            fp4x8_to_bf16x8(nb.w, sc2, o); r[12] = o[0]; r[13] = o[1]; r[14] = o[2]; r[15] = o[3];
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) r[j] = 0u;
-        }
-        ok = mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty);
+        const int32_t c0 = (j * C::kAPerW + r) * C::kAChunks;
+        if (c0 >= nchunks) continue;            // no chunk here (short last stage)
+        // slot wgi, use number `uses`: wait until the MMA has consumed the previous use
+        ok = mbar_wait(&empty_bar[wgi], (uses & 1u) ^ 1u, p.err, kErrTimeoutEmpty);
         if (!ok) break;
+        ++uses;
         __syncwarp();
         tc_fence_after();
-        tmem_st_x16(tmem_base + lane_base + kAColBase + s * 32 + wg * 16, r);
+#pragma unroll
+        for (int u = 0; u < C::kAChunks; ++u) {
+          const int32_t c = c0 + u;
+          if (c >= nchunks) break;
+          uint32_t v[16];
+          decode_group<kF16>(nb[2 * u], srow[2 * c], row_ok, v);
+          tmem_st_x16(ta + u * 32, v);
+          decode_group<kF16>(nb[2 * u + 1], srow[2 * c + 1], row_ok, v);
+          tmem_st_x16(ta + u * 32 + 16, v);
+        }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full_bar[s]);
+        if (lane == 0) mbar_arrive(&full_bar[wgi]);
       }
-      it += (uint32_t)nchunks;
-      wit += (uint32_t)nchunks;
+      ait += (uint32_t)nastages;
+      wit += (uint32_t)nstages;
       __syncwarp();
       if (lane == 0) mbar_arrive(&scempty_bar[sb]);
       if (!ok) { *abort_s = 1; break; }
@@ -360,7 +446,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint32_t tl = 0;
     for (int32_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       TileInfo ti;
-      if (!decode_tile(p, t, ftiles, ti)) continue;
+      if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
       if (*abort_s) break;
       const uint32_t ab = tl & 1, aph = (tl >> 1) & 1;
       ++tl;
@@ -373,7 +459,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int32_t ncols = (ti.nrows + 31) & ~31;
       for (int32_t c0 = 0; c0 < ncols; c0 += 32) {
         uint32_t v[32];
-        tmem_ld_x32(tmem_base + lane_base + ab * kAccCols + (uint32_t)c0, v);
+        tmem_ld_x32(tmem_base + lane_base + ab * C::kAccCols + (uint32_t)c0, v);
         tmem_ld_wait();
         if (kMode == 0) {
           // lane pair (2j, 2j+1) holds the glu / linear rows of output column j:
@@ -456,31 +542,37 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 
 
 
-template <int kMode, bool kF16>
-static void launch_variant(const CUtensorMap& ta, const CUtensorMap& tw, const GemmParams& p, int grid, int smem,
-                           cudaStream_t stream) {
+template <int kMode, bool kF16, bool kSmall>
+static void launch_variant(const CUtensorMap& ta, const CUtensorMap& ta64, const CUtensorMap& tw, const GemmParams& p,
+                           int grid, cudaStream_t stream) {
+  const int smem = GemmCfg<kSmall>::kAlloc;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(moe_gemm_tc_kernel<kMode, kF16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(moe_gemm_tc_kernel<kMode, kF16, kSmall>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr = true;
   }
-  moe_gemm_tc_kernel<kMode, kF16><<<grid, kGemmThreads, smem, stream>>>(ta, tw, p);
+  moe_gemm_tc_kernel<kMode, kF16, kSmall><<<grid, kGemmThreads, smem, stream>>>(ta, ta64, tw, p);
 }
 
 int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
-  if (L.K % kBK != 0 || L.K / 32 > kMaxGroups) return -10;
+  if (L.K % kBK != 0 || L.K / 32 > kMaxGroups || L.K / 2 < kWRowBytes) return -10;
   {
     // every tile's scale block must be a whole number of 16-byte units
     const int32_t G = L.K / 32;
     const int32_t last = L.N % kBM ? L.N % kBM : kBM;
     if (((int64_t)kBM * G) % 16 || ((int64_t)last * G) % 16 || ((int64_t)L.N * G) % 16) return -11;
   }
-  CUtensorMap tmap_act, tmap_w;
-  int rc = make_tmap_2d(&tmap_act, L.act, L.f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                        (uint64_t)L.act_rows, (uint64_t)L.K, kBK, kBoxRows, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tmap_act, tmap_act64, tmap_w;
+  const CUtensorMapDataType adt = L.f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  int rc = make_tmap_2d(&tmap_act, L.act, adt, 2, (uint64_t)L.act_rows, (uint64_t)L.K, kBK, kBoxRows,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  // (with fewer rows than one big box no tile uses it; keep the encoding valid)
+  rc = make_tmap_2d(&tmap_act64, L.act, adt, 2, (uint64_t)L.act_rows, (uint64_t)L.K, kBK,
+                    L.act_rows < kBigBoxRows ? kBoxRows : kBigBoxRows, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_tmap_2d(&tmap_w, L.blocks, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)L.E * L.N, (uint64_t)L.K / 2,
-                    kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_32B);
+                    kWRowBytes, kBM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   GemmParams p;
   p.scales = L.scales;
@@ -496,13 +588,24 @@ int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
   p.alpha = L.alpha;
   p.limit = L.limit;
   p.err = L.err;
-  const int smem = GemmSmem::kAlloc;
+  // the token-tile plan used the same rule (moe_tile_rows_max) for these rows
+  const bool small = moe_tile_rows_max(L.act_rows, L.E) <= kMoeTileRowsSmall;
   if (mode == 0) {
-    if (L.f16) launch_variant<0, true>(tmap_act, tmap_w, p, L.grid, smem, stream);
-    else launch_variant<0, false>(tmap_act, tmap_w, p, L.grid, smem, stream);
+    if (small) {
+      if (L.f16) launch_variant<0, true, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      else launch_variant<0, false, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+    } else {
+      if (L.f16) launch_variant<0, true, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      else launch_variant<0, false, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+    }
   } else {
-    if (L.f16) launch_variant<1, true>(tmap_act, tmap_w, p, L.grid, smem, stream);
-    else launch_variant<1, false>(tmap_act, tmap_w, p, L.grid, smem, stream);
+    if (small) {
+      if (L.f16) launch_variant<1, true, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      else launch_variant<1, false, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+    } else {
+      if (L.f16) launch_variant<1, true, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      else launch_variant<1, false, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+    }
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -91,30 +91,20 @@ constexpr int kRTT = 2;   // tokens per thread
 constexpr int kRTE = 8;   // experts per thread
 constexpr int kRKT = 32;  // k per shared-memory stage (multiple of 8)
 
-// bf16 rounding of two fp32 accumulators held as a packed pair.
-template <int kRound>
+// bf16 rounding of two fp32 accumulators held as a packed pair: one cvt per
+// value, whose zero low half leaves float(bf16(v)) in the register.
 __device__ __forceinline__ unsigned long long round_pair_bf16(unsigned long long s) {
-  const uint32_t lo = (uint32_t)s, hi = (uint32_t)(s >> 32);
-  if (kRound == 0) {
-    // one cvt per value; the zero half leaves float(bf16(v)) in the register
-    uint32_t a, b;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(a) : "f"(__uint_as_float(lo)), "f"(0.0f));
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(b) : "f"(__uint_as_float(hi)), "f"(0.0f));
-    return ((unsigned long long)b << 32) | a;
-  } else if (kRound == 1) {
-    // one packed cvt for both values, then split the halves back out
-    uint32_t p;
-    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(__uint_as_float(hi)), "f"(__uint_as_float(lo)));
-    return ((unsigned long long)(p & 0xFFFF0000u) << 32) | (p << 16);
-  } else {
-    // integer round-to-nearest-even on the bit patterns
-    const uint32_t a = (lo + 0x7FFFu + ((lo >> 16) & 1u)) & 0xFFFF0000u;
-    const uint32_t b = (hi + 0x7FFFu + ((hi >> 16) & 1u)) & 0xFFFF0000u;
-    return ((unsigned long long)b << 32) | a;
-  }
+  uint32_t a, b;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(a) : "f"(__uint_as_float((uint32_t)s)), "f"(0.0f));
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(b) : "f"(__uint_as_float((uint32_t)(s >> 32))), "f"(0.0f));
+  return ((unsigned long long)b << 32) | a;
 }
 
-template <int kRound, int kMaxTQ, int kMaxWQ>
+// Above this many tokens the register-tiled kernel (throughput-bound) wins
+// over one thread per chain pair (latency-bound).
+constexpr int64_t kRouterChainMaxTokens = 512;
+
+template <int kMaxTQ, int kMaxWQ>
 __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict__ t, const uint16_t* __restrict__ W,
                                                       const uint16_t* __restrict__ b, int64_t M, int32_t E, int32_t H,
                                                       int32_t block_experts, uint16_t* __restrict__ logits) {
@@ -205,7 +195,7 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
         for (int j = 0; j < kRTE / 2; ++j) {
           unsigned long long sacc = acc[i][j];
           asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(sacc) : "l"(tv[i]), "l"(wv[j]));
-          acc[i][j] = round_pair_bf16<kRound>(sacc);
+          acc[i][j] = round_pair_bf16(sacc);
         }
       }
     }
@@ -227,6 +217,93 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
       }
     }
   }
+}
+
+// Few tokens (decode): the same serial chains, one per (token, expert), but
+// spread over as many threads as there are chains -- the step latency of a
+// chain (one packed FMA + one bf16 rounding), not ALU throughput, is the
+// limit.  A block covers 16 tokens x 16 experts; thread (tok, p) runs the
+// chains of experts p and p + 8 in one packed f32x2 accumulator.  Token and
+// weight rows are staged through shared memory in k chunks with cp.async,
+// double-buffered; the row pitch (kChainK + 8 elements) keeps the 16-byte
+// reads of 8 different rows on distinct banks.
+constexpr int kChainTok = 16, kChainExp = 16, kChainK = 256, kChainPitch = kChainK + 8;
+
+__global__ void __launch_bounds__(128) router_chain_kernel(const uint16_t* __restrict__ t,
+                                                            const uint16_t* __restrict__ W,
+                                                            const uint16_t* __restrict__ b, int64_t M, int32_t E,
+                                                            int32_t H, uint16_t* __restrict__ logits) {
+  __shared__ __align__(16) uint16_t ts[2][kChainTok][kChainPitch];
+  __shared__ __align__(16) uint16_t ws[2][kChainExp][kChainPitch];
+  const int tok = threadIdx.x >> 3, p = threadIdx.x & 7;
+  const int64_t m0 = (int64_t)blockIdx.y * kChainTok;
+  const int32_t e0 = blockIdx.x * kChainExp;
+  auto load = [&](int buf, int32_t k0) {
+    const int32_t kn = min(kChainK, H - k0);
+    const int parts = kn / 8;  // 16-byte pieces per row
+    for (int j = threadIdx.x; j < 2 * 16 * parts; j += 128) {
+      const int which = j / (16 * parts), rem = j % (16 * parts);
+      const int r = rem / parts, q = rem % parts;
+      const uint16_t* src = nullptr;
+      uint16_t* dst;
+      if (which == 0) {
+        dst = &ts[buf][r][q * 8];
+        if (m0 + r < M) src = t + (m0 + r) * H + k0 + q * 8;
+      } else {
+        dst = &ws[buf][r][q * 8];
+        if (e0 + r < E) src = W + (int64_t)(e0 + r) * H + k0 + q * 8;
+      }
+      if (src)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  unsigned long long acc = 0ull;
+  load(0, 0);
+  int buf = 0;
+  for (int32_t k0 = 0; k0 < H; k0 += kChainK, buf ^= 1) {
+    if (k0 + kChainK < H) {
+      load(buf ^ 1, k0 + kChainK);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const int32_t kn = min(kChainK, H - k0);
+    const uint16_t* trow = ts[buf][tok];
+    const uint16_t* wa = ws[buf][p];
+    const uint16_t* wb = ws[buf][p + 8];
+    for (int32_t kk = 0; kk < kn; kk += 8) {
+      const uint4 tv = *(const uint4*)(trow + kk);
+      const uint4 av = *(const uint4*)(wa + kk);
+      const uint4 bv = *(const uint4*)(wb + kk);
+      const uint32_t tw[4] = {tv.x, tv.y, tv.z, tv.w};
+      const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+      const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t tf = h ? (tw[i] & 0xFFFF0000u) : (tw[i] << 16);
+          const uint32_t af = h ? (aw[i] & 0xFFFF0000u) : (aw[i] << 16);
+          const uint32_t bf = h ? (bw[i] & 0xFFFF0000u) : (bw[i] << 16);
+          const unsigned long long tp = ((unsigned long long)tf << 32) | tf;
+          const unsigned long long wp = ((unsigned long long)bf << 32) | af;
+          asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(tp), "l"(wp));
+          acc = round_pair_bf16(acc);
+        }
+      }
+    }
+    __syncthreads();  // the buffer is refilled by the next iteration's load
+  }
+  const int64_t m = m0 + tok;
+  if (m >= M) return;
+  const int32_t ea = e0 + p, eb = e0 + p + 8;
+  if (ea < E)
+    logits[m * E + ea] = f32_to_bf16_bits(__fadd_rn(__uint_as_float((uint32_t)acc), bf16_bits_to_f32(b[ea])));
+  if (eb < E)
+    logits[m * E + eb] =
+        f32_to_bf16_bits(__fadd_rn(__uint_as_float((uint32_t)(acc >> 32)), bf16_bits_to_f32(b[eb])));
 }
 
 // ------------------------------------------------------ top-k softmax --
@@ -292,8 +369,8 @@ __global__ void topk_softmax_kernel(const uint16_t* __restrict__ logits, int64_t
 // Expert-major order of the (token, rank) pairs (the layout of the grouped
 // kernels, model/mlp_optimized.py:118-170): rows of expert e occupy
 // [indptr[e], indptr[e+1]) in ascending token order.  Also builds the token
-// tiles the grouped GEMM walks: an expert with c rows gets
-// ceil(c/kMoeTileMaxRows) tiles of roundup16(ceil(c/tiles)) rows.
+// tiles the grouped GEMM walks: an expert with c rows gets ceil(c/T) tiles of
+// roundup16(ceil(c/tiles)) rows, T = moe_tile_rows_max(all rows, experts).
 // Stage 1 (one block): per-expert counts, exclusive scan, tile plan.
 __global__ void __launch_bounds__(1024) moe_count_scan_kernel(const int32_t* __restrict__ idx, int64_t pairs, int32_t E,
                                                                int32_t* __restrict__ indptr,
@@ -309,12 +386,13 @@ __global__ void __launch_bounds__(1024) moe_count_scan_kernel(const int32_t* __r
   }
   __syncthreads();
   if (threadIdx.x == 0) {
+    const int32_t tmax = moe_tile_rows_max(pairs, E);
     int32_t acc = 0, tacc = 0;
     for (int32_t e = 0; e < E; ++e) {
       const int32_t c = cnt[e];
       indptr[e] = acc;
       tile_ptr[e] = tacc;
-      const int32_t nt = (c + kMoeTileMaxRows - 1) / kMoeTileMaxRows;
+      const int32_t nt = (c + tmax - 1) / tmax;
       const int32_t per = nt ? ((((c + nt - 1) / nt) + 15) & ~15) : 0;
       tile_rows[e] = per;
       acc += c;
@@ -486,10 +564,11 @@ __global__ void weight_ranges_kernel(const uint8_t* __restrict__ s1, int64_t n1,
 __global__ void moe_plan_tiles_kernel(const int32_t* __restrict__ indptr, int32_t E, int32_t* __restrict__ tile_ptr,
                                       int32_t* __restrict__ tile_rows) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const int32_t tmax = moe_tile_rows_max(indptr[E], E);
   int32_t tacc = 0;
   for (int32_t e = 0; e < E; ++e) {
     const int32_t c = indptr[e + 1] - indptr[e];
-    const int32_t nt = (c + kMoeTileMaxRows - 1) / kMoeTileMaxRows;
+    const int32_t nt = (c + tmax - 1) / tmax;
     tile_ptr[e] = tacc;
     tile_rows[e] = nt ? ((((c + nt - 1) / nt) + 15) & ~15) : 0;
     tacc += nt;
@@ -549,27 +628,26 @@ int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, f
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-template <int kRound, int kTQ, int kWQ>
+template <int kTQ, int kWQ>
 static void launch_router_variant(dim3 grid, size_t smem, cudaStream_t s, const uint16_t* t, const uint16_t* W,
                                   const uint16_t* b, int64_t M, int32_t E, int32_t H, int32_t be, uint16_t* logits) {
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(router_kernel<kRound, kTQ, kWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    cudaFuncSetAttribute(router_kernel<kTQ, kWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr = true;
   }
-  router_kernel<kRound, kTQ, kWQ><<<grid, 128, smem, s>>>(t, W, b, M, E, H, be, logits);
+  router_kernel<kTQ, kWQ><<<grid, 128, smem, s>>>(t, W, b, M, E, H, be, logits);
 }
 
-template <int kRound>
-static int launch_router_round(int egroups, dim3 grid, size_t smem, cudaStream_t s, const uint16_t* t,
+static int launch_router_tiles(int egroups, dim3 grid, size_t smem, cudaStream_t s, const uint16_t* t,
                                const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H, int32_t be,
                                uint16_t* logits) {
   // prefetch registers per thread: token tile (btok rows x 4 pieces) and expert tile (be rows x 4 pieces)
   switch (egroups) {
-    case 8: launch_router_variant<kRound, 1, 2>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
-    case 4: launch_router_variant<kRound, 2, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
-    case 2: launch_router_variant<kRound, 4, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
-    case 1: launch_router_variant<kRound, 8, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
+    case 8: launch_router_variant<1, 2>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
+    case 4: launch_router_variant<2, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
+    case 2: launch_router_variant<4, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
+    case 1: launch_router_variant<8, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
     default: return -12;
   }
   return 0;
@@ -579,6 +657,11 @@ int launch_router(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64
                   uint16_t* logits, cudaStream_t s) {
   if (M <= 0) return 0;
   if (E % kRTE != 0 || E > 1024 || H % 8 || ((uintptr_t)t & 15) || ((uintptr_t)W & 15)) return -12;
+  if (M <= kRouterChainMaxTokens) {
+    dim3 grid((unsigned)((E + kChainExp - 1) / kChainExp), (unsigned)((M + kChainTok - 1) / kChainTok));
+    router_chain_kernel<<<grid, 128, 0, s>>>(t, W, b, M, E, H, logits);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
   const int block_experts = E >= 64 ? 64 : E;
   if (E % block_experts) return -12;
   const int egroups = block_experts / kRTE;
@@ -587,15 +670,7 @@ int launch_router(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64
   const size_t smem = (size_t)kRKT * btok * 2 * 4 + (size_t)kRKT * block_experts * 4;
   if (smem > 200 * 1024) return -12;
   dim3 grid((unsigned)((M + btok - 1) / btok), (unsigned)(E / block_experts));
-  static int round_mode = -1;
-  if (round_mode < 0) {
-    const char* env = getenv("GPTOSS_ROUTER_ROUND");
-    round_mode = env ? atoi(env) : 0;
-  }
-  int rc;
-  if (round_mode == 1) rc = launch_router_round<1>(egroups, grid, smem, s, t, W, b, M, E, H, block_experts, logits);
-  else if (round_mode == 2) rc = launch_router_round<2>(egroups, grid, smem, s, t, W, b, M, E, H, block_experts, logits);
-  else rc = launch_router_round<0>(egroups, grid, smem, s, t, W, b, M, E, H, block_experts, logits);
+  const int rc = launch_router_tiles(egroups, grid, smem, s, t, W, b, M, E, H, block_experts, logits);
   if (rc) return rc;
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

@@ -178,9 +178,10 @@ def _events(n):
     return [torch.cuda.Event(enable_timing=True) for _ in range(n)]
 
 
-def profile_moe_stages(blk: "MLPBlock", x: torch.Tensor, repeats: int = 3) -> dict:
+def profile_moe_stages(blk: "MLPBlock", x: torch.Tensor, repeats: int = 3, flush: torch.Tensor | None = None) -> dict:
     """Times each stage of the block (same kernels as forward, called one by
-    one through the C ABI) with CUDA events on the current stream."""
+    one through the C ABI) with CUDA events on the current stream.  `flush`
+    (a device buffer larger than L2) is overwritten before every repeat."""
     x2 = x.reshape(-1, blk.hidden_size).contiguous()
     M = x2.shape[0]
     E, El, k, H, I = blk.num_experts, blk.num_local_experts, blk.experts_per_token, blk.hidden_size, blk.intermediate_size
@@ -203,6 +204,8 @@ def profile_moe_stages(blk: "MLPBlock", x: torch.Tensor, repeats: int = 3) -> di
     names = ["norm", "router", "permute", "gather", "mlp1", "mlp2", "combine"]
     best = None
     for _ in range(repeats):
+        if flush is not None:
+            flush.zero_()
         ev = _events(len(names) + 1)
         ev[0].record()
         _lib.call("gptoss_rms_norm", _ptr(x2), _ptr(blk.norm_weight), M, H, ctypes.c_float(blk.rms_norm_eps), _ptr(t), S)

@@ -177,6 +177,34 @@ def test_forced_routing_multi_tile_and_empty_experts(oracle, params_e8, f16):
     G.tol_check(G.f32(r["out"][rows]), G.f32(out), what="forced output")
 
 
+@pytest.mark.parametrize("f16", [True, False], ids=["f16-path", "bf16-path"])
+def test_forced_routing_small_tiles(oracle, f16):
+    """Decode-sized batch (M*k <= 8E rows) runs the GEMM's small-tile variant:
+    256 tokens all routed to experts 0..3 of 128 -> 8 token tiles of 32 rows
+    per expert, 124 empty experts."""
+    S = synth()
+    p = S.moe_params(128, seed=0)
+    M = 256
+    x = S.activations(M, seed=11)
+    idx = np.tile(np.array([[1, 3, 0, 2]], np.int32), (M, 1))
+    wts = S.bf16_bits(np.tile(np.array([[0.5, 0.25, 0.125, 0.125]], np.float32), (M, 1)))
+    r = G.MoEPieces(p, f16=f16).run(x, routing=(wts, idx))
+    indptr, _, _, _ = oracle.moe_permute(idx, 128)
+    np.testing.assert_array_equal(r["indptr"], indptr)
+    np.testing.assert_array_equal(r["tile_ptr"], [0, 8, 16, 24] + [32] * 125)
+    np.testing.assert_array_equal(r["tile_rows"][:4], [32] * 4)
+    rows = np.array([0, 1, 31, 32, 33, 127, 200, 255])
+    t = oracle.rms_norm(x, p["norm_weight"])
+    h1 = oracle.moe_einsum(t[rows], idx[rows], p["mlp1_weight_blocks"], p["mlp1_weight_scales"], p["mlp1_bias"])
+    y = oracle.swiglu(h1)
+    h2 = oracle.moe_einsum(y, idx[rows], p["mlp2_weight_blocks"], p["mlp2_weight_scales"], p["mlp2_bias"])
+    revm = r["row_of_pair"].reshape(M, 4)
+    G.tol_check(r["y"][revm[rows].ravel()], y.reshape(-1, 2880), what="small-tile mlp1")
+    G.tol_check(r["h2"][revm[rows].ravel()], h2.reshape(-1, 2880), what="small-tile mlp2")
+    _, out = oracle.gating_residual(h2, wts[rows], x[rows])
+    G.tol_check(G.f32(r["out"][rows]), G.f32(out), what="small-tile output")
+
+
 def test_f16_path_disabled_for_out_of_range_scales():
     """A scale code outside 104..140 makes gptoss_moe_weights_prepare clear the
     f16 flag; the exact bf16 path then matches the oracle."""
@@ -244,3 +272,23 @@ def test_rmsnorm_bit_exact_odd_sizes(oracle):
         G.call("gptoss_rms_norm", G.P(xd), G.P(wd), M, 2880, G.ctypes.c_float(1e-5), G.P(out), G.S())
         torch.cuda.synchronize()
         np.testing.assert_array_equal(G.host(out), oracle.rms_norm(x, w))
+
+
+@pytest.mark.parametrize("E", [8, 32, 128])
+def test_router_bit_exact_both_kernels(oracle, E):
+    """Router logits at token counts served by the per-chain kernel (<= 512
+    tokens) and by the register-tiled kernel (> 512), bit-exact."""
+    rng = np.random.default_rng(40 + E)
+    S = synth()
+    Wg = S.bf16_bits(rng.standard_normal((E, 2880)).astype(np.float32) * 0.02)
+    bg = S.bf16_bits(rng.standard_normal(E).astype(np.float32) * 0.1)
+    for M in (1, 17, 512, 513):
+        t = S.bf16_bits(rng.standard_normal((M, 2880)).astype(np.float32))
+        td, wd, bd = G.dev(t), G.dev(Wg), G.dev(bg)
+        logits = torch.empty(M, E, dtype=torch.bfloat16, device="cuda")
+        w = torch.empty(M, 4, dtype=torch.bfloat16, device="cuda")
+        idx = torch.empty(M, 4, dtype=torch.int32, device="cuda")
+        G.call("gptoss_moe_router", G.P(td), G.P(wd), G.P(bd), M, E, 2880, 4, G.P(logits), G.P(w), G.P(idx), None,
+               G.S())
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(G.host(logits), oracle.router(t, Wg, bg), err_msg=f"M={M} E={E}")
