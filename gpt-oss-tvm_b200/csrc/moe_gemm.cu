@@ -18,7 +18,7 @@
 //     the activation operand only.
 //   * The activations (expert-major rows, bf16, K-major) are the "B" operand,
 //     brought into 128-byte-swizzled shared memory by TMA.
-//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 192
+//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 128
 //     token rows, or 32 in the decode variant, K = 16 per instruction)
 //     accumulates fp32 in TMEM.
 //   * Nibbles are streamed by TMA (32-byte swizzle) through an 8-deep ring
@@ -43,36 +43,43 @@ constexpr int kWStageBytes = kBM * kWRowBytes;     // 16 KB (128 rows x 128 B, 1
 constexpr int kMaxGroups = 96;                     // K/32 upper bound (K <= 3072)
 constexpr int kScaleBytes = kBM * kMaxGroups;      // per-tile scale buffer (row stride = G)
 constexpr int kTmemCols = 512;
-constexpr int kASlots = 4;                         // TMEM A slots: slot w is written by warpgroup w only
 constexpr int kDequantWarps = 16;  // 4 warpgroups
 constexpr int kEpiWarp0 = 16;
 constexpr int kActWarp = 20, kMmaWarp = 21, kWWarp = 22;
 
 // Two shapes of the same pipeline.
-//   Large tiles (prefill): up to 192 token rows, 6 activation stages, 3
-//   nibble stages (48 KB) and 2 TMEM A slots (the accumulators take the rest).
+//   Large tiles (prefill): up to 128 token rows, 4 activation stages of 2
+//   chunks (128 KB), 3 nibble stages (48 KB).
 //   Small tiles (decode, few rows per expert): up to 32 token rows, the MMA
 //   is nearly free and the weights must stream at HBM speed: 6 nibble stages
 //   and 6 activation stages of 4 chunks each (96 KB + up to 96 KB in flight
 //   per SM; an activation stream only a few chunks deep would queue behind
-//   the weights in the SM's TMA unit and pace the MMA) and 6 TMEM A slots.
+//   the weights in the SM's TMA unit and pace the MMA).
+// Both: 4 TMEM A slots of 2 chunks, one per dequant warpgroup.  The single
+// MMA-issuing thread waits on one barrier per A stage (the owning warpgroup
+// arrives after its TMEM stores and after the stage's activations landed) and
+// commits twice per A stage at most: its per-chunk overhead, not the tensor
+// pipe, bounds small-N tiles.
 // A nibble stage is one TMA box of 128 weight rows x 128 bytes (4 K chunks):
 // wide rows keep the TMA request rate, not HBM, from bounding the stream.
 template <bool kSmall>
 struct GemmCfg {
   static constexpr int kMaxBN = kSmall ? kMoeTileRowsSmall : kMoeTileMaxRows;
-  static constexpr int kBStages = 6;
-  static constexpr int kBChunks = kSmall ? kWChunks : 1;  // K chunks per activation stage
-  static constexpr int kAChunks = kSmall ? 2 : 1;      // K chunks per TMEM A stage (one warpgroup's round)
+  static constexpr int kBStages = kSmall ? 6 : 4;
+  static constexpr int kBChunks = kSmall ? 4 : 2;      // K chunks per activation stage
+  static constexpr int kAChunks = 2;                   // K chunks per TMEM A stage (one warpgroup's round)
+  // TMEM A slots, a multiple of 4: slot s is written only by warpgroup s % 4
+  static constexpr int kASlots = 4;
   static constexpr int kASlotCols = kAChunks * kBK / 2;  // TMEM columns of an A slot (f16/bf16 pairs)
   static constexpr int kAPerW = kWChunks / kAChunks;    // A stages per nibble stage = its reader warpgroups
-  static constexpr int kWStages = kSmall ? 6 : 3;
+  static constexpr int kWStages = kSmall ? 6 : 4;
+  static_assert(kBChunks % kAChunks == 0 && kWChunks % kAChunks == 0, "A stages nest in both rings");
   static constexpr int kActChunkBytes = kMaxBN * kBK * 2;  // one chunk of the token rows
   static constexpr int kActStageBytes = kBChunks * kActChunkBytes;
   static constexpr int kAccCols = kMaxBN;
   static constexpr int kAColBase = 2 * kAccCols;
   static_assert(kAColBase + kASlots * kASlotCols <= kTmemCols, "TMEM budget");
-  static_assert(kASlots == 4 && kDequantWarps == 16, "one A slot per dequant warpgroup");
+  static_assert(kASlots % 4 == 0 && kDequantWarps == 16, "A slots divide among the four dequant warpgroups");
   // shared memory offsets from the 1024-aligned base
   static constexpr int kAct = 0;
   static constexpr int kW = kAct + kBStages * kActStageBytes;
@@ -80,7 +87,8 @@ struct GemmCfg {
   static constexpr int kBar = kScale + 2 * kScaleBytes;
   static constexpr int kNumBars = 2 * kASlots + 2 * kBStages + 2 * kWStages + 4 + 4;
   static constexpr int kMisc = kBar + kNumBars * 8;
-  static constexpr int kAlloc = kMisc + 64 + 1024;  // + slack for manual 1024 B alignment
+  static constexpr int kEpi = kMisc + 64;        // 4 epilogue warps x (32 tokens x 16 outputs x 2 B)
+  static constexpr int kAlloc = kEpi + 4 * 1024 + 1024;  // + slack for manual 1024 B alignment
   static_assert(kAlloc <= 227 * 1024, "shared memory budget");
 };
 
@@ -106,10 +114,20 @@ struct TileInfo {
 // Tile t -> (expert, first permuted row, rows, first feature row).  A tile
 // plan made for larger tiles than this variant holds is reported and skipped
 // by every role alike.
+// Tiles run in groups of kTileGroup token tiles, feature-tile-major inside a
+// group: the CTAs running at the same time read different token tiles'
+// activations (fewer SMs on the same L2 lines) while a group's activations
+// stay in L2 across its feature tiles and each weight tile is fetched once.
+constexpr int32_t kTileGroup = 8;
+
 template <int kMaxBN>
 __device__ __forceinline__ bool decode_tile(const GemmParams& p, int32_t t, int32_t ftiles, TileInfo& ti) {
-  const int32_t g = t / ftiles;
-  const int32_t f = t - g * ftiles;
+  const int32_t gtotal = __ldg(p.tile_ptr + p.num_experts);
+  const int32_t grp = t / (kTileGroup * ftiles);
+  const int32_t rem = t - grp * (kTileGroup * ftiles);
+  const int32_t gsize = min(kTileGroup, gtotal - grp * kTileGroup);
+  const int32_t f = rem / gsize;
+  const int32_t g = grp * kTileGroup + (rem - f * gsize);
   int32_t lo = 0, hi = p.num_experts;  // find e with tile_ptr[e] <= g < tile_ptr[e+1]
   while (hi - lo > 1) {
     int32_t mid = (lo + hi) >> 1;
@@ -204,9 +222,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* w_s = smem + C::kW;
   uint8_t* sc_s = smem + C::kScale;
   uint64_t* bars = (uint64_t*)(smem + C::kBar);
-  uint64_t* full_bar = bars;                       // [kASlots] TMEM A slot written: the owning warpgroup
-  uint64_t* empty_bar = full_bar + kASlots;        // [kASlots] MMA commit
-  uint64_t* bfull_bar = empty_bar + kASlots;       // [kBStages] activation TMA tx
+  uint64_t* full_bar = bars;                       // [kASlots] A slot written and its activations landed
+  uint64_t* empty_bar = full_bar + C::kASlots;     // [kASlots] MMA commit
+  uint64_t* bfull_bar = empty_bar + C::kASlots;    // [kBStages] activation TMA tx
   uint64_t* bempty_bar = bfull_bar + C::kBStages;  // [kBStages] MMA commit
   uint64_t* wfull_bar = bempty_bar + C::kBStages;  // [kWStages] nibble TMA tx
   uint64_t* wempty_bar = wfull_bar + C::kWStages;  // [kWStages] the dequant warps that read it
@@ -228,7 +246,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int32_t total_tiles = __ldg(p.tile_ptr + p.num_experts) * ftiles;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kASlots; ++s) {
+    for (int s = 0; s < C::kASlots; ++s) {
       mbar_init(&full_bar[s], 4);
       mbar_init(&empty_bar[s], 1);
     }
@@ -325,7 +343,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (elect_one()) {
       // slot / activation-stage cursors run on across tiles, in step with the
       // dequant warpgroups (A stages) and the activation producer (stages)
-      uint32_t s = 0, ph = 0, sb = 0, phb = 0, tl = 0;
+      uint32_t s = 0, ph = 0, sb = 0, tl = 0;
       const uint64_t bdesc0 = make_sdesc_sw128(smem_u32(act_s));
       for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
         TileInfo ti;
@@ -339,11 +357,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         bool ok = true;
         int32_t sub = 0, q = 0;
         for (int32_t c = 0; c < nchunks; ++c) {
-          if (q == 0) {
-            if (!mbar_wait(&bfull_bar[sb], phb, p.err, kErrTimeoutFull)) { ok = false; break; }
-            tc_fence_after();
-          }
           if (sub == 0) {
+            // the owning warpgroup arrives once its weights are in TMEM and the
+            // activation stage holding this A stage has landed
             if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) { ok = false; break; }
             tc_fence_after();
           }
@@ -354,13 +370,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (++sub == C::kAChunks || last) {
             tc_commit(&empty_bar[s]);
             sub = 0;
-            s = (s + 1) & (kASlots - 1);
-            ph ^= s == 0 ? 1u : 0u;
+            if (++s == (uint32_t)C::kASlots) { s = 0; ph ^= 1u; }
           }
           if (++q == C::kBChunks || last) {
             tc_commit(&bempty_bar[sb]);
             q = 0;
-            if (++sb == C::kBStages) { sb = 0; phb ^= 1u; }
+            if (++sb == C::kBStages) sb = 0;
           }
         }
         if (!ok) { *abort_s = 1; break; }
@@ -372,8 +387,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // --------------------------------------------- dequant: weights -> TMEM
     // The A stages of all tiles are numbered consecutively (gai); stage gai
     // (kAChunks chunks, both MXFP4 groups of each) is decoded by warpgroup
-    // gai % 4 into TMEM slot gai % 4, so each slot has a single writer and its
-    // empty/full phases advance in that warpgroup's program order.  A nibble
+    // gai % 4 into TMEM slot gai % kASlots, so each slot has a single writer
+    // and its empty/full phases advance in that warpgroup's program order.  A nibble
     // stage holds kAPerW A stages and is read (and released) by their
     // kAPerW warpgroups: all four for large tiles; for small tiles two, the
     // two pairs alternating stages so that one pair's barrier waits overlap
@@ -382,8 +397,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int row = (warp & 3) * 32 + lane;     // weight row within the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t swz = (uint32_t)(row & 7);   // 128-byte swizzle of the nibble rows
-    const uint32_t ta = tmem_base + lane_base + C::kAColBase + (uint32_t)wgi * C::kASlotCols;
-    uint32_t ait = 0, wit = 0, tl = 0, uses = 0;
+    uint32_t ait = 0, wit = 0, bit = 0, tl = 0;
     for (int32_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       TileInfo ti;
       if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
@@ -411,29 +425,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (lane == 0) mbar_arrive(&wempty_bar[ws]);
         const int32_t c0 = (j * C::kAPerW + r) * C::kAChunks;
         if (c0 >= nchunks) continue;            // no chunk here (short last stage)
-        // slot wgi, use number `uses`: wait until the MMA has consumed the previous use
-        ok = mbar_wait(&empty_bar[wgi], (uses & 1u) ^ 1u, p.err, kErrTimeoutEmpty);
+        // decode the first chunk while the MMA may still be reading the slot
+        uint32_t v0[16], v1[16];
+        decode_group<kF16>(nb[0], srow[2 * c0], row_ok, v0);
+        decode_group<kF16>(nb[1], srow[2 * c0 + 1], row_ok, v1);
+        // wait until the MMA has consumed the slot's previous A stage
+        const uint32_t gai = ait + (uint32_t)(j * C::kAPerW + r);
+        const uint32_t slot = gai % C::kASlots, sph2 = (gai / C::kASlots) & 1u;
+        ok = mbar_wait(&empty_bar[slot], sph2 ^ 1u, p.err, kErrTimeoutEmpty);
         if (!ok) break;
-        ++uses;
+        const uint32_t ta = tmem_base + lane_base + C::kAColBase + slot * C::kASlotCols;
         __syncwarp();
         tc_fence_after();
+        tmem_st_x16(ta, v0);
+        tmem_st_x16(ta + 16, v1);
 #pragma unroll
-        for (int u = 0; u < C::kAChunks; ++u) {
+        for (int u = 1; u < C::kAChunks; ++u) {
           const int32_t c = c0 + u;
           if (c >= nchunks) break;
-          uint32_t v[16];
-          decode_group<kF16>(nb[2 * u], srow[2 * c], row_ok, v);
-          tmem_st_x16(ta + u * 32, v);
-          decode_group<kF16>(nb[2 * u + 1], srow[2 * c + 1], row_ok, v);
-          tmem_st_x16(ta + u * 32 + 16, v);
+          decode_group<kF16>(nb[2 * u], srow[2 * c], row_ok, v0);
+          decode_group<kF16>(nb[2 * u + 1], srow[2 * c + 1], row_ok, v1);
+          tmem_st_x16(ta + u * 32, v0);
+          tmem_st_x16(ta + u * 32 + 16, v1);
         }
         tmem_st_wait();
         tc_fence_before();
+        {
+          // the activation stage that holds chunks c0 .. c0 + kAChunks - 1
+          const uint32_t bsi = bit + (uint32_t)(c0 / C::kBChunks);
+          ok = mbar_wait(&bfull_bar[bsi % C::kBStages], (bsi / C::kBStages) & 1u, p.err, kErrTimeoutFull);
+          if (!ok) break;
+        }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full_bar[wgi]);
+        if (lane == 0) mbar_arrive(&full_bar[slot]);
       }
       ait += (uint32_t)nastages;
       wit += (uint32_t)nstages;
+      bit += (uint32_t)((nchunks + C::kBChunks - 1) / C::kBChunks);
       __syncwarp();
       if (lane == 0) mbar_arrive(&scempty_bar[sb]);
       if (!ok) { *abort_s = 1; break; }
@@ -462,10 +490,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_ld_x32(tmem_base + lane_base + ab * C::kAccCols + (uint32_t)c0, v);
         tmem_ld_wait();
         if (kMode == 0) {
-          // lane pair (2j, 2j+1) holds the glu / linear rows of output column j:
-          // the even lane finishes tokens c0..c0+15, the odd lane c0+16..c0+31
+          // lane pair (2j, 2j+1) holds the glu / linear rows of output feature
+          // j: the even lane finishes tokens c0..c0+15, the odd lane c0+16..31.
+          // The 32 x 16 outputs go through this warp's shared tile
+          // [token][feature] and leave as 16-byte rows of 8 features.
           const bool odd = lane & 1;
           uint16_t* out = (uint16_t*)p.out;
+          uint16_t* tile = (uint16_t*)(smem + C::kEpi) + q * 512;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float mine_lo = __uint_as_float(v[i]) + bias;
@@ -474,15 +505,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
             const float gl = odd ? recv : mine_lo;
             const float li = odd ? mine_hi : recv;
-            const int32_t col = c0 + i + (odd ? 16 : 0);
             const float g = fminf(gl, p.limit);
             const float l = fmaxf(fminf(li, p.limit), -p.limit);
-            const float sg = 1.0f / (1.0f + expf(-(p.alpha * g)));
-            const float y = (g * sg) * (l + 1.0f);
-            if (row_ok && col < ti.nrows)
-              out[(size_t)(ti.row0 + col) * p.ldo + (frow >> 1)] =
-                  kF16 ? __half_as_ushort(__float2half_rn(y)) : f32_to_bf16_bits(y);
+            // g * sigmoid(alpha * g); a huge denominator gives 0, the limit
+            const float gs = __fdividef(g, 1.0f + __expf(-(p.alpha * g)));
+            const float y = gs * (l + 1.0f);
+            const int tok = i + (odd ? 16 : 0);
+            tile[tok * 16 + (lane >> 1)] = kF16 ? __half_as_ushort(__float2half_rn(y)) : f32_to_bf16_bits(y);
           }
+          __syncwarp();
+          const bool warp_rows_ok = ti.f0 + q * 32 + 32 <= p.N;
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const int tok = lane, h = k ^ ((lane >> 2) & 1);  // alternate halves: no bank conflicts
+            const int32_t col = c0 + tok;
+            const uint4 val = *(const uint4*)(tile + tok * 16 + h * 8);
+            const int32_t f = (ti.f0 >> 1) + q * 16 + h * 8;  // first output feature of the 8
+            if (col < ti.nrows) {
+              uint16_t* dst = out + (size_t)(ti.row0 + col) * p.ldo + f;
+              if (warp_rows_ok) {
+                *(uint4*)dst = val;
+              } else {
+                const uint16_t* e = (const uint16_t*)&val;
+                for (int u = 0; u < 8; ++u)
+                  if (2 * (f + u) < p.N) dst[u] = e[u];
+              }
+            }
+          }
+          __syncwarp();
         } else {
           float* out = (float*)p.out;
 #pragma unroll
