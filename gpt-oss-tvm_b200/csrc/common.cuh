@@ -30,9 +30,9 @@ enum DeviceError : uint32_t {
 
 // Token rows of one grouped-GEMM tile (the MMA N dimension).  With few rows
 // per expert (decode) the tiles are at most 32 rows and the GEMM runs its
-// weight-streaming variant; otherwise at most 128.  The permutation plans its
+// weight-streaming variant; otherwise at most 192.  The permutation plans its
 // token tiles with the same rule as the GEMM launch.
-constexpr int kMoeTileMaxRows = 128;
+constexpr int kMoeTileMaxRows = 192;
 constexpr int kMoeTileRowsSmall = 32;
 __host__ __device__ __forceinline__ int moe_tile_rows_max(int64_t rows, int32_t num_experts) {
   return rows <= 8 * (int64_t)num_experts ? kMoeTileRowsSmall : kMoeTileMaxRows;

@@ -18,7 +18,7 @@
 //     the activation operand only.
 //   * The activations (expert-major rows, bf16, K-major) are the "B" operand,
 //     brought into 128-byte-swizzled shared memory by TMA.
-//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 128
+//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 192
 //     token rows, or 32 in the decode variant, K = 16 per instruction)
 //     accumulates fp32 in TMEM.
 //   * Nibbles are streamed by TMA (32-byte swizzle) through an 8-deep ring
@@ -48,14 +48,16 @@ constexpr int kEpiWarp0 = 16;
 constexpr int kActWarp = 20, kMmaWarp = 21, kWWarp = 22;
 
 // Two shapes of the same pipeline.
-//   Large tiles (prefill): up to 128 token rows, 4 activation stages of 2
-//   chunks (128 KB), 3 nibble stages (48 KB).
+//   Large tiles (prefill): up to 192 token rows, 6 one-chunk activation
+//   stages (144 KB), 3 nibble stages (48 KB), 4 one-chunk TMEM A slots (the
+//   two 192-column accumulators take the rest of TMEM).
 //   Small tiles (decode, few rows per expert): up to 32 token rows, the MMA
 //   is nearly free and the weights must stream at HBM speed: 6 nibble stages
 //   and 6 activation stages of 4 chunks each (96 KB + up to 96 KB in flight
 //   per SM; an activation stream only a few chunks deep would queue behind
 //   the weights in the SM's TMA unit and pace the MMA).
-// Both: 4 TMEM A slots of 2 chunks, one per dequant warpgroup.  The single
+// Small tiles use 4 TMEM A slots of 2 chunks; one slot per dequant warpgroup
+// in both variants.  The single
 // MMA-issuing thread waits on one barrier per A stage (the owning warpgroup
 // arrives after its TMEM stores and after the stage's activations landed) and
 // commits twice per A stage at most: its per-chunk overhead, not the tensor
@@ -65,14 +67,14 @@ constexpr int kActWarp = 20, kMmaWarp = 21, kWWarp = 22;
 template <bool kSmall>
 struct GemmCfg {
   static constexpr int kMaxBN = kSmall ? kMoeTileRowsSmall : kMoeTileMaxRows;
-  static constexpr int kBStages = kSmall ? 6 : 4;
-  static constexpr int kBChunks = kSmall ? 4 : 2;      // K chunks per activation stage
-  static constexpr int kAChunks = 2;                   // K chunks per TMEM A stage (one warpgroup's round)
+  static constexpr int kBStages = 6;
+  static constexpr int kBChunks = kSmall ? 4 : 1;      // K chunks per activation stage
+  static constexpr int kAChunks = kSmall ? 2 : 1;      // K chunks per TMEM A stage (one warpgroup's round)
   // TMEM A slots, a multiple of 4: slot s is written only by warpgroup s % 4
   static constexpr int kASlots = 4;
   static constexpr int kASlotCols = kAChunks * kBK / 2;  // TMEM columns of an A slot (f16/bf16 pairs)
   static constexpr int kAPerW = kWChunks / kAChunks;    // A stages per nibble stage = its reader warpgroups
-  static constexpr int kWStages = kSmall ? 6 : 4;
+  static constexpr int kWStages = kSmall ? 6 : 3;
   static_assert(kBChunks % kAChunks == 0 && kWChunks % kAChunks == 0, "A stages nest in both rings");
   static constexpr int kActChunkBytes = kMaxBN * kBK * 2;  // one chunk of the token rows
   static constexpr int kActStageBytes = kBChunks * kActChunkBytes;

@@ -138,7 +138,7 @@ def test_config3_scale_routing_bit_exact_and_sampled_experts(oracle):
     np.testing.assert_array_equal(r["weights"], w)
     _check_permutation(oracle, r, 128)
     counts = np.diff(r["indptr"])
-    assert counts.max() > 128, "expected some expert with more than one token tile"
+    assert counts.max() > 192, "expected some expert with more than one token tile"
     rows = np.sort(np.random.default_rng(3).choice(M, 12, replace=False))
     # include a token of the most loaded expert
     e_max = int(np.argmax(counts))
@@ -152,7 +152,7 @@ def test_config3_scale_routing_bit_exact_and_sampled_experts(oracle):
 
 @pytest.mark.parametrize("f16", [True, False], ids=["f16-path", "bf16-path"])
 def test_forced_routing_multi_tile_and_empty_experts(oracle, params_e8, f16):
-    """Every token routed to experts 0..3 (600 rows each -> 5 token tiles per
+    """Every token routed to experts 0..3 (600 rows each -> 4 token tiles per
     expert, 4 empty experts)."""
     M = 600
     x = synth().activations(M, seed=9)
@@ -161,7 +161,7 @@ def test_forced_routing_multi_tile_and_empty_experts(oracle, params_e8, f16):
     r = G.MoEPieces(params_e8, f16=f16).run(x, routing=(wts, idx))
     indptr, tok, rev, _ = oracle.moe_permute(idx, 8)
     np.testing.assert_array_equal(r["indptr"], indptr)
-    nt = -(-M // 128)  # token tiles of at most 128 rows per expert
+    nt = -(-M // 192)  # token tiles of at most 192 rows per expert
     np.testing.assert_array_equal(r["tile_ptr"], [0, nt, 2 * nt, 3 * nt] + [4 * nt] * 5)
     rows = np.array([0, 1, 255, 256, 257, 511, 512, 599])
     t = oracle.rms_norm(x, params_e8["norm_weight"])
