@@ -43,7 +43,7 @@ METRIC = "MoE-layer tokens/s (gpt-oss-120b MoE layer, 8192-token prefill)"
 FP4_DENSE_PEAK_TFLOPS = 9000.0  # nominal dense e2m1 tensor peak of one B200
 # DRAM bytes (read + write) of one gate/up GEMM launch at the 8192-token workload, from the
 # ncu capture summarised in profiles/moe_gemm_config3_prefill.md
-MLP1_DRAM_TRAFFIC_BYTES = 1.319099e9 + 0.184780e9
+MLP1_DRAM_TRAFFIC_BYTES = 1.325005e9 + 0.183311e9
 
 
 def measured_peaks():
@@ -263,6 +263,7 @@ def run_b200(args):
         }
         if args.decode and world == 1:
             line["decode"] = {name: decode_bench(dev, E, M, 20, peaks) for name, (E, M) in DECODE_CASES.items()}
+            line["attention"] = attention_bench(dev, peaks)
         if args.cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args)
         print(json.dumps(line), flush=True)
@@ -377,6 +378,79 @@ def decode_bench(dev, E, M, steps, peaks):
             "hbm_frac": round(gbs / float(peaks.get("hbm_gbs", 6650.0)), 4),
             "l2": "flushed before every step (256 MB write)", "cuda_graph": True,
             "stages_ms": stages, "stages_note": "kernels launched one by one (not graph-replayed), L2 flushed"}
+
+
+def attention_bench(dev, peaks, iters=10):
+    """Attention with sinks, gpt-oss config 1: prefill of
+    4096 tokens on a full-causal and a 128-window layer, and decode of one token
+    for 32 sequences over 8192 cached keys (full layer).  Inputs are bf16 N(0,1)
+    resident on the device; CUDA events around `iters` back-to-back calls, the
+    256 MB L2 flush before each call.  FLOPs (full prefill) = 4 x (S^2/2) x 64 x 64
+    heads; bytes (windowed prefill) = q+k+v+o; bytes (decode) = K+V of the 32 caches."""
+    import torch
+    lib = importlib.import_module("gpt-oss-tvm_b200._lib")
+    g = torch_gen(dev, 21)
+    S, HQ, HKV, D = 4096, 64, 8, 64
+    P = lambda a: ctypes.c_void_p(a.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    sinks = torch.randn(HQ, generator=g, device=dev).to(torch.bfloat16)
+
+    def timed(fn):
+        times = []
+        for i in range(iters + 2):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= 2:
+                times.append(e0.elapsed_time(e1))
+        return statistics.median(times)
+
+    out = {}
+    q = torch.randn(S, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(S, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(S, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    lse = torch.empty(S, HQ, dtype=torch.float32, device=dev)
+    for window in (0, 128):
+        ms = timed(lambda: lib.call("gptoss_attn_prefill", P(q), P(k), P(v), P(sinks), S, S, HQ, HKV, D, window,
+                                    ctypes.c_float(0.125), P(o), P(lse), stream))
+        if window == 0:
+            flops = 4.0 * (S * S / 2) * D * HQ
+            tf = flops / (ms / 1e3) / 1e12
+            out["prefill 4096, full causal layer"] = {
+                "ms": round(ms, 4), "tflops": round(tf, 1), "peak_tflops": peaks.get("bf16_tflops"),
+                "frac": round(tf / float(peaks.get("bf16_tflops", 1590.0)), 4),
+                "kernel": "attn_prefill_kernel (mma.sync m16n8k16 bf16, fp32 softmax)"}
+        else:
+            nbytes = S * (HQ + 2 * HKV + HQ) * D * 2
+            gbs = nbytes / (ms / 1e3) / 1e9
+            out["prefill 4096, window 128 layer"] = {
+                "ms": round(ms, 4), "bytes": nbytes, "achieved_gbs": round(gbs, 1),
+                "hbm_frac": round(gbs / float(peaks.get("hbm_gbs", 6650.0)), 4)}
+    del q, k, v, o, lse
+    B, L = 32, 8192
+    qd = torch.randn(B, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+    kc = torch.randn(B, L, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(B, L, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+    kv_len = torch.full((B,), L, dtype=torch.int32, device=dev)
+    od = torch.empty_like(qd)
+    lsed = torch.empty(B, HQ, dtype=torch.float32, device=dev)
+    nb = int(lib.load().gptoss_attn_decode_scratch_bytes(B, HQ, L, 0))
+    scratch = torch.empty(max(nb // 4, 1), dtype=torch.float32, device=dev)
+    ms = timed(lambda: lib.call("gptoss_attn_decode", P(qd), P(kc), P(vc), P(kv_len), B, L, HQ, HKV, D, 0,
+                                ctypes.c_float(0.125), P(sinks), P(scratch), nb, P(od), P(lsed), stream))
+    nbytes = 2 * B * L * HKV * D * 2
+    gbs = nbytes / (ms / 1e3) / 1e9
+    out["decode B=32 x KV 8192, full layer"] = {
+        "ms": round(ms, 4), "bytes": nbytes, "achieved_gbs": round(gbs, 1),
+        "hbm_frac": round(gbs / float(peaks.get("hbm_gbs", 6650.0)), 4),
+        "kernel": "attn_decode_kernel (split-KV, 8 GQA heads per mma) + merge"}
+    out["note"] = "L2 flushed (256 MB write) before every call; inputs bf16 N(0,1) on the device"
+    return out
 
 
 def cpu_baseline(args):

@@ -116,20 +116,13 @@ struct TileInfo {
 // Tile t -> (expert, first permuted row, rows, first feature row).  A tile
 // plan made for larger tiles than this variant holds is reported and skipped
 // by every role alike.
-// Tiles run in groups of kTileGroup token tiles, feature-tile-major inside a
-// group: the CTAs running at the same time read different token tiles'
-// activations (fewer SMs on the same L2 lines) while a group's activations
-// stay in L2 across its feature tiles and each weight tile is fetched once.
-constexpr int32_t kTileGroup = 8;
-
+// Token-tile-major order: the CTAs running at the same time share one token
+// tile's activations (L2 hits) and an expert's weight tiles are reused by its
+// token tiles within a short window (DRAM reads close to the algorithmic ones).
 template <int kMaxBN>
 __device__ __forceinline__ bool decode_tile(const GemmParams& p, int32_t t, int32_t ftiles, TileInfo& ti) {
-  const int32_t gtotal = __ldg(p.tile_ptr + p.num_experts);
-  const int32_t grp = t / (kTileGroup * ftiles);
-  const int32_t rem = t - grp * (kTileGroup * ftiles);
-  const int32_t gsize = min(kTileGroup, gtotal - grp * kTileGroup);
-  const int32_t f = rem / gsize;
-  const int32_t g = grp * kTileGroup + (rem - f * gsize);
+  const int32_t g = t / ftiles;
+  const int32_t f = t - g * ftiles;
   int32_t lo = 0, hi = p.num_experts;  // find e with tile_ptr[e] <= g < tile_ptr[e+1]
   while (hi - lo > 1) {
     int32_t mid = (lo + hi) >> 1;
