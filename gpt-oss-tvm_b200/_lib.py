@@ -51,6 +51,7 @@ SIGNATURES = {
     "gptoss_moe_mlp2": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P]),
     "gptoss_moe_weights_prepare": (ctypes.c_int, [ctypes.POINTER(gptoss_moe_weights), _P]),
     "gptoss_moe_combine": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P]),
+    "gptoss_moe_combine_bf16": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P]),
     "gptoss_mxfp4_dequant": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _P]),
     "gptoss_moe_forward_noalloc": (ctypes.c_int, [_P, _I64, ctypes.POINTER(gptoss_moe_weights), _P, _P]),
     "gptoss_yarn_inv_freq": (ctypes.c_int, [_I32, _F, _F, _F, _F, _I32, _P, _P]),

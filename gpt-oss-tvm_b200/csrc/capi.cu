@@ -179,6 +179,13 @@ int gptoss_moe_combine(const float* h2, const int32_t* row_of_pair, const uint16
                       "combine");
 }
 
+int gptoss_moe_combine_bf16(const uint16_t* h2, const int32_t* row_of_pair, const uint16_t* topk_weights,
+                            const uint16_t* x, int64_t M, int32_t K, int32_t H, uint16_t* out, void* stream) {
+  if (M < 0 || K < 1 || K > 8 || H <= 0 || H % 4) return fail(-1, "gptoss_moe_combine_bf16: bad shape");
+  return check_launch(launch_combine_bf16(h2, row_of_pair, topk_weights, x, M, K, H, out, GPTOSS_STREAM(stream)),
+                      "combine_bf16");
+}
+
 int gptoss_mxfp4_dequant(const uint8_t* blocks, const uint8_t* scales, int64_t rows, int32_t groups,
                          uint16_t* out, void* stream) {
   if (rows < 0 || groups <= 0) return fail(-1, "gptoss_mxfp4_dequant: bad shape");
@@ -195,7 +202,7 @@ int gptoss_moe_plan_tiles(const int32_t* indptr, int32_t E, int32_t* tile_ptr, i
 int gptoss_moe_segment_copy(const void* src, void* dst, const int32_t* counts, int32_t num_ranks,
                             int32_t local_experts, int64_t row_bytes, int32_t direction, int32_t* indptr_local,
                             void* stream) {
-  if (num_ranks <= 0 || local_experts <= 0 || row_bytes <= 0 || row_bytes % 16 || (direction != 0 && direction != 1))
+  if (num_ranks <= 0 || local_experts <= 0 || row_bytes <= 0 || row_bytes % 16 || direction < 0 || direction > 2)
     return fail(-1, "gptoss_moe_segment_copy: bad arguments");
   if (local_experts + 1 > 256 && indptr_local) return fail(-1, "gptoss_moe_segment_copy: at most 255 local experts");
   return check_launch(launch_segment_copy(src, dst, counts, num_ranks, local_experts, row_bytes, direction,

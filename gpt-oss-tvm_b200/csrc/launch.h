@@ -37,6 +37,8 @@ int launch_combine(const float*, const int32_t*, const uint16_t*, const uint16_t
                    uint16_t*, cudaStream_t);
 int launch_mxfp4_dequant(const uint8_t*, const uint8_t*, int64_t, uint16_t*, cudaStream_t);
 int launch_plan_tiles(const int32_t*, int32_t, int32_t*, int32_t*, cudaStream_t);
+int launch_combine_bf16(const uint16_t* h2, const int32_t* row_of_pair, const uint16_t* w, const uint16_t* x,
+                        int64_t M, int32_t K, int32_t H, uint16_t* out, cudaStream_t s);
 int launch_segment_copy(const void*, void*, const int32_t*, int32_t, int32_t, int64_t, int32_t, int32_t*,
                         cudaStream_t);
 int launch_weight_ranges(const uint8_t* s1, int64_t n1, const uint8_t* s2, int64_t n2, const uint16_t* norm_w,

@@ -473,12 +473,15 @@ __global__ void gather_rows_kernel(const uint16_t* __restrict__ t, const int32_t
 // with the serial fp32 sum over r of run_gating (model/mlp.py:328-369) and
 // the residual of model/mlp.py:399-402.  One block per token, 4 columns per
 // thread (16-byte loads of the fp32 expert rows).
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ h2, const int32_t* __restrict__ row_of_pair,
+// TIn = float: expert outputs in fp32 (the reference's arithmetic); uint16_t:
+// expert outputs already rounded to bf16 (the expert-parallel return path).
+template <typename TIn>
+__global__ void __launch_bounds__(256) combine_kernel(const TIn* __restrict__ h2, const int32_t* __restrict__ row_of_pair,
                                                       const uint16_t* __restrict__ w, const uint16_t* __restrict__ x,
                                                       int64_t M, int32_t K, int32_t H, uint16_t* __restrict__ out) {
   const int64_t m = blockIdx.x;
   if (m >= M) return;
-  const float* rows[8];
+  const TIn* rows[8];
   float wr[8];
   for (int32_t r = 0; r < K; ++r) {
     rows[r] = h2 + (int64_t)__ldg(row_of_pair + m * K + r) * H;
@@ -487,7 +490,14 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
   for (int32_t c4 = threadIdx.x; c4 < H / 4; c4 += blockDim.x) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int32_t r = 0; r < K; ++r) {
-      const float4 v = __ldg((const float4*)rows[r] + c4);
+      float4 v;
+      if constexpr (sizeof(TIn) == 4) {
+        v = __ldg((const float4*)rows[r] + c4);
+      } else {
+        const uint2 b = __ldg((const uint2*)rows[r] + c4);
+        v = make_float4(__uint_as_float(b.x << 16), __uint_as_float(b.x & 0xFFFF0000u), __uint_as_float(b.y << 16),
+                        __uint_as_float(b.y & 0xFFFF0000u));
+      }
       acc[0] = __fadd_rn(acc[0], __fmul_rn(v.x, wr[r]));
       acc[1] = __fadd_rn(acc[1], __fmul_rn(v.y, wr[r]));
       acc[2] = __fadd_rn(acc[2], __fmul_rn(v.z, wr[r]));
@@ -604,6 +614,18 @@ __global__ void segment_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __
   const int64_t b = dir == 0 ? dst_off : src_off;  // write position
   const int64_t vec = row_bytes / 16;
   const uint4* in = (const uint4*)(src + a * row_bytes);
+  if (dir == 2) {
+    // fp32 rows of row_bytes -> bf16 rows of row_bytes / 2 (round to nearest even)
+    uint2* out = (uint2*)(dst + b * (row_bytes / 2));
+    for (int64_t i = threadIdx.x; i < rows * vec; i += blockDim.x) {
+      const uint4 v = in[i];
+      uint2 o;
+      o.x = (uint32_t)f32_to_bf16_bits(__uint_as_float(v.x)) | ((uint32_t)f32_to_bf16_bits(__uint_as_float(v.y)) << 16);
+      o.y = (uint32_t)f32_to_bf16_bits(__uint_as_float(v.z)) | ((uint32_t)f32_to_bf16_bits(__uint_as_float(v.w)) << 16);
+      out[i] = o;
+    }
+    return;
+  }
   uint4* out = (uint4*)(dst + b * row_bytes);
   for (int64_t i = threadIdx.x; i < rows * vec; i += blockDim.x) out[i] = in[i];
 }
@@ -707,7 +729,15 @@ int launch_combine(const float* h2, const int32_t* row_of_pair, const uint16_t* 
   if (M <= 0) return 0;
   if (H % 4 || K > 8) return -12;
   const int64_t blocks = M;
-  combine_kernel<<<(unsigned)blocks, 256, 0, s>>>(h2, row_of_pair, w, x, M, K, H, out);
+  combine_kernel<float><<<(unsigned)blocks, 256, 0, s>>>(h2, row_of_pair, w, x, M, K, H, out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int launch_combine_bf16(const uint16_t* h2, const int32_t* row_of_pair, const uint16_t* w, const uint16_t* x,
+                        int64_t M, int32_t K, int32_t H, uint16_t* out, cudaStream_t s) {
+  if (M <= 0) return 0;
+  if (H % 4 || K > 8) return -12;
+  combine_kernel<uint16_t><<<(unsigned)M, 256, 0, s>>>(h2, row_of_pair, w, x, M, K, H, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

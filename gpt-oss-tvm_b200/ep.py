@@ -12,8 +12,10 @@ over NCCL) owns ``num_experts / world`` experts and routes its own tokens:
   5. reorder of the received rows from source-major to expert-major
      (gptoss_moe_segment_copy), tile plan, grouped MXFP4 GEMMs (mlp1 + SwiGLU,
      mlp2) on the local experts;
-  6. reorder back to source-major, one NCCL all-to-all-v of the fp32 expert
-     outputs back to the owning ranks;
+  6. reorder back to source-major, one NCCL all-to-all-v of the expert
+     outputs back to the owning ranks -- rounded to bf16 on the way (half the
+     bytes; within the block's tolerance) unless ``exact_return`` keeps them
+     fp32, which makes the result bit-equal to the single-GPU block;
   7. weighted combine + residual on the owning rank.
 
 Steps 1-2, 5 and 7 run in libgptoss_b200.so; the exchanges are plain NCCL
@@ -42,9 +44,10 @@ def _stream():
 class CudaBackend:
     """Device steps of the expert-parallel MoE block, through the C ABI."""
 
-    def __init__(self, blk, max_tokens: int, world: int):
+    def __init__(self, blk, max_tokens: int, world: int, exact_return: bool = False):
         self.blk = blk
         self.world = world
+        self.exact_return = exact_return
         E, El, k, H, I = blk.num_experts, blk.num_local_experts, blk.experts_per_token, blk.hidden_size, \
             blk.intermediate_size
         dev = blk.device
@@ -69,7 +72,8 @@ class CudaBackend:
         self.err = torch.zeros(4, **i32)
         self.f16 = 1 if blk.f16_path else 0  # rows travel in the GEMM's activation type
         self._recv_cap = 0
-        self.h2_back = torch.empty(R, H, dtype=torch.float32, device=dev)
+        self.back_dtype = torch.float32 if exact_return else torch.bfloat16
+        self.h2_back = torch.empty(R, H, dtype=self.back_dtype, device=dev)
 
     def _ensure_recv(self, rows: int):
         if rows > self._recv_cap:
@@ -79,7 +83,7 @@ class CudaBackend:
             self.act = torch.empty(cap, H, dtype=torch.bfloat16, device=dev)
             self.y = torch.empty(cap, I, dtype=torch.bfloat16, device=dev)
             self.h2_local = torch.empty(cap, H, dtype=torch.float32, device=dev)
-            self.h2_src = torch.empty(cap, H, dtype=torch.float32, device=dev)
+            self.h2_src = torch.empty(cap, H, dtype=self.back_dtype, device=dev)
             self._recv_cap = cap
 
     # -- step 1-2
@@ -115,7 +119,7 @@ class CudaBackend:
                   _ptr(self.tile_rows), El, H, I, _ptr(blk.mlp2_weight_blocks), _ptr(blk.mlp2_weight_scales),
                   _ptr(blk.mlp2_bias), self.f16, _ptr(self.h2_local), _ptr(self.err), S)
         _lib.call("gptoss_moe_segment_copy", _ptr(self.h2_local), _ptr(self.h2_src), _ptr(recv_counts), self.world, El,
-                  H * 4, 1, None, S)
+                  H * 4, 1 if self.exact_return else 2, None, S)
         return self.h2_src[:recv_rows]
 
     def recv_buffer(self, rows: int):
@@ -128,8 +132,8 @@ class CudaBackend:
     # -- step 7
     def combine(self, h2_back, x, out):
         M = x.shape[0]
-        _lib.call("gptoss_moe_combine", _ptr(h2_back), _ptr(self.rev), _ptr(self.w), _ptr(x), M, self.k, self.H,
-                  _ptr(out), _stream())
+        fn = "gptoss_moe_combine" if self.exact_return else "gptoss_moe_combine_bf16"
+        _lib.call(fn, _ptr(h2_back), _ptr(self.rev), _ptr(self.w), _ptr(x), M, self.k, self.H, _ptr(out), _stream())
         return out
 
     def device_error(self) -> int:
@@ -141,7 +145,7 @@ class CudaBackend:
 class ExpertParallelMoE:
     """MLPBlock.forward with the experts sharded over the ranks of `group`."""
 
-    def __init__(self, blk, max_tokens: int, group=None, backend=None):
+    def __init__(self, blk, max_tokens: int, group=None, backend=None, exact_return: bool = False):
         self.blk = blk
         self.group = group
         self.world = dist.get_world_size(group)
@@ -155,7 +159,7 @@ class ExpertParallelMoE:
             f = torch.tensor([int(blk.flags)], dtype=torch.int32, device=blk.device)
             dist.all_reduce(f, op=dist.ReduceOp.MIN, group=group)
             blk.flags = int(f.item())
-        self.backend = backend or CudaBackend(blk, max_tokens, self.world)
+        self.backend = backend or CudaBackend(blk, max_tokens, self.world, exact_return)
         self.last_splits = None
 
     def forward(self, x, out=None):
@@ -225,7 +229,7 @@ class ExpertParallelMoE:
                       _ptr(b.tile_rows), El, H, I, _ptr(blk.mlp2_weight_blocks), _ptr(blk.mlp2_weight_scales),
                       _ptr(blk.mlp2_bias), b.f16, _ptr(b.h2_local), _ptr(b.err), S)
             _lib.call("gptoss_moe_segment_copy", _ptr(b.h2_local), _ptr(b.h2_src), _ptr(recv_counts), b.world, El,
-                      H * 4, 1, None, S)
+                      H * 4, 1 if b.exact_return else 2, None, S)
             ev[6].record()
             back = b.back_buffer(send.shape[0])
             dist.all_to_all_single(back, b.h2_src[:recv_rows], output_split_sizes=in_splits,

@@ -234,11 +234,19 @@ int gptoss_moe_plan_tiles(const int32_t* indptr, int32_t E, int32_t* tile_ptr, i
 /* Reorders rows between source-major order (for each source rank s, the rows
  * of local experts 0..El-1, counts[s*El + e] rows each) and expert-major order
  * (for each expert, the rows of sources 0..P-1).  direction 0: src -> expert
- * major (also writes indptr_local [El+1] when non-NULL); 1: the reverse.
+ * major (also writes indptr_local [El+1] when non-NULL); 1: the reverse;
+ * 2: the reverse with fp32 source rows of row_bytes rounded to bf16 rows of
+ * row_bytes / 2 (the expert outputs travel back in bf16).
  * row_bytes must be a multiple of 16.  counts is device memory. */
 int gptoss_moe_segment_copy(const void* src, void* dst, const int32_t* counts, int32_t num_ranks,
                             int32_t local_experts, int64_t row_bytes, int32_t direction, int32_t* indptr_local,
                             void* stream);
+
+/* gptoss_moe_combine with the expert outputs already rounded to bf16 (the
+ * expert-parallel return path): out[m] = bf16(x[m] + bf16(sum_r float(h2[..]) * w[m,r])).
+ * No counterpart in the reference (it has no expert parallelism). */
+int gptoss_moe_combine_bf16(const uint16_t* h2, const int32_t* row_of_pair, const uint16_t* topk_weights,
+                            const uint16_t* x, int64_t M, int32_t K, int32_t H, uint16_t* out, void* stream);
 
 #ifdef __cplusplus
 }

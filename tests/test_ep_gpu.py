@@ -1,6 +1,9 @@
-"""Expert parallelism on 2+ GPUs (NCCL): every rank's output must equal the
-single-GPU MLPBlock output for the same tokens, bit for bit (the same kernels
-run on the same rows; only the rows' placement differs)."""
+"""Expert parallelism on 2+ GPUs (NCCL).  With the fp32 return path every
+rank's output equals the single-GPU MLPBlock output for the same tokens, bit
+for bit (the same kernels run on the same rows; only the rows' placement
+differs).  With the default bf16 return path (expert outputs rounded to bf16
+before the weighted combine) the output is within the block's tolerance of
+the single-GPU one: max |diff| / max |ref| <= 2e-2, cosine >= 0.9995."""
 import os
 import socket
 
@@ -24,7 +27,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, E, M, q):
+def _worker(rank, world, port, E, M, exact, q):
     import datetime
     import importlib
     import sys
@@ -49,30 +52,43 @@ def _worker(rank, world, port, E, M, q):
         full = mlp.MLPBlock(cfg, device=dev).load_state(p)
         x = synth.activations(M, seed=100 + rank)
         xd = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(dev)
-        runner = ep.ExpertParallelMoE(blk, M)
+        runner = ep.ExpertParallelMoE(blk, M, exact_return=exact)
         out = runner.forward(xd)
         ref = full.forward(xd)
         torch.cuda.synchronize()
         same = bool(torch.equal(out.view(torch.int16), ref.view(torch.int16)))
-        maxdiff = float((out.float() - ref.float()).abs().max())
-        q.put((rank, same, maxdiff, runner.last_splits))
+        # compare the MoE part (output minus the residual input)
+        d, r = (out.float() - xd.float()).flatten(), (ref.float() - xd.float()).flatten()
+        rel = float((d - r).abs().max() / r.abs().max().clamp_min(1e-30))
+        cos = float(torch.dot(d, r) / (d.norm() * r.norm()).clamp_min(1e-30))
+        q.put((rank, same, rel, cos, runner.last_splits))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("M", [1, 300])
-def test_expert_parallel_matches_single_gpu(M):
+def _run(M, exact):
     world = 2
     ctx = torch.multiprocessing.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, 16, M, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, 16, M, exact, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(world)]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, same, maxdiff, splits in res:
-        assert same, f"rank {rank}: EP output differs from single-GPU (max |diff| {maxdiff})"
+    return res
+
+
+@pytest.mark.parametrize("M", [1, 300])
+def test_expert_parallel_exact_return_matches_single_gpu(M):
+    for rank, same, rel, cos, splits in _run(M, True):
+        assert same, f"rank {rank}: EP output differs from single-GPU (rel {rel}, cos {cos})"
+
+
+@pytest.mark.parametrize("M", [1, 300])
+def test_expert_parallel_bf16_return_within_tolerance(M):
+    for rank, same, rel, cos, splits in _run(M, False):
+        assert rel <= 2e-2 and cos >= 0.9995, f"rank {rank}: rel {rel:.3e}, cos {cos:.6f}"
