@@ -461,13 +461,15 @@ def attention_bench(dev, peaks, iters=10):
             out["prefill 4096, full causal layer"] = {
                 "ms": round(ms, 4), "tflops": round(tf, 1), "peak_tflops": peaks.get("bf16_tflops"),
                 "frac": round(tf / float(peaks.get("bf16_tflops", 1590.0)), 4),
-                "kernel": "attn_prefill_kernel (mma.sync m16n8k16 bf16, fp32 softmax)"}
+                "kernel": "attn_prefill_tc_kernel (tcgen05.mma kind::f16, S and O in TMEM, two query tiles "
+                          "ping-pong)"}
         else:
             nbytes = S * (HQ + 2 * HKV + HQ) * D * 2
             gbs = nbytes / (ms / 1e3) / 1e9
             out["prefill 4096, window 128 layer"] = {
                 "ms": round(ms, 4), "bytes": nbytes, "achieved_gbs": round(gbs, 1),
-                "hbm_frac": round(gbs / float(peaks.get("hbm_gbs", 6650.0)), 4)}
+                "hbm_frac": round(gbs / float(peaks.get("hbm_gbs", 6650.0)), 4),
+                "kernel": "attn_prefill_kernel (short windows: 64-query tiles, mma.sync bf16)"}
     del q, k, v, o, lse
     B, L = 32, 8192
     qd = torch.randn(B, HQ, D, generator=g, device=dev).to(torch.bfloat16)

@@ -4,6 +4,9 @@
 //   qkv_rope_kernel      split of the fused QKV projection, YaRN RoPE on q and
 //                        k (attention.py:96-180), k/v written to cache slots
 //                        (the append_mha_kv step, attention.py:214)
+//   attn_prefill_tc_kernel  tcgen05 attention for long key ranges (full-causal
+//                        layers): two 128-query tiles ping-pong on one SM,
+//                        scores and outputs in TMEM (see below)
 //   attn_prefill_kernel  FlashAttention-style causal attention of a chunk of
 //                        queries over its keys, optional sliding window,
 //                        base-2 online softmax, lse, sink rescale fused
@@ -325,6 +328,334 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const uint16_t* __res
   }
 }
 
+// ------------------------------------------------------ prefill, tcgen05 --
+// One CTA = two tiles of 128 queries (tile t = 0, 1: rows i0 + 128 t ..) of one
+// q head, 10 warps:
+//   warps 0-3 / 4-7  softmax of tile 0 / tile 1: thread = query row = TMEM
+//              lane.  Per key block it reads the score tile S (fp32, 128 keys)
+//              from TMEM in one go, masks, runs the base-2 online softmax and
+//              writes P (bf16) to TMEM as the A operand of O += P V;
+//   warp 8     TMA: the two Q tiles once, then K and V tiles of 128 keys;
+//   warp 9     MMA issuer (owns TMEM): S_t = Q_t K_j^T (A = Q_t, B = K_j in
+//              shared memory, M = N = 128, K = 64) and O_t += P_t V_j (A = P_t
+//              in TMEM, B = V_j read MN-major, N = 64, K = 128), O_t staying in
+//              TMEM for the whole key loop.
+// The two tiles ping-pong: while one tile's softmax runs, the tensor core
+// works on the other tile.  The output is rescaled lazily: P uses the row's
+// reference maximum m_ref, which only moves (and O_t, l are rescaled, a
+// TMEM read-modify-write of O_t) when the running maximum exceeds it by more
+// than 8 (P <= 2^8 stays exact enough in bf16 and fp32).  TMEM columns:
+// S_0 [0,128), S_1 [128,256), O_0 [256,320), O_1 [320,384), P_0 [384,448),
+// P_1 [448,512).
+constexpr int kTcBQ = 128, kTcBK = 128, kTcStages = 3, kTcThreads = 320;
+constexpr int kAttShortWindow = 512;  // windows up to this many keys take the mma.sync kernel
+constexpr uint32_t kTcColO = 256, kTcColP = 384;
+constexpr float kTcRescale = 8.0f;
+constexpr int kTcQBytes = kTcBQ * 128, kTcKVBytes = kTcBK * 128;
+constexpr int kTcSmemKV = 2 * kTcQBytes;
+constexpr int kTcSmemBar = kTcSmemKV + kTcStages * 2 * kTcKVBytes;
+constexpr int kTcSmemAlloc = kTcSmemBar + 256 + 1024;  // > 114 KB: one CTA (and its 512 TMEM columns) per SM
+
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+// 32 lanes x 32 bit, 32 consecutive columns per thread, no wait.
+__device__ __forceinline__ void tmem_ld_x32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ unsigned long long pack_f32x2(float lo, float hi) {
+  return ((unsigned long long)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
+                           const __grid_constant__ CUtensorMap tmap_v, const uint16_t* __restrict__ sinks, int64_t Sq,
+                           int64_t Skv, int32_t Hq, int32_t Hkv, int32_t window, float sm_scale,
+                           uint16_t* __restrict__ o, float* __restrict__ lse) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = (uint64_t*)(smem + kTcSmemBar);
+  uint64_t* qfull = bars;
+  uint64_t* kvfull = bars + 1;             // [kTcStages]
+  uint64_t* kvempty = kvfull + kTcStages;  // [kTcStages] MMA commit after both tiles' P V
+  uint64_t* sfull = kvempty + kTcStages;   // [2] per tile: MMA commit after Q K^T
+  uint64_t* sfree = sfull + 2;             // [2] per tile: its 4 softmax warps read S
+  uint64_t* pfull = sfree + 2;             // [2] per tile: its 4 softmax warps wrote P (and rescaled O)
+  uint64_t* ofull = pfull + 2;             // [2] per tile: MMA commit after P V
+  volatile uint32_t* tmem_slot = (volatile uint32_t*)(ofull + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y;
+  const int hk = h / (Hq / Hkv);
+  const int64_t qt = (int64_t)gridDim.x - 1 - blockIdx.x;  // the longest key ranges first
+  const int64_t i0 = qt * 2 * kTcBQ;
+  const int64_t off = Skv - Sq;
+  const int64_t last_q = min64(i0 + 2 * kTcBQ - 1, Sq - 1);
+  const int64_t j_end = min64(Skv, off + last_q + 1);
+  int64_t j_beg = 0;
+  if (window > 0) j_beg = max64(0, off + i0 - window + 1);
+  j_beg = (j_beg / kTcBK) * kTcBK;
+  const int n = (int)((j_end - j_beg + kTcBK - 1) / kTcBK);
+
+  if (threadIdx.x == 0) {
+    mbar_init(qfull, 1);
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&kvfull[s], 1);
+      mbar_init(&kvempty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&sfull[t], 1);
+      mbar_init(&sfree[t], 4);
+      mbar_init(&pfull[t], 4);
+      mbar_init(&ofull[t], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc((uint32_t*)tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ loads
+    if (elect_one()) {
+      mbar_arrive_expect_tx(qfull, 2 * kTcQBytes);
+      tma_load_3d(smem, &tmap_q, 0, h, (int32_t)i0, qfull);
+      tma_load_3d(smem + kTcQBytes, &tmap_q, 0, h, (int32_t)(i0 + kTcBQ), qfull);
+      for (int j = 0; j < n; ++j) {
+        const int s = j % kTcStages;
+        const uint32_t ph = (uint32_t)(j / kTcStages) & 1u;
+        if (!mbar_wait(&kvempty[s], ph ^ 1u, nullptr, 0)) break;
+        uint8_t* kv = smem + kTcSmemKV + s * 2 * kTcKVBytes;
+        mbar_arrive_expect_tx(&kvfull[s], 2 * kTcKVBytes);
+        const int32_t kz = (int32_t)(j_beg + (int64_t)j * kTcBK);
+        tma_load_3d(kv, &tmap_k, 0, hk, kz, &kvfull[s]);
+        tma_load_3d(kv + kTcKVBytes, &tmap_v, 0, hk, kz, &kvfull[s]);
+      }
+    }
+  } else if (warp == 9) {
+    // --------------------------------------------------------------- MMA
+    if (elect_one()) {
+      const uint32_t idesc_s = make_idesc_bf16(kTcBQ, kTcBK);
+      const uint32_t idesc_pv = make_idesc_bf16(kTcBQ, 64) | (1u << 16);  // B (V) read MN-major
+      bool ok = mbar_wait(qfull, 0, nullptr, 0);
+      auto issue_s = [&](int t, int j) {
+        const int s = j % kTcStages;
+        const uint64_t qdesc = make_sdesc_sw128(smem_u32(smem + t * kTcQBytes));
+        const uint64_t kdesc = make_sdesc_sw128(smem_u32(smem + kTcSmemKV + s * 2 * kTcKVBytes));
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma_ss(tmem + (uint32_t)t * kTcBK, qdesc + 2 * kk, kdesc + 2 * kk, idesc_s, kk > 0 ? 1u : 0u);
+        tc_commit(&sfull[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const int s = j % kTcStages;
+        // V tile: 128 key rows of 128 B, 128-byte swizzle; MN-major B with
+        // 8-row groups 1024 B apart; 16 keys (2048 B) per K step
+        const uint64_t vdesc = make_sdesc_sw128(smem_u32(smem + kTcSmemKV + s * 2 * kTcKVBytes + kTcKVBytes));
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_ts(tmem + kTcColO + 64 * t, tmem + kTcColP + 64 * t + kk * 8, vdesc + 128 * kk, idesc_pv,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&ofull[t]);
+      };
+      if (ok && n > 0) {
+        ok = mbar_wait(&kvfull[0], 0, nullptr, 0);
+        if (ok) {
+          tc_fence_after();
+          issue_s(0, 0);
+          issue_s(1, 0);
+        }
+      }
+      for (int j = 0; j < n && ok; ++j) {
+        const bool more = j + 1 < n;
+        if (more) {
+          ok = mbar_wait(&kvfull[(j + 1) % kTcStages], (uint32_t)((j + 1) / kTcStages) & 1u, nullptr, 0);
+          if (!ok) break;
+        }
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (more) {
+            ok = mbar_wait(&sfree[t], (uint32_t)j & 1u, nullptr, 0);  // the softmax has read S_t(j)
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(t, j + 1);
+          }
+          ok = mbar_wait(&pfull[t], (uint32_t)j & 1u, nullptr, 0);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(t, j);
+        }
+        tc_commit(&kvempty[j % kTcStages]);
+      }
+    }
+  } else {
+    // ----------------------------------------------------------- softmax
+    const int t = warp >> 2;                       // tile
+    const int row = (warp & 3) * 32 + lane;        // TMEM lane
+    const int64_t qi = i0 + t * kTcBQ + row;
+    const int64_t pos = off + qi;
+    const bool row_ok = qi < Sq;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t s_col = tmem + lane_base + (uint32_t)t * kTcBK;
+    const uint32_t o_col = tmem + lane_base + kTcColO + 64 * t;
+    const uint32_t p_col = tmem + lane_base + kTcColP + 64 * t;
+    const float scale2 = sm_scale * kLog2e;
+    const int64_t tile_last = min64(i0 + t * kTcBQ + kTcBQ - 1, Sq - 1);
+    float m_ref = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n && ok; ++j) {
+      if (!mbar_wait(&sfull[t], (uint32_t)j & 1u, nullptr, 0)) { ok = false; break; }
+      tc_fence_after();
+      const int64_t j0 = j_beg + (int64_t)j * kTcBK;
+      const bool full_tile = (j0 + kTcBK - 1 <= off + i0 + t * kTcBQ) && (j0 + kTcBK <= Skv) &&
+                             (window <= 0 || j0 >= off + tile_last - window + 1);
+      // raw score of key j0 + e with the mask applied (-inf when not visible)
+      auto masked = [&](uint32_t bits, int e) -> uint32_t {
+        const int64_t kj = j0 + e;
+        bool vis = kj <= pos && kj < Skv && row_ok;
+        if (window > 0) vis = vis && kj >= pos - window + 1;
+        return vis ? bits : __float_as_uint(-INFINITY);
+      };
+      // pass 1: row max of the raw scores (sm_scale * log2(e) > 0)
+      float mx = -INFINITY;
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t r[64];
+        tmem_ld_x32_nowait(s_col + 64 * hb, r);
+        tmem_ld_x32_nowait(s_col + 64 * hb + 32, r + 32);
+        tmem_ld_wait();
+        if (full_tile) {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) mx = fmaxf(mx, __uint_as_float(r[e]));
+        } else {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) mx = fmaxf(mx, __uint_as_float(masked(r[e], 64 * hb + e)));
+        }
+      }
+      const float mxs = mx * scale2;  // base-2 row max of this block
+      // lazy rescale: move the reference maximum only when P would exceed 2^8
+      const bool move = mxs > m_ref + kTcRescale;
+      const float m_new = move ? mxs : m_ref;
+      const float c = move ? fast_exp2(m_ref - m_new) : 1.0f;
+      const float m_eff = m_new == -INFINITY ? 0.f : m_new;  // fully masked so far: every p is 0
+      // P_t and O_t are free once P_t(j-1) V(j-1) is done
+      if (j > 0) {
+        if (!mbar_wait(&ofull[t], (uint32_t)(j - 1) & 1u, nullptr, 0)) { ok = false; break; }
+        tc_fence_after();
+      }
+      // pass 2: p = 2^(s * scale2 - m) two at a time (packed f32x2 FMA / add),
+      // stored to TMEM as bf16 32 keys at a time; the row sum stays fp32
+      const unsigned long long sc2 = pack_f32x2(scale2, scale2), negm = pack_f32x2(-m_eff, -m_eff);
+      unsigned long long acc2 = 0ull;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t r[32], pk[16];
+        tmem_ld_x32_nowait(s_col + 32 * q4, r);
+        tmem_ld_wait();
+        if (!full_tile) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = masked(r[e], 32 * q4 + e);
+        }
+#pragma unroll
+        for (int e2 = 0; e2 < 16; ++e2) {
+          const int e = 2 * e2;
+          unsigned long long x = ((unsigned long long)r[e + 1] << 32) | r[e];
+          asm("fma.rn.f32x2 %0, %0, %1, %2;" : "+l"(x) : "l"(sc2), "l"(negm));
+          const float p0 = fast_exp2(__uint_as_float((uint32_t)x));
+          const float p1 = fast_exp2(__uint_as_float((uint32_t)(x >> 32)));
+          const unsigned long long pp = pack_f32x2(p0, p1);
+          asm("add.rn.f32x2 %0, %0, %1;" : "+l"(acc2) : "l"(pp));
+          pk[e2] = pack_bf16x2(p0, p1);
+        }
+        tmem_st_x16(p_col + 16 * q4, pk);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sfree[t]);  // S_t read: the next Q K^T may overwrite it
+      const float rs = __uint_as_float((uint32_t)acc2) + __uint_as_float((uint32_t)(acc2 >> 32));
+      l = l * c + rs;
+      m_ref = m_new;
+      if (j > 0 && __any_sync(0xffffffffu, move)) {
+        // the reference maximum moved: O_t (blocks < j) by c, before P_t V(j) adds to it
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t ov[32];
+          tmem_ld_x32(o_col + 32 * hf, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int d = 0; d < 32; ++d) ov[d] = __float_as_uint(__uint_as_float(ov[d]) * c);
+          tmem_st_x32(o_col + 32 * hf, ov);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pfull[t]);
+    }
+    // normalise, lse, sink rescale, store (attention.py:240-247)
+    if (ok && n > 0 && mbar_wait(&ofull[t], (uint32_t)(n - 1) & 1u, nullptr, 0)) {
+      tc_fence_after();
+      uint32_t ov[64];
+      tmem_ld_x32_nowait(o_col, ov);
+      tmem_ld_x32_nowait(o_col + 32, ov + 32);
+      tmem_ld_wait();
+      if (row_ok) {
+        const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+        const float lse2 = m_ref + log2f(l);
+        if (lse) lse[qi * Hq + h] = lse2;
+        const float ss = sinks ? sink_scale(lse2, bf16_bits_to_f32(sinks[h])) : 1.0f;
+        uint4* orow = (uint4*)(o + (qi * Hq + h) * kAttD);
+#pragma unroll
+        for (int d8 = 0; d8 < 8; ++d8) {
+          uint32_t w4[4];
+#pragma unroll
+          for (int q2 = 0; q2 < 4; ++q2) {
+            float v0 = round_bf16(__uint_as_float(ov[8 * d8 + 2 * q2]) * inv_l);
+            float v1 = round_bf16(__uint_as_float(ov[8 * d8 + 2 * q2 + 1]) * inv_l);
+            if (sinks) {
+              v0 = __fmul_rn(v0, ss);
+              v1 = __fmul_rn(v1, ss);
+            }
+            w4[q2] = (uint32_t)f32_to_bf16_bits(v0) | ((uint32_t)f32_to_bf16_bits(v1) << 16);
+          }
+          orow[d8] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 // --------------------------------------------------------------- decode --
 // One CTA = (sequence b, kv head g, key split).  The 8 query heads of the
 // group (GQA) are rows 0..7 of a 16-row MMA tile (rows 8..15 are zero).
@@ -599,8 +930,31 @@ int launch_attn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                         float* lse, cudaStream_t s) {
   if (Sq <= 0) return 0;
   if (D != kAttD || Hq % Hkv || Skv < Sq) return -12;
-  dim3 grid((unsigned)((Sq + kAttBQ - 1) / kAttBQ), (unsigned)Hq);
-  attn_prefill_kernel<<<grid, 128, 0, s>>>(q, k, v, sinks, Sq, Skv, Hq, Hkv, window, sm_scale, o, lse);
+  if (window > 0 && window <= kAttShortWindow) {
+    // a few key blocks per query tile: the 64-query mma.sync kernel's lower
+    // fixed cost per CTA wins over the tcgen05 kernel's pipeline fill
+    dim3 grid((unsigned)((Sq + kAttBQ - 1) / kAttBQ), (unsigned)Hq);
+    attn_prefill_kernel<<<grid, 128, 0, s>>>(q, k, v, sinks, Sq, Skv, Hq, Hkv, window, sm_scale, o, lse);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
+  if (((uintptr_t)q & 15) || ((uintptr_t)k & 15) || ((uintptr_t)v & 15) || ((uintptr_t)o & 15)) return -12;
+  // q [Sq, Hq, 64], k / v [Skv, Hkv, 64] bf16: boxes of 64 dims x 1 head x 128 tokens
+  CUtensorMap tq, tk, tv;
+  const uint32_t box[3] = {64, 1, 128};
+  const uint64_t dq[3] = {64, (uint64_t)Hq, (uint64_t)Sq}, sq_[2] = {128, (uint64_t)Hq * 128};
+  const uint64_t dk[3] = {64, (uint64_t)Hkv, (uint64_t)Skv}, sk_[2] = {128, (uint64_t)Hkv * 128};
+  if (make_tmap_3d(&tq, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dq, sq_, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      make_tmap_3d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dk, sk_, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      make_tmap_3d(&tv, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dk, sk_, box, CU_TENSOR_MAP_SWIZZLE_128B))
+    return -2;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemAlloc);
+    attr = true;
+  }
+  dim3 grid((unsigned)((Sq + 2 * kTcBQ - 1) / (2 * kTcBQ)), (unsigned)Hq);
+  attn_prefill_tc_kernel<<<grid, kTcThreads, kTcSmemAlloc, s>>>(tq, tk, tv, sinks, Sq, Skv, Hq, Hkv, window,
+                                                                sm_scale, o, lse);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

@@ -1,6 +1,7 @@
 // launch.h -- host-side launch helpers shared between the kernel files and the C ABI.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -50,6 +51,8 @@ int launch_qkv_rope(const uint16_t* qkv, const int32_t* pos, const int32_t* slot
                     uint16_t* v_cache, cudaStream_t s);
 int launch_rope(const uint16_t* x, const int32_t* pos, int64_t S, int32_t Hh, int32_t D, const float* inv_freq,
                 float conc, uint16_t* out, cudaStream_t s);
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, const uint64_t dims[3],
+                 const uint64_t strides[2], const uint32_t box[3], CUtensorMapSwizzle swz);
 int launch_attn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* sinks, int64_t Sq,
                         int64_t Skv, int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale, uint16_t* o,
                         float* lse, cudaStream_t s);

@@ -571,6 +571,20 @@ static PFN_encodeTiled get_encode_fn() {
   return fn;
 }
 
+// 3-D tensor map: dims innermost first, byte strides of dims 1 and 2.
+int make_tmap_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, const uint64_t dims[3],
+                 const uint64_t strides[2], const uint32_t box[3], CUtensorMapSwizzle swz) {
+  PFN_encodeTiled enc = get_encode_fn();
+  if (!enc) return -1;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {strides[0], strides[1]};
+  cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dtype, 3, const_cast<void*>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -2;
+}
+
 // 2-D tensor map over a row-major matrix [rows, cols] of `esize`-byte elements.
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int esize, uint64_t rows,
                  uint64_t cols, uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swz) {

@@ -120,8 +120,9 @@ def _run_prefill(q, k, v, sinks, window, with_sinks=True):
     return G.host(o), G.host(lse)
 
 
-@pytest.mark.parametrize("window", [0, 128])
-@pytest.mark.parametrize("Sq,Skv", [(300, 300), (1, 77), (72, 200), (130, 130)])
+# window 0 and 700: the tcgen05 kernel; 128: the short-window mma.sync kernel
+@pytest.mark.parametrize("window", [0, 128, 700])
+@pytest.mark.parametrize("Sq,Skv", [(300, 300), (1, 77), (72, 200), (130, 130), (600, 900)])
 def test_prefill_matches_oracle(oracle, Sq, Skv, window):
     q, k, v, sinks = synth().attention_inputs(Skv, seed=10 + Sq + window)
     q = np.ascontiguousarray(q[Skv - Sq:])
@@ -138,7 +139,7 @@ def test_prefill_without_sinks_is_plain_attention(oracle):
     G.tol_check(G.f32(o), G.f32(o_ref), what="prefill without sinks")
 
 
-@pytest.mark.parametrize("window", [0, 128])
+@pytest.mark.parametrize("window", [0, 128, 700])
 def test_prefill_config1_seq4096_sampled_rows(oracle, window):
     """Config 1 prefill (seq 4096, 64 q / 8 kv heads): every row computed on the
     GPU, a sample of rows checked against the oracle."""
