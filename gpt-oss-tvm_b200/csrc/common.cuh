@@ -30,9 +30,11 @@ enum DeviceError : uint32_t {
 
 // Token rows of one grouped-GEMM tile (the MMA N dimension).  With few rows
 // per expert (decode) the tiles are at most 32 rows and the GEMM runs its
-// weight-streaming variant; otherwise at most 192.  The permutation plans its
+// weight-streaming variant; otherwise at most 160 (two 160-column
+// accumulators leave TMEM room for four one-chunk weight slots; a multiple
+// of 32, the granularity of a CTA-pair MMA's N).  The permutation plans its
 // token tiles with the same rule as the GEMM launch.
-constexpr int kMoeTileMaxRows = 192;
+constexpr int kMoeTileMaxRows = 160;
 constexpr int kMoeTileRowsSmall = 32;
 __host__ __device__ __forceinline__ int moe_tile_rows_max(int64_t rows, int32_t num_experts) {
   return rows <= 8 * (int64_t)num_experts ? kMoeTileRowsSmall : kMoeTileMaxRows;
@@ -242,6 +244,86 @@ __device__ __forceinline__ void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ------------------------------------------------- CTA pairs (clusters of 2) --
+// Kernels built on these run as clusters of two CTAs on the two SMs of a TPC;
+// rank 0 issues the pair's tensor-core work.  Every tcgen05 instruction that
+// names a CTA group in such a kernel names cta_group::2.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// All threads of both CTAs; orders everything before it cluster-wide.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster (address from
+// mapa_shared).  Default (CTA-scope release) semantics: what the barrier
+// publishes between the CTAs of a pair is TMEM contents, ordered by
+// tcgen05.wait::st / tcgen05.ld waits and tcgen05.fence::before_thread_sync on
+// the arriving side and tcgen05.fence::after_thread_sync after the wait.  A
+// cluster-scope release here costs ~1.6 k cycles per arrive (measured).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 2-D tiled load into this CTA's shared memory whose completion (tx bytes) is
+// signalled on a barrier of either CTA of the pair (`bar_cluster` from
+// mapa_shared).  No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, int32_t x, int32_t y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(tmap), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+// TMEM allocation for a CTA pair: the same warp of both CTAs issues it and
+// both get the same column range.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Pair MMA (M = 256: 128 A rows from each CTA's TMEM, B rows split in halves
+// between the two CTAs' shared memory at the same offset, D rows in each
+// CTA's TMEM).  Four K=16 steps of one 64-wide K chunk, as tc_mma4_ts.
+__device__ __forceinline__ void tc_mma4_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.eq.b32 q, 0, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, {%11, %11, %11, %11, %11, %11, %11, %11}, p;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %6, %3, {%11, %11, %11, %11, %11, %11, %11, %11}, q;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %8, %3, {%11, %11, %11, %11, %11, %11, %11, %11}, q;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%9], %10, %3, {%11, %11, %11, %11, %11, %11, %11, %11}, q;\n\t}" ::
+          "r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(a_tmem + 8), "l"(b_desc + 2), "r"(a_tmem + 16),
+      "l"(b_desc + 4), "r"(a_tmem + 24), "l"(b_desc + 6), "r"(0u)
+      : "memory");
+}
+// Arrive once on the barrier at this offset in every CTA of `cta_mask` when
+// the pair MMAs issued so far by this thread have completed.
+__device__ __forceinline__ void tc_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
 
 // ------------------------------------------------------------- misc PTX --
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

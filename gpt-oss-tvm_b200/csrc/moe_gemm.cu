@@ -11,19 +11,21 @@
 //                      (clamped SwiGLU, model/mlp.py:29-60)
 //   mode 1 (down):     out[r, n] = h[r, n]   (fp32, combined later)
 //
-// Design (sm_100a, one persistent CTA per SM):
+// Design (sm_100a, persistent: one CTA per SM, or one cluster of two CTAs
+// per TPC for prefill-sized tiles):
 //   * The weights are the MMA "A" operand and live in TMEM: dequant warps (one
 //     TMEM lane = one weight row each) turn e2m1 nibbles into exact bf16 and
 //     write them with tcgen05.st.  This keeps the shared-memory bandwidth for
 //     the activation operand only.
 //   * The activations (expert-major rows, bf16, K-major) are the "B" operand,
 //     brought into 128-byte-swizzled shared memory by TMA.
-//   * tcgen05.mma.cta_group::1.kind::f16 (M = 128 weight rows, N = up to 192
-//     token rows, or 32 in the decode variant, K = 16 per instruction)
-//     accumulates fp32 in TMEM.
-//   * Nibbles are streamed by TMA (32-byte swizzle) through an 8-deep ring
-//     (32-deep in the decode variant); each tile's 128 x K/32 scale bytes
-//     arrive with one bulk copy.
+//   * tcgen05.mma.kind::f16 (K = 16 per instruction) accumulates fp32 in
+//     TMEM: cta_group::2 with M = 256 weight rows (128 per CTA of a pair) for
+//     prefill-sized tiles of up to 128 token rows, cta_group::1 with M = 128
+//     for decode-sized tiles of up to 32 token rows (and for prefill tiles
+//     when GPTOSS_MOE_PAIR=0).
+//   * Nibbles are streamed by TMA (128-byte swizzle, 4 K chunks per stage);
+//     each tile's 128 x K/32 scale bytes arrive with one bulk copy.
 // Warp roles: 0-15 dequant (four warpgroups), 16-19 epilogue (double-buffered
 // TMEM accumulator, so the epilogue of tile i overlaps the main loop of tile
 // i+1), 20 activation TMA, 21 MMA issuer (also owns TMEM), 22 weight TMA.
@@ -47,50 +49,69 @@ constexpr int kDequantWarps = 16;  // 4 warpgroups
 constexpr int kEpiWarp0 = 16;
 constexpr int kActWarp = 20, kMmaWarp = 21, kWWarp = 22;
 
-// Two shapes of the same pipeline.
-//   Large tiles (prefill): up to 192 token rows, 6 one-chunk activation
-//   stages (144 KB), 3 nibble stages (48 KB), 4 one-chunk TMEM A slots (the
-//   two 192-column accumulators take the rest of TMEM).
-//   Small tiles (decode, few rows per expert): up to 32 token rows, the MMA
-//   is nearly free and the weights must stream at HBM speed: 6 nibble stages
-//   and 6 activation stages of 4 chunks each (96 KB + up to 96 KB in flight
-//   per SM; an activation stream only a few chunks deep would queue behind
-//   the weights in the SM's TMA unit and pace the MMA).
-// Small tiles use 4 TMEM A slots of 2 chunks; one slot per dequant warpgroup
-// in both variants.  The single
-// MMA-issuing thread waits on one barrier per A stage (the owning warpgroup
-// arrives after its TMEM stores and after the stage's activations landed) and
-// commits twice per A stage at most: its per-chunk overhead, not the tensor
-// pipe, bounds small-N tiles.
+// Three shapes of one pipeline (kVar):
+//   kVarSmall (decode, few rows per expert): up to 32 token rows; the MMA is
+//     nearly free and the weights must stream at HBM speed: 6 nibble stages
+//     and 6 activation stages of 4 chunks (96 KB + up to 96 KB in flight per
+//     SM; an activation stream only a few chunks deep would queue behind the
+//     weights in the SM's TMA unit and pace the MMA); 4 TMEM A slots of 2
+//     chunks.
+//   kVarPair (prefill): clusters of two CTAs on the two SMs of a TPC and
+//     tcgen05.mma.cta_group::2 -- one MMA covers 256 weight rows (128 from
+//     each CTA's TMEM) x up to 128 token rows, and each CTA stages only half
+//     of the token rows (the MMA reads the other half from the peer's shared
+//     memory), so per MMA cycle an SM takes in half the activation bytes of
+//     the single-CTA form.  That L2 -> SM stream, not DRAM or the issue
+//     slots, bounds the single-CTA form on prefill.  Rank 0's MMA thread
+//     issues every MMA of the pair and its commits arrive on both CTAs'
+//     barriers; rank 1's dequant and epilogue warps arrive on rank 0's
+//     barriers and its activation loads complete on rank 0's.
+//   kVarLarge: the single-CTA form of the same tiles (GPTOSS_MOE_PAIR=0, or
+//     when no CTA pair fits).
+// Prefill tiles hold up to 160 token rows: two 160-column accumulators and
+// four one-chunk TMEM A slots fill TMEM.  Measured on B200 (8192-token
+// layer): 160-row tiles with one-chunk A stages beat 128-row tiles with eight
+// one-chunk or four two-chunk A slots (smaller N leaves the single MMA
+// thread's per-chunk waits and commits, not the tensor pipe, as the pace),
+// and prefetching the next tile into L2 slows the loads it competes with.
 // A nibble stage is one TMA box of 128 weight rows x 128 bytes (4 K chunks):
 // wide rows keep the TMA request rate, not HBM, from bounding the stream.
-template <bool kSmall>
+enum GemmVariant { kVarSmall = 0, kVarLarge = 1, kVarPair = 2 };
+
+template <int kVar>
 struct GemmCfg {
-  static constexpr int kMaxBN = kSmall ? kMoeTileRowsSmall : kMoeTileMaxRows;
-  static constexpr int kBStages = 6;
-  static constexpr int kBChunks = kSmall ? 4 : 1;      // K chunks per activation stage
-  static constexpr int kAChunks = kSmall ? 2 : 1;      // K chunks per TMEM A stage (one warpgroup's round)
+  static constexpr bool kPair = kVar == kVarPair;
+  static constexpr bool kSmall = kVar == kVarSmall;
+  static constexpr int kMaxBN = kSmall ? kMoeTileRowsSmall : kMoeTileMaxRows;  // token rows per tile (MMA N)
+  static constexpr int kRowsCta = kPair ? kMaxBN / 2 : kMaxBN;  // token rows staged per CTA
+  static constexpr int kMmaM = kPair ? 2 * kBM : kBM;           // weight rows per MMA
+  static constexpr int kNRound = kPair ? 32 : 16;               // MMA N granularity
+  static constexpr int kBStages = kPair ? 10 : 6;
+  static constexpr int kBChunks = kSmall ? 4 : 1;  // K chunks per activation stage
+  static constexpr int kAChunks = kSmall ? 2 : 1;  // K chunks per TMEM A stage (one warpgroup's round)
   // TMEM A slots, a multiple of 4: slot s is written only by warpgroup s % 4
   static constexpr int kASlots = 4;
   static constexpr int kASlotCols = kAChunks * kBK / 2;  // TMEM columns of an A slot (f16/bf16 pairs)
   static constexpr int kAPerW = kWChunks / kAChunks;    // A stages per nibble stage = its reader warpgroups
-  static constexpr int kWStages = kSmall ? 6 : 3;
+  static constexpr int kWStages = kSmall ? 6 : (kPair ? 4 : 3);
   static_assert(kBChunks % kAChunks == 0 && kWChunks % kAChunks == 0, "A stages nest in both rings");
-  static constexpr int kActChunkBytes = kMaxBN * kBK * 2;  // one chunk of the token rows
+  static constexpr int kActChunkBytes = kRowsCta * kBK * 2;  // one chunk of this CTA's token rows
   static constexpr int kActStageBytes = kBChunks * kActChunkBytes;
   static constexpr int kAccCols = kMaxBN;
   static constexpr int kAColBase = 2 * kAccCols;
   static_assert(kAColBase + kASlots * kASlotCols <= kTmemCols, "TMEM budget");
   static_assert(kASlots % 4 == 0 && kDequantWarps == 16, "A slots divide among the four dequant warpgroups");
+  static_assert(kMaxBN % kNRound == 0 && (kRowsCta % kBoxRows) == 0, "whole TMA boxes per CTA");
   // shared memory offsets from the 1024-aligned base
   static constexpr int kAct = 0;
   static constexpr int kW = kAct + kBStages * kActStageBytes;
   static constexpr int kScale = kW + kWStages * kWStageBytes;
   static constexpr int kBar = kScale + 2 * kScaleBytes;
-  static constexpr int kNumBars = 2 * kASlots + 2 * kBStages + 2 * kWStages + 4 + 4;
+  static constexpr int kNumBars = 2 * kASlots + 2 * kBStages + 2 * kWStages + 4 + 4 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
-  static constexpr int kEpi = kMisc + 64;        // 4 epilogue warps x (32 tokens x 16 outputs x 2 B)
+  static constexpr int kEpi = (kMisc + 64 + 15) & ~15;  // 4 epilogue warps x (32 tokens x 16 outputs x 2 B)
   static constexpr int kAlloc = kEpi + 4 * 1024 + 1024;  // + slack for manual 1024 B alignment
+  static_assert(kW % 1024 == 0 && kActChunkBytes % 1024 == 0, "128-byte swizzle atoms stay 1024-aligned");
   static_assert(kAlloc <= 227 * 1024, "shared memory budget");
 };
 
@@ -119,8 +140,11 @@ struct TileInfo {
 // Token-tile-major order: the CTAs running at the same time share one token
 // tile's activations (L2 hits) and an expert's weight tiles are reused by its
 // token tiles within a short window (DRAM reads close to the algorithmic ones).
+// The feature rows of tile t start at f * fstride + fofs (the CTA-pair kernel
+// covers 2 x 128 rows per tile, its CTA of rank r the rows from r * 128).
 template <int kMaxBN>
-__device__ __forceinline__ bool decode_tile(const GemmParams& p, int32_t t, int32_t ftiles, TileInfo& ti) {
+__device__ __forceinline__ bool decode_tile(const GemmParams& p, int32_t t, int32_t ftiles, TileInfo& ti,
+                                            int32_t fstride = kBM, int32_t fofs = 0) {
   const int32_t g = t / ftiles;
   const int32_t f = t - g * ftiles;
   int32_t lo = 0, hi = p.num_experts;  // find e with tile_ptr[e] <= g < tile_ptr[e+1]
@@ -136,7 +160,7 @@ __device__ __forceinline__ bool decode_tile(const GemmParams& p, int32_t t, int3
   ti.expert = e;
   ti.row0 = base + tt * per;
   ti.nrows = min(per, cnt - tt * per);
-  ti.f0 = f * kBM;
+  ti.f0 = f * fstride + fofs;
   if (per > kMaxBN) {
     if (f == 0 && threadIdx.x == 0) raise_error(p.err, kErrBadTilePlan);
     return false;
@@ -202,47 +226,118 @@ __device__ __forceinline__ void decode_group(const uint4 nb, uint32_t sc, bool r
   }
 }
 
+// Epilogue of one 32-token column block of a finished accumulator: this
+// thread holds weight row `frow` (TMEM lane q * 32 + lane) for tokens
+// c0 .. c0 + 31 of the tile in v[].  Mode 0 applies the clamped SwiGLU to
+// (glu, linear) lane pairs and stores bf16 (f16) outputs through the warp's
+// shared tile; mode 1 stores fp32.
+template <int kMode, bool kF16>
+__device__ __forceinline__ void epilogue_block(const GemmParams& p, const TileInfo& ti, const uint32_t (&v)[32],
+                                               int32_t c0, int q, int lane, float bias, bool row_ok, int32_t frow,
+                                               uint16_t* tile) {
+  if (kMode == 0) {
+    // lane pair (2j, 2j+1) holds the glu / linear rows of output feature
+    // j: the even lane finishes tokens c0..c0+15, the odd lane c0+16..31.
+    // The 32 x 16 outputs go through this warp's shared tile
+    // [token][feature] and leave as 16-byte rows of 8 features.
+    const bool odd = lane & 1;
+    uint16_t* out = (uint16_t*)p.out;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float mine_lo = __uint_as_float(v[i]) + bias;
+      const float mine_hi = __uint_as_float(v[16 + i]) + bias;
+      const float send = odd ? mine_lo : mine_hi;
+      const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+      const float gl = odd ? recv : mine_lo;
+      const float li = odd ? mine_hi : recv;
+      const float g = fminf(gl, p.limit);
+      const float l = fmaxf(fminf(li, p.limit), -p.limit);
+      // g * sigmoid(alpha * g); a huge denominator gives 0, the limit
+      const float gs = __fdividef(g, 1.0f + __expf(-(p.alpha * g)));
+      const float y = gs * (l + 1.0f);
+      const int tok = i + (odd ? 16 : 0);
+      tile[tok * 16 + (lane >> 1)] = kF16 ? __half_as_ushort(__float2half_rn(y)) : f32_to_bf16_bits(y);
+    }
+    __syncwarp();
+    const bool warp_rows_ok = ti.f0 + q * 32 + 32 <= p.N;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int tok = lane, h = k ^ ((lane >> 2) & 1);  // alternate halves: no bank conflicts
+      const int32_t col = c0 + tok;
+      const uint4 val = *(const uint4*)(tile + tok * 16 + h * 8);
+      const int32_t f = (ti.f0 >> 1) + q * 16 + h * 8;  // first output feature of the 8
+      if (col < ti.nrows) {
+        uint16_t* dst = out + (size_t)(ti.row0 + col) * p.ldo + f;
+        if (warp_rows_ok) {
+          *(uint4*)dst = val;
+        } else {
+          const uint16_t* e = (const uint16_t*)&val;
+          for (int u = 0; u < 8; ++u)
+            if (2 * (f + u) < p.N) dst[u] = e[u];
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    float* out = (float*)p.out;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int32_t col = c0 + j;
+      if (row_ok && col < ti.nrows)
+        out[(size_t)(ti.row0 + col) * p.ldo + frow] = __uint_as_float(v[j]) + bias;
+    }
+  }
+}
+
 // kF16: weights decoded to f16 by the hardware converter and activations in
 // f16 (the fast path, valid when every scale code is in 104..140); otherwise
-// exact bf16 decode and bf16 activations.
-template <int kMode, bool kF16, bool kSmall>
+// exact bf16 decode and bf16 activations.  kVar: GemmVariant.
+template <int kMode, bool kF16, int kVar>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_act, const __grid_constant__ CUtensorMap tmap_act64,
-                       const __grid_constant__ CUtensorMap tmap_w,
-                       const GemmParams p) {
-  using C = GemmCfg<kSmall>;
+                       const __grid_constant__ CUtensorMap tmap_w, const GemmParams p) {
+  using C = GemmCfg<kVar>;
+  constexpr bool kPair = C::kPair;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* act_s = smem + C::kAct;
   uint8_t* w_s = smem + C::kW;
   uint8_t* sc_s = smem + C::kScale;
   uint64_t* bars = (uint64_t*)(smem + C::kBar);
-  uint64_t* full_bar = bars;                       // [kASlots] A slot written and its activations landed
-  uint64_t* empty_bar = full_bar + C::kASlots;     // [kASlots] MMA commit
-  uint64_t* bfull_bar = empty_bar + C::kASlots;    // [kBStages] activation TMA tx
-  uint64_t* bempty_bar = bfull_bar + C::kBStages;  // [kBStages] MMA commit
-  uint64_t* wfull_bar = bempty_bar + C::kBStages;  // [kWStages] nibble TMA tx
-  uint64_t* wempty_bar = wfull_bar + C::kWStages;  // [kWStages] the dequant warps that read it
-  uint64_t* scfull_bar = wempty_bar + C::kWStages; // [2] scale bulk copy tx
-  uint64_t* scempty_bar = scfull_bar + 2;          // [2] all 16 dequant warps
-  uint64_t* accfull_bar = scempty_bar + 2;         // [2] MMA commit
-  uint64_t* accempty_bar = accfull_bar + 2;        // [2] 4 epilogue warps
+  uint64_t* full_bar = bars;                        // [kASlots] A slot written (both CTAs) and its activations landed
+  uint64_t* empty_bar = full_bar + C::kASlots;      // [kASlots] MMA commit
+  uint64_t* bfull_bar = empty_bar + C::kASlots;     // [kBStages] activation TMA tx (both halves on rank 0)
+  uint64_t* bempty_bar = bfull_bar + C::kBStages;   // [kBStages] MMA commit
+  uint64_t* wfull_bar = bempty_bar + C::kBStages;   // [kWStages] nibble TMA tx
+  uint64_t* wempty_bar = wfull_bar + C::kWStages;   // [kWStages] the dequant warps that read it
+  uint64_t* scfull_bar = wempty_bar + C::kWStages;  // [2] scale bulk copy tx
+  uint64_t* scempty_bar = scfull_bar + 2;           // [2] all 16 dequant warps
+  uint64_t* accfull_bar = scempty_bar + 2;          // [2] MMA commit
+  uint64_t* accempty_bar = accfull_bar + 2;         // [2] the epilogue warps (both CTAs)
+  uint64_t* drain_bar = accempty_bar + 2;           // [1] every MMA complete
   uint32_t* misc = (uint32_t*)(smem + C::kMisc);
   volatile uint32_t* tmem_slot = misc;
   volatile uint32_t* abort_s = misc + 1;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // a pair of CTAs (cluster of two, rank 0 issues the MMAs) or one CTA works a tile
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const int32_t unit = kPair ? (int32_t)(blockIdx.x >> 1) : (int32_t)blockIdx.x;
+  const int32_t nunits = kPair ? (int32_t)(gridDim.x >> 1) : (int32_t)gridDim.x;
+  const int32_t fstride = kPair ? 2 * kBM : kBM;  // weight rows per tile
+  const int32_t fofs = (int32_t)rank * kBM;       // this CTA's first weight row in the tile
   const int32_t G = p.K >> 5;
   const int32_t nchunks = p.K / kBK;
   const int32_t nstages = (nchunks + kWChunks - 1) / kWChunks;  // nibble stages per tile
   const int32_t nastages = (nchunks + C::kAChunks - 1) / C::kAChunks;  // TMEM A stages per tile
-  const int32_t ftiles = (p.N + kBM - 1) / kBM;
+  const int32_t nbstages = (nchunks + C::kBChunks - 1) / C::kBChunks;  // activation stages per tile
+  const int32_t ftiles = (p.N + fstride - 1) / fstride;
   const int32_t total_tiles = __ldg(p.tile_ptr + p.num_experts) * ftiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kASlots; ++s) {
-      mbar_init(&full_bar[s], 4);
+      mbar_init(&full_bar[s], kPair ? 8 : 4);
       mbar_init(&empty_bar[s], 1);
     }
     for (int s = 0; s < C::kBStages; ++s) {
@@ -257,145 +352,194 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&scfull_bar[s], 1);
       mbar_init(&scempty_bar[s], kDequantWarps);
       mbar_init(&accfull_bar[s], 1);
-      mbar_init(&accempty_bar[s], 4);
+      mbar_init(&accempty_bar[s], kPair ? 8 : 4);
     }
+    mbar_init(drain_bar, 1);
     *abort_s = 0;
     fence_mbar_init();
   }
   if (warp == kMmaWarp) {
-    tmem_alloc((uint32_t*)tmem_slot, kTmemCols);
-    tmem_relinquish();
+    if (kPair) {
+      tmem_alloc_pair((uint32_t*)tmem_slot, kTmemCols);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc((uint32_t*)tmem_slot, kTmemCols);
+      tmem_relinquish();
+    }
   }
   if (warp == kActWarp && lane == 0) {
     tma_prefetch_desc(&tmap_act);
     tma_prefetch_desc(&tmap_act64);
     tma_prefetch_desc(&tmap_w);
   }
+  // barrier initialisation and the TMEM address visible to every role (and,
+  // for a pair, to the other CTA)
   tc_fence_before();
-  __syncthreads();
+  if (kPair) cluster_sync_all();
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == kActWarp) {
     // ------------------------------------------------ activation producer
     if (elect_one()) {
+      const uint32_t bfull0 = kPair ? mapa_shared(smem_u32(bfull_bar), 0) : 0u;
       uint32_t bit = 0;
-      for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
+      for (int32_t t = unit; t < total_tiles && !*abort_s; t += nunits) {
         TileInfo ti;
-        if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
-        const int32_t nbig = kSmall ? 0 : ti.nrows / kBigBoxRows;
-        const int32_t nbox = (ti.nrows - nbig * kBigBoxRows + kBoxRows - 1) / kBoxRows;
+        if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti, fstride, fofs)) continue;
+        // this CTA's token rows: all of the tile, or for a pair its half of
+        // the MMA's N (rows rounded up to 32)
+        int32_t r0 = ti.row0, rows = ti.nrows;
+        if (kPair) {
+          rows = ((ti.nrows + 31) & ~31) >> 1;
+          r0 += (int32_t)rank * rows;
+        }
+        const int32_t nbig = C::kSmall ? 0 : rows / kBigBoxRows;
+        const int32_t nbox = (rows - nbig * kBigBoxRows + kBoxRows - 1) / kBoxRows;
         const int32_t brows = nbig * kBigBoxRows + nbox * kBoxRows;  // rows landed per chunk
+
         for (int32_t c0 = 0; c0 < nchunks; c0 += C::kBChunks, ++bit) {
           const uint32_t s = bit % C::kBStages, ph = (bit / C::kBStages) & 1;
           const int32_t nq = min(C::kBChunks, nchunks - c0);
           if (!mbar_wait(&bempty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
-          mbar_arrive_expect_tx(&bfull_bar[s], (uint32_t)(nq * brows * 128));
+          // rank 0's barrier counts both halves
+          if (rank == 0) mbar_arrive_expect_tx(&bfull_bar[s], (uint32_t)(nq * brows * 128 * (kPair ? 2 : 1)));
           for (int32_t q = 0; q < nq; ++q) {
             uint8_t* dst = act_s + s * C::kActStageBytes + q * C::kActChunkBytes;
-            for (int32_t b = 0; b < nbig; ++b)
-              tma_load_2d(dst + b * kBigBoxRows * 128, &tmap_act64, (c0 + q) * kBK, ti.row0 + b * kBigBoxRows,
-                          &bfull_bar[s]);
-            for (int32_t b = 0; b < nbox; ++b)
-              tma_load_2d(dst + (nbig * kBigBoxRows + b * kBoxRows) * 128, &tmap_act, (c0 + q) * kBK,
-                          ti.row0 + nbig * kBigBoxRows + b * kBoxRows, &bfull_bar[s]);
+            const int32_t x = (c0 + q) * kBK;
+            for (int32_t b = 0; b < nbig; ++b) {
+              if (kPair)
+                tma_load_2d_pair(dst + b * kBigBoxRows * 128, &tmap_act64, x, r0 + b * kBigBoxRows, bfull0 + s * 8);
+              else
+                tma_load_2d(dst + b * kBigBoxRows * 128, &tmap_act64, x, r0 + b * kBigBoxRows, &bfull_bar[s]);
+            }
+            for (int32_t b = 0; b < nbox; ++b) {
+              uint8_t* d = dst + (nbig * kBigBoxRows + b * kBoxRows) * 128;
+              const int32_t y = r0 + nbig * kBigBoxRows + b * kBoxRows;
+              if (kPair) tma_load_2d_pair(d, &tmap_act, x, y, bfull0 + s * 8);
+              else tma_load_2d(d, &tmap_act, x, y, &bfull_bar[s]);
+            }
           }
         }
       }
     }
   } else if (warp == kWWarp) {
-    // ---------------------------------------------------- weight producer
+    // ------------------------------------- weight producer (this CTA's rows)
     if (elect_one()) {
       uint32_t wit = 0, tl = 0;
-      for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
+      for (int32_t t = unit; t < total_tiles && !*abort_s; t += nunits) {
         TileInfo ti;
-        if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
+        if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti, fstride, fofs)) continue;
         const uint32_t sb = tl & 1, sph = (tl >> 1) & 1;
         ++tl;
         if (!mbar_wait(&scempty_bar[sb], sph ^ 1, p.err, kErrTimeoutEmpty)) { *abort_s = 1; break; }
+        // rows past N (a pair's last tile when N is not a multiple of 256)
+        // load nothing; their TMEM rows decode to zeros
         const int32_t frows = min(kBM, p.N - ti.f0);
-        const uint32_t sbytes = (uint32_t)(frows * G);
-        mbar_arrive_expect_tx(&scfull_bar[sb], sbytes);
-        const uint8_t* src = p.scales + ((size_t)ti.expert * p.N + ti.f0) * G;
-        asm volatile(
-            "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                smem_u32(sc_s + sb * kScaleBytes)),
-            "l"(src), "r"(sbytes), "r"(smem_u32(&scfull_bar[sb]))
-            : "memory");
+        if (frows > 0) {
+          const uint32_t sbytes = (uint32_t)(frows * G);
+          mbar_arrive_expect_tx(&scfull_bar[sb], sbytes);
+          const uint8_t* src = p.scales + ((size_t)ti.expert * p.N + ti.f0) * G;
+          asm volatile(
+              "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                  smem_u32(sc_s + sb * kScaleBytes)),
+              "l"(src), "r"(sbytes), "r"(smem_u32(&scfull_bar[sb]))
+              : "memory");
+        } else {
+          mbar_arrive(&scfull_bar[sb]);
+        }
         const int32_t wrow = ti.expert * p.N + ti.f0;
         bool ok = true;
         for (int32_t j = 0; j < nstages; ++j, ++wit) {
           const uint32_t s = wit % C::kWStages, ph = (wit / C::kWStages) & 1;
           if (!mbar_wait(&wempty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&wfull_bar[s], kWStageBytes);  // the zero-filled tail counts too
-          tma_load_2d(w_s + s * kWStageBytes, &tmap_w, j * kWRowBytes, wrow, &wfull_bar[s]);
+          if (frows > 0) {
+            mbar_arrive_expect_tx(&wfull_bar[s], kWStageBytes);  // the zero-filled tail counts too
+            tma_load_2d(w_s + s * kWStageBytes, &tmap_w, j * kWRowBytes, wrow, &wfull_bar[s]);
+          } else {
+            mbar_arrive(&wfull_bar[s]);
+          }
         }
         if (!ok) { *abort_s = 1; break; }
       }
     }
   } else if (warp == kMmaWarp) {
-    // --------------------------------------------------------- MMA issuer
-    if (elect_one()) {
+    // ------------------------------------------ MMA issuer (a pair: rank 0)
+    if (rank == 0 && elect_one()) {
       // slot / activation-stage cursors run on across tiles, in step with the
       // dequant warpgroups (A stages) and the activation producer (stages)
       uint32_t s = 0, ph = 0, sb = 0, tl = 0;
+      bool ok = true;
       const uint64_t bdesc0 = make_sdesc_sw128(smem_u32(act_s));
-      for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
+      for (int32_t t = unit; t < total_tiles && !*abort_s; t += nunits) {
         TileInfo ti;
-        if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
-        const uint32_t n_mma = (uint32_t)((ti.nrows + 15) & ~15);
-        const uint32_t idesc = kF16 ? make_idesc_f16(kBM, n_mma) : make_idesc_bf16(kBM, n_mma);
+        if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti, fstride, fofs)) continue;
+        const uint32_t n_mma = (uint32_t)((ti.nrows + C::kNRound - 1) & ~(C::kNRound - 1));
+        const uint32_t idesc = kF16 ? make_idesc_f16(C::kMmaM, n_mma) : make_idesc_bf16(C::kMmaM, n_mma);
         const uint32_t ab = tl & 1, aph = (tl >> 1) & 1;
-        if (!mbar_wait(&accempty_bar[ab], aph ^ 1, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
+        if (!mbar_wait(&accempty_bar[ab], aph ^ 1, p.err, kErrTimeoutAccum)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ab * C::kAccCols;
-        bool ok = true;
         int32_t sub = 0, q = 0;
         for (int32_t c = 0; c < nchunks; ++c) {
           if (sub == 0) {
-            // the owning warpgroup arrives once its weights are in TMEM and the
-            // activation stage holding this A stage has landed
+            // the owning warpgroup(s) arrive once the weights are in TMEM and
+            // the activation stage holding this A stage has landed
             if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) { ok = false; break; }
             tc_fence_after();
           }
           // start-address field of the descriptor: (byte offset >> 4), no carry out of its 14 bits
           const uint64_t bdesc = bdesc0 + (uint64_t)((uint32_t)(sb * C::kActStageBytes + q * C::kActChunkBytes) >> 4);
-          tc_mma4_ts(d_tmem, tmem_base + C::kAColBase + s * C::kASlotCols + sub * 32, bdesc, idesc, c > 0 ? 1u : 0u);
+          const uint32_t a_tmem = tmem_base + C::kAColBase + s * C::kASlotCols + sub * 32;
+          if (kPair) tc_mma4_ts_pair(d_tmem, a_tmem, bdesc, idesc, c > 0 ? 1u : 0u);
+          else tc_mma4_ts(d_tmem, a_tmem, bdesc, idesc, c > 0 ? 1u : 0u);
           const bool last = c == nchunks - 1;
           if (++sub == C::kAChunks || last) {
-            tc_commit(&empty_bar[s]);
+            if (kPair) tc_commit_pair(&empty_bar[s], 3);
+            else tc_commit(&empty_bar[s]);
             sub = 0;
             if (++s == (uint32_t)C::kASlots) { s = 0; ph ^= 1u; }
           }
           if (++q == C::kBChunks || last) {
-            tc_commit(&bempty_bar[sb]);
+            if (kPair) tc_commit_pair(&bempty_bar[sb], 3);
+            else tc_commit(&bempty_bar[sb]);
             q = 0;
             if (++sb == C::kBStages) sb = 0;
           }
         }
-        if (!ok) { *abort_s = 1; break; }
-        tc_commit(&accfull_bar[ab]);
+        if (!ok) break;
+        if (kPair) tc_commit_pair(&accfull_bar[ab], 3);
+        else tc_commit(&accfull_bar[ab]);
         ++tl;
       }
+      if (!ok) *abort_s = 1;
+      // every MMA has completed before teardown frees TMEM (and, for a pair,
+      // before either CTA exits)
+      if (kPair) tc_commit_pair(drain_bar, 1);
+      else tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, p.err, kErrTimeoutOther);
     }
   } else if (warp < kDequantWarps) {
-    // --------------------------------------------- dequant: weights -> TMEM
+    // ------------------------------- dequant: this CTA's weight rows -> TMEM
     // The A stages of all tiles are numbered consecutively (gai); stage gai
     // (kAChunks chunks, both MXFP4 groups of each) is decoded by warpgroup
     // gai % 4 into TMEM slot gai % kASlots, so each slot has a single writer
     // and its empty/full phases advance in that warpgroup's program order.  A nibble
     // stage holds kAPerW A stages and is read (and released) by their
-    // kAPerW warpgroups: all four for large tiles; for small tiles two, the
+    // kAPerW warpgroups: all four for one-chunk A stages, else two, the
     // two pairs alternating stages so that one pair's barrier waits overlap
-    // the other pair's decode.
+    // the other pair's decode.  In a pair both CTAs' warpgroups arrive on
+    // rank 0's full barrier; rank 0's first wait for the stage's activations.
     const int wgi = warp >> 2;
     const int row = (warp & 3) * 32 + lane;     // weight row within the tile == TMEM lane
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t swz = (uint32_t)(row & 7);   // 128-byte swizzle of the nibble rows
+    const uint32_t full0 = kPair ? mapa_shared(smem_u32(full_bar), 0) : 0u;
     uint32_t ait = 0, wit = 0, bit = 0, tl = 0;
-    for (int32_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+    for (int32_t t = unit; t < total_tiles; t += nunits) {
       TileInfo ti;
-      if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
+      if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti, fstride, fofs)) continue;
       if (*abort_s) break;
       const uint32_t sb = tl & 1, sph = (tl >> 1) & 1;
       ++tl;
@@ -445,31 +589,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         tmem_st_wait();
         tc_fence_before();
-        {
+        if (rank == 0) {
           // the activation stage that holds chunks c0 .. c0 + kAChunks - 1
+          // (for a pair: both CTAs' halves, counted on this barrier)
           const uint32_t bsi = bit + (uint32_t)(c0 / C::kBChunks);
           ok = mbar_wait(&bfull_bar[bsi % C::kBStages], (bsi / C::kBStages) & 1u, p.err, kErrTimeoutFull);
           if (!ok) break;
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full_bar[slot]);
+        if (lane == 0) {
+          if (rank == 0) mbar_arrive(&full_bar[slot]);
+          else mbar_arrive_cluster(full0 + slot * 8);
+        }
       }
       ait += (uint32_t)nastages;
       wit += (uint32_t)nstages;
-      bit += (uint32_t)((nchunks + C::kBChunks - 1) / C::kBChunks);
+      bit += (uint32_t)nbstages;
       __syncwarp();
       if (lane == 0) mbar_arrive(&scempty_bar[sb]);
       if (!ok) { *abort_s = 1; break; }
     }
   } else {
-    // ---------------------------------------- epilogue: TMEM -> registers -> global
+    // ------------------------ epilogue: this CTA's rows, TMEM -> registers -> global
     const int q = warp - kEpiWarp0;               // TMEM lane quarter
     const int row = q * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    const uint32_t accempty0 = kPair ? mapa_shared(smem_u32(accempty_bar), 0) : 0u;
     uint32_t tl = 0;
-    for (int32_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+    for (int32_t t = unit; t < total_tiles; t += nunits) {
       TileInfo ti;
-      if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti)) continue;
+      if (!decode_tile<C::kMaxBN>(p, t, ftiles, ti, fstride, fofs)) continue;
       if (*abort_s) break;
       const uint32_t ab = tl & 1, aph = (tl >> 1) & 1;
       ++tl;
@@ -479,78 +628,34 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&accfull_bar[ab], aph, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
       __syncwarp();
       tc_fence_after();
-      const int32_t ncols = (ti.nrows + 31) & ~31;
+      const int32_t ncols = ti.f0 < p.N ? (ti.nrows + 31) & ~31 : 0;
       for (int32_t c0 = 0; c0 < ncols; c0 += 32) {
         uint32_t v[32];
         tmem_ld_x32(tmem_base + lane_base + ab * C::kAccCols + (uint32_t)c0, v);
         tmem_ld_wait();
-        if (kMode == 0) {
-          // lane pair (2j, 2j+1) holds the glu / linear rows of output feature
-          // j: the even lane finishes tokens c0..c0+15, the odd lane c0+16..31.
-          // The 32 x 16 outputs go through this warp's shared tile
-          // [token][feature] and leave as 16-byte rows of 8 features.
-          const bool odd = lane & 1;
-          uint16_t* out = (uint16_t*)p.out;
-          uint16_t* tile = (uint16_t*)(smem + C::kEpi) + q * 512;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float mine_lo = __uint_as_float(v[i]) + bias;
-            const float mine_hi = __uint_as_float(v[16 + i]) + bias;
-            const float send = odd ? mine_lo : mine_hi;
-            const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
-            const float gl = odd ? recv : mine_lo;
-            const float li = odd ? mine_hi : recv;
-            const float g = fminf(gl, p.limit);
-            const float l = fmaxf(fminf(li, p.limit), -p.limit);
-            // g * sigmoid(alpha * g); a huge denominator gives 0, the limit
-            const float gs = __fdividef(g, 1.0f + __expf(-(p.alpha * g)));
-            const float y = gs * (l + 1.0f);
-            const int tok = i + (odd ? 16 : 0);
-            tile[tok * 16 + (lane >> 1)] = kF16 ? __half_as_ushort(__float2half_rn(y)) : f32_to_bf16_bits(y);
-          }
-          __syncwarp();
-          const bool warp_rows_ok = ti.f0 + q * 32 + 32 <= p.N;
-#pragma unroll
-          for (int k = 0; k < 2; ++k) {
-            const int tok = lane, h = k ^ ((lane >> 2) & 1);  // alternate halves: no bank conflicts
-            const int32_t col = c0 + tok;
-            const uint4 val = *(const uint4*)(tile + tok * 16 + h * 8);
-            const int32_t f = (ti.f0 >> 1) + q * 16 + h * 8;  // first output feature of the 8
-            if (col < ti.nrows) {
-              uint16_t* dst = out + (size_t)(ti.row0 + col) * p.ldo + f;
-              if (warp_rows_ok) {
-                *(uint4*)dst = val;
-              } else {
-                const uint16_t* e = (const uint16_t*)&val;
-                for (int u = 0; u < 8; ++u)
-                  if (2 * (f + u) < p.N) dst[u] = e[u];
-              }
-            }
-          }
-          __syncwarp();
-        } else {
-          float* out = (float*)p.out;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int32_t col = c0 + j;
-            if (row_ok && col < ti.nrows)
-              out[(size_t)(ti.row0 + col) * p.ldo + frow] = __uint_as_float(v[j]) + bias;
-          }
-        }
+        epilogue_block<kMode, kF16>(p, ti, v, c0, q, lane, bias, row_ok, frow,
+                                    (uint16_t*)(smem + C::kEpi) + q * 512);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&accempty_bar[ab]);
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(&accempty_bar[ab]);
+        else mbar_arrive_cluster(accempty0 + ab * 8);
+      }
     }
   }
 
-  // ---- teardown: everyone drains, then the allocating warp frees TMEM
+  // ---- teardown: every role drains (the MMAs have completed), then the
+  // allocating warp(s) free TMEM
+  __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  if (kPair) cluster_sync_all();
+  else __syncthreads();
   if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    if (kPair) tmem_dealloc_pair(tmem_base, kTmemCols);
+    else tmem_dealloc(tmem_base, kTmemCols);
   }
 }
 
@@ -601,16 +706,58 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 
 
 
-template <int kMode, bool kF16, bool kSmall>
+template <int kMode, bool kF16, int kVar>
 static void launch_variant(const CUtensorMap& ta, const CUtensorMap& ta64, const CUtensorMap& tw, const GemmParams& p,
                            int grid, cudaStream_t stream) {
-  const int smem = GemmCfg<kSmall>::kAlloc;
+  const int smem = GemmCfg<kVar>::kAlloc;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(moe_gemm_tc_kernel<kMode, kF16, kSmall>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(moe_gemm_tc_kernel<kMode, kF16, kVar>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr = true;
   }
-  moe_gemm_tc_kernel<kMode, kF16, kSmall><<<grid, kGemmThreads, smem, stream>>>(ta, ta64, tw, p);
+  moe_gemm_tc_kernel<kMode, kF16, kVar><<<grid, kGemmThreads, smem, stream>>>(ta, ta64, tw, p);
+}
+
+// Clusters of two CTAs, at most as many as fit at once (one CTA per SM);
+// returns false when no cluster fits, so the caller can use the single-CTA form.
+template <int kMode, bool kF16>
+static bool launch_pair(const CUtensorMap& ta, const CUtensorMap& ta64, const CUtensorMap& tw, const GemmParams& p,
+                        int grid, cudaStream_t stream) {
+  auto kern = moe_gemm_tc_kernel<kMode, kF16, kVarPair>;
+  const int smem = GemmCfg<kVarPair>::kAlloc;
+  static int max_pairs = -1;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (max_pairs < 0) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cfg.gridDim = dim3((unsigned)(grid & ~1));
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    max_pairs = n;
+  }
+  const int pairs = grid / 2 < max_pairs ? grid / 2 : max_pairs;
+  if (pairs <= 0) return false;
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
+  return cudaLaunchKernelEx(&cfg, kern, ta, ta64, tw, p) == cudaSuccess;
+}
+
+// Prefill-sized tiles run on CTA pairs unless GPTOSS_MOE_PAIR=0 (the
+// single-CTA form, kept for comparison and as the fallback).
+static bool pair_enabled() {
+  const char* e = getenv("GPTOSS_MOE_PAIR");
+  return !(e && e[0] == '0');
 }
 
 int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
@@ -649,21 +796,32 @@ int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
   p.err = L.err;
   // the token-tile plan used the same rule (moe_tile_rows_max) for these rows
   const bool small = moe_tile_rows_max(L.act_rows, L.E) <= kMoeTileRowsSmall;
+  if (!small && pair_enabled()) {
+    bool launched;
+    if (mode == 0)
+      launched = L.f16 ? launch_pair<0, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream)
+                       : launch_pair<0, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+    else
+      launched = L.f16 ? launch_pair<1, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream)
+                       : launch_pair<1, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+    if (launched) return 0;
+    (void)cudaGetLastError();
+  }
   if (mode == 0) {
     if (small) {
-      if (L.f16) launch_variant<0, true, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
-      else launch_variant<0, false, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      if (L.f16) launch_variant<0, true, kVarSmall>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      else launch_variant<0, false, kVarSmall>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
     } else {
-      if (L.f16) launch_variant<0, true, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
-      else launch_variant<0, false, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      if (L.f16) launch_variant<0, true, kVarLarge>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      else launch_variant<0, false, kVarLarge>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
     }
   } else {
     if (small) {
-      if (L.f16) launch_variant<1, true, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
-      else launch_variant<1, false, true>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      if (L.f16) launch_variant<1, true, kVarSmall>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      else launch_variant<1, false, kVarSmall>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
     } else {
-      if (L.f16) launch_variant<1, true, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
-      else launch_variant<1, false, false>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      if (L.f16) launch_variant<1, true, kVarLarge>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
+      else launch_variant<1, false, kVarLarge>(tmap_act, tmap_act64, tmap_w, p, L.grid, stream);
     }
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
