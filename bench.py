@@ -43,7 +43,7 @@ METRIC = "MoE-layer tokens/s (gpt-oss-120b MoE layer, 8192-token prefill)"
 FP4_DENSE_PEAK_TFLOPS = 9000.0  # nominal dense e2m1 tensor peak of one B200
 # DRAM bytes (read + write) of one gate/up GEMM launch at the 8192-token workload, from the
 # ncu capture summarised in profiles/moe_gemm_config3_prefill.md
-MLP1_DRAM_TRAFFIC_BYTES = 1.319516e9 + 0.183879e9
+MLP1_DRAM_TRAFFIC_BYTES = 1.335910e9 + 0.181591e9
 
 
 def measured_peaks():
