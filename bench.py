@@ -150,7 +150,7 @@ def run_b200(args):
     blk.prepare()  # one-time weight check (enables the f16 GEMM path for these scale codes)
     x = torch.randn(TOKENS, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
     out = torch.empty_like(x)
-    runner = ep.ExpertParallelMoE(blk, TOKENS) if ep else None
+    runner = ep.ExpertParallelMoE(blk, TOKENS, peer=args.exchange == "peer") if ep else None
 
     def step():
         if runner is not None:
@@ -280,6 +280,8 @@ def run_b200(args):
             "config": {"workload": "gpt-oss-120b MoE layer prefill (configs[3])", "tokens_per_gpu": TOKENS,
                        "num_experts": NUM_EXPERTS, "experts_per_gpu": E_local, "top_k": TOP_K, "hidden": HIDDEN,
                        "intermediate": INTER, "parallelism": f"ep{world}" if world > 1 else "single",
+                       **({"exchange": "peer memory (CUDA IPC buffers, NVLink stores)" if args.exchange == "peer"
+                           else "NCCL all-to-all-v"} if world > 1 else {}),
                        "l2": "no flush: 1.7 GB of expert weights per step exceed the 126 MB L2"},
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": TOKENS * HIDDEN * 2, "d2h_bytes_per_step": TOKENS * HIDDEN * 2,
@@ -564,6 +566,8 @@ def main():
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU (default: the configs[3] 8192)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-decode", dest="decode", action="store_false", help="skip the MoE decode measurements")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="expert-parallel row exchange (N > 1): stores into the ranks' IPC-shared buffers or NCCL")
     ap.add_argument("--decode-only", type=int, default=None, choices=range(len(DECODE_CASES)),
                     help="run only this decode case (index into DECODE_CASES) and print its measurement")
     args = ap.parse_args()

@@ -65,6 +65,14 @@ SIGNATURES = {
     "gptoss_attn_sink_rescale": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P]),
     "gptoss_moe_plan_tiles": (ctypes.c_int, [_P, _I32, _P, _P, _P]),
     "gptoss_moe_segment_copy": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I64, _I32, _P, _P]),
+    "gptoss_ipc_alloc": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(_P), _P]),
+    "gptoss_ipc_open": (ctypes.c_int, [_P, ctypes.POINTER(_P)]),
+    "gptoss_ipc_close": (ctypes.c_int, [_P]),
+    "gptoss_ipc_free": (ctypes.c_int, [_P]),
+    "gptoss_moe_dispatch_peer": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _I64,
+                                                _I32, _P]),
+    "gptoss_moe_mlp2_peer": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _I32,
+                                            _I64, _I32, _P, _P]),
 }
 
 _lib = None

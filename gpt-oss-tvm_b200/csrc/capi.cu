@@ -144,6 +144,111 @@ int gptoss_moe_mlp2(const uint16_t* y, int64_t act_rows, const int32_t* indptr, 
                      act_f16, err, stream);
 }
 
+int gptoss_moe_mlp2_peer(const uint16_t* y, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
+                         const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
+                         const uint8_t* scales, const uint16_t* bias, int32_t act_f16, const int32_t* origin,
+                         void* const* peer_back, int32_t num_ranks, int64_t back_rows, int32_t back_bf16,
+                         uint32_t* err, void* stream) {
+  if (act_rows <= 0) return 0;
+  if (!origin || !peer_back || num_ranks < 1 || num_ranks > kMaxPeerRanks)
+    return fail(-1, "moe_mlp2_peer: origin, peer_back and 1 <= num_ranks <= %d required", kMaxPeerRanks);
+  if (E <= 0 || H <= 0 || I <= 0 || I % 64)
+    return fail(-1, "moe_mlp2_peer: I must be a positive multiple of 64 (got %d)", I);
+  if (((uintptr_t)y & 15) || ((uintptr_t)blocks & 15) || ((uintptr_t)scales & 15))
+    return fail(-1, "moe_mlp2_peer: y, blocks and scales must be 16-byte aligned");
+  GemmLaunch L;
+  L.act = y;
+  L.act_rows = act_rows;
+  L.blocks = blocks;
+  L.scales = scales;
+  L.bias = bias;
+  L.indptr = indptr;
+  L.tile_ptr = tile_ptr;
+  L.tile_rows = tile_rows;
+  L.out = nullptr;
+  L.E = E;
+  L.N = H;
+  L.K = I;
+  L.ldo = H;
+  L.alpha = 0.f;
+  L.limit = 0.f;
+  L.err = err;
+  L.grid = num_sms();
+  L.f16 = act_f16 ? 1 : 0;
+  L.row_dst = origin;
+  for (int i = 0; i < num_ranks; ++i) L.peer_out[i] = peer_back[i];
+  L.peer_out_rows = back_rows;
+  L.out_bf16 = back_bf16 ? 1 : 0;
+  return check_launch(launch_moe_gemm(1, L, GPTOSS_STREAM(stream)), "moe_mlp2_peer");
+}
+
+int gptoss_moe_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, const int32_t* expert_of_row,
+                             const int32_t* indptr, int64_t rows, int32_t H, int32_t num_experts,
+                             int32_t local_experts, int32_t rank, const int32_t* dst_base, void* const* peer_rows,
+                             int32_t* const* peer_origin, int32_t num_ranks, int64_t cap_rows, int32_t to_f16,
+                             void* stream) {
+  if (rows > 0 && (!peer_rows || !peer_origin || !dst_base))
+    return fail(-1, "moe_dispatch_peer: peer_rows, peer_origin and dst_base required");
+  return check_launch(launch_dispatch_peer(t, token_of_row, expert_of_row, indptr, rows, H, num_experts,
+                                           local_experts, rank, dst_base, peer_rows, peer_origin, num_ranks,
+                                           cap_rows, to_f16, GPTOSS_STREAM(stream)),
+                      "moe_dispatch_peer");
+}
+
+int gptoss_ipc_alloc(uint64_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(-1, "ipc_alloc: null output or zero size");
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(-4, "ipc_alloc: cudaMalloc(%llu) failed", (unsigned long long)bytes);
+  }
+  // zero-filled: an origin word never written decodes to a valid (rank 0, row 0)
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return fail(-4, "ipc_alloc: cudaMemset failed");
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, *ptr) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return fail(-4, "ipc_alloc: cudaIpcGetMemHandle failed");
+  }
+  static_assert(sizeof(h) == 64, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return 0;
+}
+
+int gptoss_ipc_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(-1, "ipc_open: null handle or output");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    const cudaError_t e = cudaGetLastError();
+    return fail(-4, "ipc_open: cudaIpcOpenMemHandle failed (%s)", cudaGetErrorString(e));
+  }
+  return 0;
+}
+
+int gptoss_ipc_close(void* ptr) {
+  if (ptr && cudaIpcCloseMemHandle(ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(-4, "ipc_close: cudaIpcCloseMemHandle failed");
+  }
+  return 0;
+}
+
+int gptoss_ipc_free(void* ptr) {
+  if (ptr && cudaFree(ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(-4, "ipc_free: cudaFree failed");
+  }
+  return 0;
+}
+
 int gptoss_moe_weights_prepare(gptoss_moe_weights* w, void* stream) {
   if (!w) return fail(-1, "gptoss_moe_weights_prepare: null weights");
   const int64_t El = w->num_local_experts;

@@ -7,6 +7,9 @@
 
 namespace gptoss {
 
+// Ranks of one expert-parallel group whose memory the peer kernels address.
+constexpr int kMaxPeerRanks = 8;
+
 // Arguments of one grouped expert GEMM (moe_gemm.cu).
 struct GemmLaunch {
   const uint16_t* act;   // [act_rows, K] bf16 or f16, expert-major rows
@@ -23,6 +26,12 @@ struct GemmLaunch {
   uint32_t* err;
   int grid;
   int f16;  // 1: f16 activations and hardware e2m1 -> f16 weight decode
+  // mode 1 only, optional: output row r goes to row (row_dst[r] & 0xFFFFFF) of
+  // peer_out[row_dst[r] >> 24] (row stride ldo), as bf16 when out_bf16
+  const int32_t* row_dst = nullptr;
+  void* peer_out[kMaxPeerRanks] = {};
+  int64_t peer_out_rows = 0;  // rows of each peer_out buffer; stores beyond it are dropped
+  int out_bf16 = 0;
 };
 int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream);
 
@@ -44,6 +53,12 @@ int launch_segment_copy(const void*, void*, const int32_t*, int32_t, int32_t, in
                         cudaStream_t);
 int launch_weight_ranges(const uint8_t* s1, int64_t n1, const uint8_t* s2, int64_t n2, const uint16_t* norm_w,
                          int32_t H, uint32_t* out4, cudaStream_t);
+
+// moe_peer.cu
+int launch_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, const int32_t* expert_of_row,
+                         const int32_t* indptr, int64_t rows, int32_t H, int32_t E, int32_t El, int32_t rank,
+                         const int32_t* dst_base, void* const* peer_rows, int32_t* const* peer_origin,
+                         int32_t num_ranks, int64_t cap_rows, int32_t to_f16, cudaStream_t s);
 
 // attention.cu
 int launch_qkv_rope(const uint16_t* qkv, const int32_t* pos, const int32_t* slot, int64_t S, int32_t Hq, int32_t Hkv,

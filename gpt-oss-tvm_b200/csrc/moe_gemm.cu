@@ -112,8 +112,8 @@ struct GemmCfg {
   static constexpr int kBar = kScale + 2 * kScaleBytes;
   static constexpr int kNumBars = 2 * kASlots + 2 * kBStages + 2 * kWStages + 4 + 4 + 1;
   static constexpr int kMisc = kBar + kNumBars * 8;
-  static constexpr int kEpi = (kMisc + 64 + 15) & ~15;  // 4 epilogue warps x (32 tokens x 16 outputs x 2 B)
-  static constexpr int kAlloc = kEpi + 4 * 1024 + 1024;  // + slack for manual 1024 B alignment
+  static constexpr int kEpi = (kMisc + 64 + 15) & ~15;  // 4 epilogue warps x (32 tokens x 32 features x 2 B)
+  static constexpr int kAlloc = kEpi + 4 * 2048 + 1024;  // + slack for manual 1024 B alignment
   static_assert(kW % 1024 == 0 && kActChunkBytes % 1024 == 0, "128-byte swizzle atoms stay 1024-aligned");
   static_assert(kAlloc <= 227 * 1024, "shared memory budget");
 };
@@ -131,6 +131,12 @@ struct GemmParams {
   int32_t ldo;               // output row stride in elements
   float alpha, limit;        // SwiGLU constants (mode 0)
   uint32_t* err;
+  // mode 1, optional: row r of the output goes to row (row_dst[r] & 0xFFFFFF)
+  // of peer_out[row_dst[r] >> 24] (another GPU's memory), bf16 if out_bf16
+  const int32_t* row_dst;
+  void* peer_out[kMaxPeerRanks];
+  int64_t peer_out_rows;
+  int32_t out_bf16;
 };
 
 struct TileInfo {
@@ -233,7 +239,9 @@ __device__ __forceinline__ void decode_group(const uint4 nb, uint32_t sc, bool r
 // thread holds weight row `frow` (TMEM lane q * 32 + lane) for tokens
 // c0 .. c0 + 31 of the tile in v[].  Mode 0 applies the clamped SwiGLU to
 // (glu, linear) lane pairs and stores bf16 (f16) outputs through the warp's
-// shared tile; mode 1 stores fp32.
+// shared tile; mode 1 stores fp32, or scatters the rows to other GPUs'
+// return buffers (bf16 through the shared tile, or fp32).  `tile`: the warp's
+// 2 KB of shared memory.
 template <int kMode, bool kF16>
 __device__ __forceinline__ void epilogue_block(const GemmParams& p, const TileInfo& ti, const uint32_t (&v)[32],
                                                int32_t c0, int q, int lane, float bias, bool row_ok, int32_t frow,
@@ -281,6 +289,53 @@ __device__ __forceinline__ void epilogue_block(const GemmParams& p, const TileIn
       }
     }
     __syncwarp();
+  } else if (p.row_dst != nullptr && p.out_bf16) {
+    // each token row to its owner's return buffer, bf16: the warp's 32
+    // features x 32 tokens go through its shared tile [token][feature] and
+    // leave as 16-byte pieces (8 features of one token per lane, 8 tokens per
+    // instruction) instead of 2-byte stores
+    const int32_t mine = c0 + lane < ti.nrows ? __ldg(p.row_dst + ti.row0 + c0 + lane) : 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      tile[j * 32 + lane] = row_ok ? f32_to_bf16_bits(__uint_as_float(v[j]) + bias) : (uint16_t)0;
+    __syncwarp();
+    const int32_t fq = lane & 3;                        // 8-feature piece of the warp's 32 features
+    const int32_t f = ti.f0 + q * 32 + fq * 8;          // its first feature
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int32_t tok = (lane >> 2) + 8 * k;
+      const uint32_t o = (uint32_t)__shfl_sync(0xffffffffu, mine, tok);
+      const uint32_t peer = o >> 24, orow = o & 0xFFFFFFu;
+      void* base = peer < (uint32_t)kMaxPeerRanks ? p.peer_out[peer] : nullptr;
+      if (c0 + tok < ti.nrows && base != nullptr && (int64_t)orow < p.peer_out_rows && f < p.N) {
+        const uint4 val = *(const uint4*)(tile + tok * 32 + fq * 8);
+        uint16_t* dst = (uint16_t*)base + (size_t)orow * p.ldo + f;
+        if (f + 8 <= p.N) {
+          *(uint4*)dst = val;
+        } else {
+          const uint16_t* e = (const uint16_t*)&val;
+          for (int u = 0; u < 8 && f + u < p.N; ++u) dst[u] = e[u];
+        }
+      }
+    }
+    __syncwarp();
+  } else if (p.row_dst != nullptr) {
+    // fp32 rows to their owners' return buffers: the 32 lanes store 32
+    // consecutive features of one row per instruction
+    const int32_t mine = c0 + lane < ti.nrows ? __ldg(p.row_dst + ti.row0 + c0 + lane) : 0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int32_t col = c0 + j;
+      const uint32_t o = (uint32_t)__shfl_sync(0xffffffffu, mine, j);
+      const uint32_t peer = o >> 24, orow = o & 0xFFFFFFu;
+      void* base = peer < (uint32_t)kMaxPeerRanks ? p.peer_out[peer] : nullptr;
+      if (row_ok && col < ti.nrows && base != nullptr && (int64_t)orow < p.peer_out_rows) {
+        const size_t at = (size_t)orow * p.ldo + frow;
+        const float y = __uint_as_float(v[j]) + bias;
+        if (p.out_bf16) ((uint16_t*)base)[at] = f32_to_bf16_bits(y);
+        else ((float*)base)[at] = y;
+      }
+    }
   } else {
     float* out = (float*)p.out;
 #pragma unroll
@@ -637,7 +692,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_ld_x32(tmem_base + lane_base + ab * C::kAccCols + (uint32_t)c0, v);
         tmem_ld_wait();
         epilogue_block<kMode, kF16>(p, ti, v, c0, q, lane, bias, row_ok, frow,
-                                    (uint16_t*)(smem + C::kEpi) + q * 512);
+                                    (uint16_t*)(smem + C::kEpi) + q * 1024);
       }
       tc_fence_before();
       __syncwarp();
@@ -646,6 +701,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         else mbar_arrive_cluster(accempty0 + ab * 8);
       }
     }
+    // rows stored into other GPUs' memory are visible there before the
+    // collective that follows the kernel
+    if (kMode == 1 && p.row_dst != nullptr) __threadfence_system();
   }
 
   // ---- teardown: every role drains (the MMAs have completed), then the
@@ -797,6 +855,10 @@ int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
   p.alpha = L.alpha;
   p.limit = L.limit;
   p.err = L.err;
+  p.row_dst = mode == 1 ? L.row_dst : nullptr;
+  for (int i = 0; i < kMaxPeerRanks; ++i) p.peer_out[i] = L.peer_out[i];
+  p.peer_out_rows = L.peer_out_rows;
+  p.out_bf16 = L.out_bf16;
   // the token-tile plan used the same rule (moe_tile_rows_max) for these rows
   const bool small = moe_tile_rows_max(L.act_rows, L.E) <= kMoeTileRowsSmall;
   if (!small && pair_enabled()) {

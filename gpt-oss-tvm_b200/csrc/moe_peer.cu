@@ -1,0 +1,86 @@
+// moe_peer.cu -- expert-parallel data movement over peer memory (NVLink).
+//
+// The expert-parallel MoE block (gpt-oss-tvm_b200/ep.py) shards the experts of
+// the block over the ranks of one node (one process per GPU).  Instead of
+// all-to-all exchanges through NCCL plus reorder passes, each rank writes the
+// rows straight into the rank that uses them:
+//   * dispatch: the token row of every (token, expert) pair is stored into
+//     the owning rank's expert-major activation matrix at its final row, in
+//     the GEMM's activation type, together with the row's origin;
+//   * return: the down-projection GEMM's epilogue stores each output row into
+//     the return buffer of the rank that owns the token (moe_gemm.cu).
+// Buffers are plain cudaMalloc allocations shared with cudaIpc handles; the
+// kernels use ordinary stores to peer addresses (no multicast, no waits on
+// other GPUs).  Ordering between ranks is the host's: every writing kernel
+// ends with a system-scope fence and the ranks meet at a collective before
+// the rows are read.
+#include "common.cuh"
+#include "launch.h"
+
+namespace gptoss {
+
+struct PeerRows {
+  void* rows[kMaxPeerRanks];      // per destination rank: activation matrix [cap_rows, H]
+  int32_t* origin[kMaxPeerRanks];  // per destination rank: origin of each row (rank << 24 | send row)
+};
+
+// Send row r (this rank's expert-major order over the global experts) of
+// expert eg goes to rank d = eg / El, local expert e = eg % El, row
+// dst_base[d * El + e] + (r - indptr[eg]): the block of this rank's rows of
+// expert e on rank d, in this rank's order.  One warp per row, 16-byte
+// pieces, bf16 -> f16 on the way for the f16 GEMM path (as gather_rows_kernel).
+template <bool kToF16>
+__global__ void dispatch_peer_kernel(const uint16_t* __restrict__ t, const int32_t* __restrict__ token_of_row,
+                                     const int32_t* __restrict__ expert_of_row, const int32_t* __restrict__ indptr,
+                                     int64_t rows, int32_t H, int32_t E, int32_t El, int32_t rank,
+                                     const int32_t* __restrict__ dst_base, int64_t cap_rows, const PeerRows peers) {
+  const int64_t r = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int32_t eg = expert_of_row[r];
+  if (eg < 0 || eg >= E) return;  // routing errors are reported by the router
+  const int32_t d = eg / El, e = eg - d * El;
+  const int64_t dst = (int64_t)dst_base[d * El + e] + (r - indptr[eg]);
+  if (dst < 0 || dst >= cap_rows) return;  // (capacities hold every rank's rows)
+  const uint4* s = (const uint4*)(t + (int64_t)token_of_row[r] * H);
+  uint4* o = (uint4*)((uint16_t*)peers.rows[d] + dst * H);
+  for (int32_t i = lane; i < H / 8; i += 32) {
+    uint4 v = s[i];
+    if (kToF16) {
+      uint32_t* w = (uint32_t*)&v;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const __half2 h = __floats2half2_rn(__uint_as_float(w[q] << 16), __uint_as_float(w[q] & 0xFFFF0000u));
+        w[q] = *(const uint32_t*)&h;
+      }
+    }
+    o[i] = v;
+  }
+  if (lane == 0) peers.origin[d][dst] = (rank << 24) | (int32_t)r;
+  __threadfence_system();
+}
+
+int launch_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, const int32_t* expert_of_row,
+                         const int32_t* indptr, int64_t rows, int32_t H, int32_t E, int32_t El, int32_t rank,
+                         const int32_t* dst_base, void* const* peer_rows, int32_t* const* peer_origin,
+                         int32_t num_ranks, int64_t cap_rows, int32_t to_f16, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  if (H % 8 || num_ranks < 1 || num_ranks > kMaxPeerRanks || El <= 0 || E != El * num_ranks || rank < 0 ||
+      rank >= num_ranks || rows >= (1 << 24))
+    return -12;
+  PeerRows pr;
+  for (int i = 0; i < kMaxPeerRanks; ++i) {
+    pr.rows[i] = i < num_ranks ? peer_rows[i] : nullptr;
+    pr.origin[i] = i < num_ranks ? peer_origin[i] : nullptr;
+  }
+  const unsigned blocks = (unsigned)((rows + 7) / 8);
+  if (to_f16)
+    dispatch_peer_kernel<true><<<blocks, 256, 0, s>>>(t, token_of_row, expert_of_row, indptr, rows, H, E, El, rank,
+                                                       dst_base, cap_rows, pr);
+  else
+    dispatch_peer_kernel<false><<<blocks, 256, 0, s>>>(t, token_of_row, expert_of_row, indptr, rows, H, E, El, rank,
+                                                        dst_base, cap_rows, pr);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+}  // namespace gptoss

@@ -248,6 +248,50 @@ int gptoss_moe_segment_copy(const void* src, void* dst, const int32_t* counts, i
 int gptoss_moe_combine_bf16(const uint16_t* h2, const int32_t* row_of_pair, const uint16_t* topk_weights,
                             const uint16_t* x, int64_t M, int32_t K, int32_t H, uint16_t* out, void* stream);
 
+/* ----------------------------------------- expert parallelism over peer memory
+ * No counterpart in the reference (it runs the block on one device).  The
+ * ranks of one node share buffers through CUDA IPC and write each other's
+ * rows directly (plain stores over NVLink; no multicast, no device-side
+ * waits on other GPUs).  The caller orders the ranks: every writing call
+ * ends with a system-scope fence, and the ranks meet at a collective before
+ * the written rows are read or written again. */
+
+/* cudaMalloc of `bytes` on the current device, zero-filled; its IPC handle
+ * (64 bytes) in `handle`.  Free with gptoss_ipc_free. */
+int gptoss_ipc_alloc(uint64_t bytes, void** ptr, void* handle);
+/* Map another process's allocation from its 64-byte handle (peer access
+ * enabled); unmap with gptoss_ipc_close. */
+int gptoss_ipc_open(const void* handle, void** ptr);
+int gptoss_ipc_close(void* ptr);
+int gptoss_ipc_free(void* ptr);
+
+/* Expert-parallel dispatch: for every send row r of this rank (the
+ * expert-major order of gptoss_moe_permute over the global experts), with
+ * eg = expert_of_row[r], d = eg / local_experts, e = eg % local_experts:
+ *   rank d's rows[dst] = t[token_of_row[r]] (f16 when to_f16), and
+ *   rank d's origin[dst] = (rank << 24) | r,
+ * dst = dst_base[d * local_experts + e] + r - indptr[eg] (device int32
+ * [num_ranks * local_experts]).  peer_rows / peer_origin: host arrays of
+ * num_ranks device pointers (this rank's own buffers at index `rank`), each
+ * buffer holding cap_rows rows of H elements / cap_rows int32.  num_ranks <= 8,
+ * rows < 2^24. */
+int gptoss_moe_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, const int32_t* expert_of_row,
+                             const int32_t* indptr, int64_t rows, int32_t H, int32_t num_experts,
+                             int32_t local_experts, int32_t rank, const int32_t* dst_base, void* const* peer_rows,
+                             int32_t* const* peer_origin, int32_t num_ranks, int64_t cap_rows, int32_t to_f16,
+                             void* stream);
+
+/* gptoss_moe_mlp2 whose output row r goes to row (origin[r] & 0xFFFFFF) of
+ * peer_back[origin[r] >> 24] (row stride H): fp32, or bf16 (rounded to
+ * nearest even) when back_bf16.  peer_back: host array of num_ranks device
+ * pointers (<= 8), each holding back_rows rows (a row index beyond it, or a
+ * rank beyond num_ranks, is dropped). */
+int gptoss_moe_mlp2_peer(const uint16_t* y, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
+                         const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
+                         const uint8_t* scales, const uint16_t* bias, int32_t act_f16, const int32_t* origin,
+                         void* const* peer_back, int32_t num_ranks, int64_t back_rows, int32_t back_bf16,
+                         uint32_t* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

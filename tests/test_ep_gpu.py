@@ -1,9 +1,13 @@
-"""Expert parallelism on 2+ GPUs (NCCL).  With the fp32 return path every
-rank's output equals the single-GPU MLPBlock output for the same tokens, bit
-for bit (the same kernels run on the same rows; only the rows' placement
-differs).  With the default bf16 return path (expert outputs rounded to bf16
-before the weighted combine) the output is within the block's tolerance of
-the single-GPU one: max |diff| / max |ref| <= 2e-2, cosine >= 0.9995."""
+"""Expert parallelism on 2+ GPUs, both ways of moving the rows: NCCL
+all-to-all-v (peer=False) and stores into the other ranks' IPC-shared
+buffers (peer=True, the default).  With the fp32 return path every rank's
+output equals the single-GPU MLPBlock output for the same tokens, bit for bit
+(the same kernels run on the same rows; only the rows' placement differs).
+With the default bf16 return path (expert outputs rounded to bf16 before the
+weighted combine) the output is within the block's tolerance of the
+single-GPU one: max |diff| / max |ref| <= 2e-2, cosine >= 0.9995; and the two
+ways of moving the rows give the same bits.  Every run does two steps (the
+second reuses every buffer)."""
 import os
 import socket
 
@@ -27,7 +31,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, E, M, exact, q):
+def _worker(rank, world, port, E, M, exact, peer, q):
     import datetime
     import importlib
     import sys
@@ -52,27 +56,36 @@ def _worker(rank, world, port, E, M, exact, q):
         full = mlp.MLPBlock(cfg, device=dev).load_state(p)
         x = synth.activations(M, seed=100 + rank)
         xd = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(dev)
-        runner = ep.ExpertParallelMoE(blk, M, exact_return=exact)
-        out = runner.forward(xd)
+        runner = ep.ExpertParallelMoE(blk, M, exact_return=exact, peer=peer)
+        other = ep.ExpertParallelMoE(blk, M, exact_return=exact, peer=not peer)
+        for step in range(2):
+            if step:
+                x = synth.activations(M, seed=200 + rank)
+                xd = torch.from_numpy(x.view(np.int16)).view(torch.bfloat16).to(dev)
+            out = runner.forward(xd).clone()
+            out_other = other.forward(xd)
         ref = full.forward(xd)
         torch.cuda.synchronize()
         same = bool(torch.equal(out.view(torch.int16), ref.view(torch.int16)))
+        same_paths = bool(torch.equal(out.view(torch.int16), out_other.view(torch.int16)))
         # compare the MoE part (output minus the residual input)
         d, r = (out.float() - xd.float()).flatten(), (ref.float() - xd.float()).flatten()
         rel = float((d - r).abs().max() / r.abs().max().clamp_min(1e-30))
         cos = float(torch.dot(d, r) / (d.norm() * r.norm()).clamp_min(1e-30))
-        q.put((rank, same, rel, cos, runner.last_splits))
+        q.put((rank, same, rel, cos, same_paths))
         dist.barrier()
+        runner.close()
+        other.close()
     finally:
         dist.destroy_process_group()
 
 
-def _run(M, exact):
+def _run(M, exact, peer=True):
     world = 2
     ctx = torch.multiprocessing.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, 16, M, exact, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, 16, M, exact, peer, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(world)]
@@ -82,13 +95,16 @@ def _run(M, exact):
     return res
 
 
+@pytest.mark.parametrize("peer", [True, False], ids=["peer", "nccl"])
 @pytest.mark.parametrize("M", [1, 300])
-def test_expert_parallel_exact_return_matches_single_gpu(M):
-    for rank, same, rel, cos, splits in _run(M, True):
+def test_expert_parallel_exact_return_matches_single_gpu(M, peer):
+    for rank, same, rel, cos, same_paths in _run(M, True, peer):
         assert same, f"rank {rank}: EP output differs from single-GPU (rel {rel}, cos {cos})"
+        assert same_paths, f"rank {rank}: peer and NCCL paths differ"
 
 
 @pytest.mark.parametrize("M", [1, 300])
 def test_expert_parallel_bf16_return_within_tolerance(M):
-    for rank, same, rel, cos, splits in _run(M, False):
+    for rank, same, rel, cos, same_paths in _run(M, False, True):
         assert rel <= 2e-2 and cos >= 0.9995, f"rank {rank}: rel {rel:.3e}, cos {cos:.6f}"
+        assert same_paths, f"rank {rank}: peer and NCCL paths differ"
