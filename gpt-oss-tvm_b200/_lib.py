@@ -69,6 +69,7 @@ SIGNATURES = {
     "gptoss_ipc_open": (ctypes.c_int, [_P, ctypes.POINTER(_P)]),
     "gptoss_ipc_close": (ctypes.c_int, [_P]),
     "gptoss_ipc_free": (ctypes.c_int, [_P]),
+    "gptoss_moe_peer_layout": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P]),
     "gptoss_moe_dispatch_peer": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P, _P, _I32, _I64,
                                                 _I32, _P]),
     "gptoss_moe_mlp2_peer": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _I32,

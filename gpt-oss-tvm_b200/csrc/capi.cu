@@ -182,6 +182,13 @@ int gptoss_moe_mlp2_peer(const uint16_t* y, int64_t act_rows, const int32_t* ind
   return check_launch(launch_moe_gemm(1, L, GPTOSS_STREAM(stream)), "moe_mlp2_peer");
 }
 
+int gptoss_moe_peer_layout(const int32_t* counts_all, int32_t num_ranks, int32_t local_experts, int32_t rank,
+                           int32_t* dst_base, int32_t* indptr_local, void* stream) {
+  return check_launch(launch_peer_layout(counts_all, num_ranks, local_experts, rank, dst_base, indptr_local,
+                                         GPTOSS_STREAM(stream)),
+                      "moe_peer_layout");
+}
+
 int gptoss_moe_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, const int32_t* expert_of_row,
                              const int32_t* indptr, int64_t rows, int32_t H, int32_t num_experts,
                              int32_t local_experts, int32_t rank, const int32_t* dst_base, void* const* peer_rows,

@@ -55,6 +55,8 @@ int launch_weight_ranges(const uint8_t* s1, int64_t n1, const uint8_t* s2, int64
                          int32_t H, uint32_t* out4, cudaStream_t);
 
 // moe_peer.cu
+int launch_peer_layout(const int32_t* counts, int32_t P, int32_t El, int32_t rank, int32_t* dst_base,
+                       int32_t* indptr_local, cudaStream_t s);
 int launch_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, const int32_t* expert_of_row,
                          const int32_t* indptr, int64_t rows, int32_t H, int32_t E, int32_t El, int32_t rank,
                          const int32_t* dst_base, void* const* peer_rows, int32_t* const* peer_origin,

@@ -60,6 +60,38 @@ __global__ void dispatch_peer_kernel(const uint16_t* __restrict__ t, const int32
   __threadfence_system();
 }
 
+// Row addressing of the peer path from the all-gathered counts
+// [num_ranks, num_ranks * El] (rows of source rank s for each global expert),
+// as peer_layout in ep.py: rank d's matrix is expert-major over its local
+// experts and source-major inside an expert.
+//   dst_base[d * El + e] = first row on rank d of this rank's rows of e;
+//   indptr_local[e] = first row of this rank's own local expert e.
+__global__ void peer_layout_kernel(const int32_t* __restrict__ counts, int32_t P, int32_t El, int32_t rank,
+                                   int32_t* __restrict__ dst_base, int32_t* __restrict__ indptr_local) {
+  const int32_t E = P * El;
+  for (int32_t i = threadIdx.x; i < P * El; i += blockDim.x) {
+    const int32_t d = i / El, e = i % El;
+    int32_t v = 0;
+    for (int32_t ep = 0; ep < e; ++ep)
+      for (int32_t s = 0; s < P; ++s) v += counts[s * E + d * El + ep];
+    for (int32_t s = 0; s < rank; ++s) v += counts[s * E + d * El + e];
+    dst_base[i] = v;
+  }
+  for (int32_t e = threadIdx.x; e <= El; e += blockDim.x) {
+    int32_t v = 0;
+    for (int32_t ep = 0; ep < e; ++ep)
+      for (int32_t s = 0; s < P; ++s) v += counts[s * E + rank * El + ep];
+    indptr_local[e] = v;
+  }
+}
+
+int launch_peer_layout(const int32_t* counts, int32_t P, int32_t El, int32_t rank, int32_t* dst_base,
+                       int32_t* indptr_local, cudaStream_t s) {
+  if (P < 1 || P > kMaxPeerRanks || El <= 0 || rank < 0 || rank >= P) return -12;
+  peer_layout_kernel<<<1, 256, 0, s>>>(counts, P, El, rank, dst_base, indptr_local);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
 int launch_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, const int32_t* expert_of_row,
                          const int32_t* indptr, int64_t rows, int32_t H, int32_t E, int32_t El, int32_t rank,
                          const int32_t* dst_base, void* const* peer_rows, int32_t* const* peer_origin,

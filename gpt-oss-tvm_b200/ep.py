@@ -178,20 +178,24 @@ class CudaBackend:
                   _ptr(self.exr), _ptr(self.tile_ptr_g), _ptr(self.tile_rows_g), _ptr(self.err), S)
         return (self.indptr[1:] - self.indptr[:-1]).contiguous()
 
-    def dispatch_peer(self, M: int, dst_base_host):
+    def layout_peer(self, counts_all, rank: int):
+        """Row addressing from the all-gathered counts, on the device (peer_layout)."""
+        _lib.call("gptoss_moe_peer_layout", _ptr(counts_all), self.world, self.El, rank, _ptr(self.peer["dst_base"]),
+                  _ptr(self.indptr_local), _stream())
+
+    def dispatch_peer(self, M: int):
         P, S = self.peer, _stream()
-        P["dst_base"].copy_(dst_base_host.reshape(-1), non_blocking=True)
         _lib.call("gptoss_moe_dispatch_peer", _ptr(self.t), _ptr(self.tok), _ptr(self.exr), _ptr(self.indptr),
                   M * self.k, self.H, self.E, self.El, P["rank"], _ptr(P["dst_base"]), P["rows"], P["origin"],
                   self.world, P["cap"], self.f16, S)
 
-    def experts_peer(self, recv_rows: int, indptr_local_host):
-        """mlp1 + mlp2 on this rank's rows; mlp2's rows go to their owners' return buffers."""
+    def experts_peer(self):
+        """mlp1 + mlp2 on this rank's rows; mlp2's rows go to their owners' return buffers.
+        The row count stays on the device: the GEMMs are launched on the buffer
+        capacity and take their tiles from the device-side plan."""
         blk, P, S = self.blk, self.peer, _stream()
         H, I, El = self.H, self.I, self.El
-        if recv_rows == 0:
-            return
-        self.indptr_local.copy_(indptr_local_host, non_blocking=True)
+        recv_rows = P["cap"]
         _lib.call("gptoss_moe_plan_tiles", _ptr(self.indptr_local), El, _ptr(self.tile_ptr), _ptr(self.tile_rows), S)
         y = P["y"]
         _lib.call("gptoss_moe_mlp1", P["act"], recv_rows, _ptr(self.indptr_local), _ptr(self.tile_ptr),
@@ -303,17 +307,28 @@ class ExpertParallelMoE:
         self.backend = backend or CudaBackend(blk, max_tokens, self.world, exact_return)
         if self.peer:
             self.backend.setup_peer(group, self.rank)
-        self.last_splits = None
+        self._splits = None
+        self._counts_all = None
 
     def _layout(self, counts):
-        """All-gather the per-expert row counts; the one host synchronisation of a step."""
+        """All-gather the per-expert row counts and lay out the rows (no host round trip)."""
         counts_all = torch.empty(self.world * counts.numel(), dtype=counts.dtype, device=counts.device)
         dist.all_gather_into_tensor(counts_all, counts, group=self.group)
-        ca = counts_all.cpu().view(self.world, counts.numel())
-        El = self.blk.num_local_experts
-        per = ca.reshape(self.world, self.world, El).sum(2)  # [source, destination]
-        self.last_splits = (per[self.rank].tolist(), per[:, self.rank].tolist())
-        return peer_layout(ca, self.rank, El)
+        self._counts_all = counts_all.view(self.world, counts.numel())
+        self.backend.layout_peer(self._counts_all, self.rank)
+
+    @property
+    def last_splits(self):
+        """(rows sent to each rank, rows received from each rank) of the last step."""
+        if self._splits is None and self._counts_all is not None:
+            El = self.blk.num_local_experts
+            per = self._counts_all.cpu().reshape(self.world, self.world, El).sum(2)  # [source, destination]
+            self._splits = (per[self.rank].tolist(), per[:, self.rank].tolist())
+        return self._splits
+
+    @last_splits.setter
+    def last_splits(self, v):
+        self._splits = v
 
     def _order(self):
         """Every rank's kernels issued so far have completed (their peer stores are visible)."""
@@ -321,11 +336,12 @@ class ExpertParallelMoE:
 
     def _forward_peer(self, x2, out2):
         b = self.backend
+        self._splits = None
         counts = b.route(x2)
-        dst_base, indptr_local, recv_rows = self._layout(counts)
-        b.dispatch_peer(x2.shape[0], dst_base)
+        self._layout(counts)
+        b.dispatch_peer(x2.shape[0])
         self._order()
-        b.experts_peer(recv_rows, indptr_local)
+        b.experts_peer()
         self._order()
         b.combine_peer(x2, out2)
 
@@ -371,15 +387,15 @@ class ExpertParallelMoE:
             ev[0].record()
             counts = b.route(x2)
             ev[1].record()
-            dst_base, indptr_local, recv_rows = self._layout(counts)
+            self._layout(counts)
             ev[2].record()
-            b.dispatch_peer(x2.shape[0], dst_base)
+            b.dispatch_peer(x2.shape[0])
             ev[3].record()
             self._order()
             ev[4].record()
             blk, P, S = self.blk, b.peer, _stream()
             H, I, El = b.H, b.I, b.El
-            b.indptr_local.copy_(indptr_local, non_blocking=True)
+            recv_rows = P["cap"]
             _lib.call("gptoss_moe_plan_tiles", _ptr(b.indptr_local), El, _ptr(b.tile_ptr), _ptr(b.tile_rows), S)
             _lib.call("gptoss_moe_mlp1", P["act"], recv_rows, _ptr(b.indptr_local), _ptr(b.tile_ptr),
                       _ptr(b.tile_rows), El, H, I, _ptr(blk.mlp1_weight_blocks), _ptr(blk.mlp1_weight_scales),
@@ -398,7 +414,7 @@ class ExpertParallelMoE:
             ev[8].record()
             torch.cuda.synchronize()
             tms = {f"{n}_ms": ev[i].elapsed_time(ev[i + 1]) for i, n in enumerate(names)}
-            tms["recv_rows"] = recv_rows
+            tms["recv_rows"] = int(b.indptr_local[-1].item())
             if best is None or tms["mlp1_ms"] < best["mlp1_ms"]:
                 best = tms
         R = best.pop("recv_rows")

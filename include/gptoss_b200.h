@@ -265,6 +265,16 @@ int gptoss_ipc_open(const void* handle, void** ptr);
 int gptoss_ipc_close(void* ptr);
 int gptoss_ipc_free(void* ptr);
 
+/* Row addressing of the expert-parallel dispatch, on the device (no host
+ * round trip): counts_all [num_ranks, num_ranks * local_experts] int32 holds
+ * every rank's rows per global expert (an all-gather of the per-expert counts).
+ * Rank d's activation matrix is expert-major over its local experts and
+ * source-rank-major inside an expert.  Writes dst_base [num_ranks *
+ * local_experts] (first row on rank d of this rank's rows of d's expert e) and
+ * indptr_local [local_experts + 1] (this rank's own expert offsets). */
+int gptoss_moe_peer_layout(const int32_t* counts_all, int32_t num_ranks, int32_t local_experts, int32_t rank,
+                           int32_t* dst_base, int32_t* indptr_local, void* stream);
+
 /* Expert-parallel dispatch: for every send row r of this rank (the
  * expert-major order of gptoss_moe_permute over the global experts), with
  * eg = expert_of_row[r], d = eg / local_experts, e = eg % local_experts:

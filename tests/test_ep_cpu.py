@@ -206,7 +206,12 @@ class TorchPeerBackend(TorchBackend):
     def route_fn(self, x):
         return TorchBackend.route(self, x)
 
-    def dispatch_peer(self, M, dst_base):
+    def layout_peer(self, counts_all, rank):
+        ep = _ep_module()
+        self.dst_base, self.indptr_local, self.recv_rows = ep.peer_layout(counts_all, rank, self.El)
+
+    def dispatch_peer(self, M):
+        dst_base = self.dst_base
         for r in range(self.send_tok.numel()):
             eg = int(self.send_exp[r])
             d, e = eg // self.El, eg % self.El
@@ -214,7 +219,8 @@ class TorchPeerBackend(TorchBackend):
             self.shared[d]["act"][dst] = self.x[self.send_tok[r]]
             self.shared[d]["origin"][dst] = (self.rank << 24) | r
 
-    def experts_peer(self, recv_rows, indptr_local):
+    def experts_peer(self):
+        indptr_local = self.indptr_local
         me = self.shared[self.rank]
         for e in range(self.El):
             for row in range(int(indptr_local[e]), int(indptr_local[e + 1])):
