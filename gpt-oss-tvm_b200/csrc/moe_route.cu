@@ -88,7 +88,8 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
 // thread owns a 4-token x 8-expert register tile of independent serial
 // chains; two chains share one packed f32x2 FMA.
 constexpr int kRTT = 2;   // tokens per thread
-constexpr int kRTE = 8;   // experts per thread
+constexpr int kRTE = 8;   // experts per thread (a multiple of 4)
+static_assert(kRTE % 4 == 0, "expert values load as 16-byte pairs");
 constexpr int kRKT = 32;  // k per shared-memory stage (multiple of 8)
 
 // bf16 rounding of two fp32 accumulators held as a packed pair: one cvt per
@@ -184,11 +185,26 @@ __global__ void __launch_bounds__(128) router_kernel(const uint16_t* __restrict_
     if (k0 + kRKT < H) load_stage(k0 + kRKT);  // next stage's loads overlap this stage's chains
     const int32_t kn = min(kRKT, H - k0);
     for (int32_t kk = 0; kk < kn; ++kk) {
-      const ulonglong2 t01 = *(const ulonglong2*)(ts + (kk * btok + tg * kRTT) * 2);
-      const unsigned long long tv[2] = {t01.x, t01.y};
+      // this thread's kRTT token values (each duplicated) and kRTE expert values
+      unsigned long long tv[kRTT], wv[kRTE / 2];
+      const unsigned long long* tp = (const unsigned long long*)(ts + (kk * btok + tg * kRTT) * 2);
+#pragma unroll
+      for (int i = 0; i < kRTT; i += 2) {
+        if (i + 1 < kRTT) {
+          const ulonglong2 v = *(const ulonglong2*)(tp + i);
+          tv[i] = v.x;
+          tv[i + 1] = v.y;
+        } else {
+          tv[i] = tp[i];
+        }
+      }
       const ulonglong2* wp = (const ulonglong2*)(ws + kk * block_experts + eg * kRTE);
-      const ulonglong2 w01 = wp[0], w23 = wp[1];
-      const unsigned long long wv[4] = {w01.x, w01.y, w23.x, w23.y};
+#pragma unroll
+      for (int q = 0; q < kRTE / 4; ++q) {
+        const ulonglong2 v = wp[q];
+        wv[2 * q] = v.x;
+        wv[2 * q + 1] = v.y;
+      }
 #pragma unroll
       for (int i = 0; i < kRTT; ++i) {
 #pragma unroll
@@ -666,6 +682,7 @@ static int launch_router_tiles(int egroups, dim3 grid, size_t smem, cudaStream_t
                                uint16_t* logits) {
   // prefetch registers per thread: token tile (btok rows x 4 pieces) and expert tile (be rows x 4 pieces)
   switch (egroups) {
+    case 16: launch_router_variant<1, 2>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
     case 8: launch_router_variant<1, 2>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
     case 4: launch_router_variant<2, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
     case 2: launch_router_variant<4, 1>(grid, smem, s, t, W, b, M, E, H, be, logits); break;
