@@ -303,6 +303,10 @@ def run_b200(args):
         if args.decode and world == 1:
             line["decode"] = {name: decode_bench(dev, E, M, 20, peaks) for name, (E, M) in DECODE_CASES.items()}
             line["attention"] = attention_bench(dev, peaks)
+        if args.full_model != "none" and world == 1:
+            names = [n for n in FULL_MODEL_CASES if args.full_model == "all" or n.startswith(args.full_model)]
+            line["full_model"] = {n: full_model_bench(dev, peaks, n, steps=args.steps, warmup=args.warmup)
+                                  for n in names}
         if args.cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args)
         print(json.dumps(line), flush=True)
@@ -494,6 +498,224 @@ def attention_bench(dev, peaks, iters=10):
     return out
 
 
+FULL_MODEL_CASES = {
+    # name: (config factory, decode context, decode batches, prompts prefilled for the decode context, prefill length)
+    "gpt-oss-20b (configs[2])": ("gpt_oss_20b", 2048, (1, 8, 64), 64, 4096),
+    "gpt-oss-120b (configs[4])": ("gpt_oss_120b", 4096, (256,), 16, 16384),
+}
+EXPERT_BYTES = (5760 * 90 * 16 + 5760 * 90 + 5760 * 2) + (2880 * 90 * 16 + 2880 * 90 + 2880 * 2)
+
+
+def _routed_experts(model, cache, ids, lib):
+    """Distinct experts each layer's router picks for one decode step of the
+    batch (an extra, untimed forward; the cache is rolled back after it)."""
+    import torch
+    cfg = model.config
+    E, H, K, B = cfg.num_experts, cfg.hidden_size, cfg.num_experts_per_tok, ids.numel()
+    P = lambda a: ctypes.c_void_p(a.data_ptr())  # noqa: E731
+    counts = []
+
+    class Counting:
+        def __init__(self, mlp):
+            self.mlp = mlp
+
+        def __call__(self, x, out=None):
+            S = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            x2 = x.reshape(-1, H).contiguous()
+            t = torch.empty_like(x2)
+            lib.call("gptoss_rms_norm", P(x2), P(self.mlp.norm_weight), B, H, ctypes.c_float(1e-5), P(t), S)
+            logits = torch.empty(B, E, dtype=torch.bfloat16, device=x.device)
+            w = torch.empty(B, K, dtype=torch.bfloat16, device=x.device)
+            idx = torch.empty(B, K, dtype=torch.int32, device=x.device)
+            err = torch.zeros(4, dtype=torch.int32, device=x.device)
+            lib.call("gptoss_moe_router", P(t), P(self.mlp.gate_weight), P(self.mlp.gate_bias), B, E, H, K, P(logits),
+                     P(w), P(idx), P(err), S)
+            counts.append(int(torch.unique(idx).numel()))
+            return self.mlp.forward(x, out)
+
+    blocks = model.model.block
+    saved = [b.mlp for b in blocks]
+    try:
+        for b in blocks:
+            b.mlp = Counting(b.mlp)
+        cache.begin_decode_on_device(B)
+        model.decode(model.embed(ids), cache)
+        torch.cuda.synchronize()
+    finally:
+        for b, m in zip(blocks, saved):
+            b.mlp = m
+        cache.rollback_device()
+    return counts
+
+
+def full_model_bench(dev, peaks, name, steps=20, warmup=3):
+    """Full-model forward (GPTOssForCausalLM, random-init weights from a
+    seed): greedy decode at the configuration's batch sizes over its context
+    (sequences 0..B-1, one CUDA graph per step: embedding, every layer, final
+    norm, unembedding, argmax), and one long prefill.
+
+    Decode: the context is prefilled for real (distinct prompts; with fewer
+    distinct prompts than sequences their KV rows are copied to the others,
+    each sequence then decoding its own token), every batch restarts at the
+    same context length, W warm-up replays, K timed replays (CUDA events).
+    Algorithmic bytes of a step = attention and router weights of every layer
+    + the experts the routers pick (counted by an untimed forward of the same
+    step) + the KV rows each layer reads (the window on sliding layers) +
+    embedding rows, unembedding weight and the logits.  The >= 13 GB of
+    weights read per step exceed the 126 MB L2 (no flush needed).
+    e2e: the same steps with each step's input tokens copied from pinned host
+    memory and its greedy tokens copied back (host sync every step)."""
+    import numpy as np
+    import torch
+    modm = importlib.import_module("gpt-oss-tvm_b200.model")
+    engm = importlib.import_module("gpt-oss-tvm_b200.engine")
+    cfgm = importlib.import_module("gpt-oss-tvm_b200.config")
+    lib = importlib.import_module("gpt-oss-tvm_b200._lib")
+    factory, ctx, batches, distinct, P_len = FULL_MODEL_CASES[name]
+    cfg = getattr(cfgm, factory)()
+    L, V, H = cfg.num_hidden_layers, cfg.vocab_size, cfg.hidden_size
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    tc_peak = float(peaks.get("bf16_tflops", 1590.0))
+    t0 = time.perf_counter()
+    model = modm.random_init(modm.GPTOssForCausalLM(cfg, device=dev), seed=0)
+    Bmax = max(batches)
+    model.reserve(max(P_len, Bmax, ctx))
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    res = {"weights_gb": round(sum(t.numel() * t.element_size() for _, t in model.named_parameters()) / 1e9, 2),
+           "init_s": round(time.perf_counter() - t0, 1)}
+
+    def ev():
+        return torch.cuda.Event(enable_timing=True)
+
+    # ---- prefill of one P_len-token prompt
+    pc = model.create_paged_kv_cache(1, P_len)
+    ids = torch.randint(0, V, (P_len,), generator=g, device=dev)
+
+    def prefill(ids_dev):
+        pc.clear()
+        pc.begin_forward([0], [P_len])
+        lg, _ = model.prefill(model.embed(ids_dev), pc)
+        return lg
+
+    for _ in range(2):
+        prefill(ids)
+    times = []
+    for _ in range(3):
+        a, b = ev(), ev()
+        a.record()
+        prefill(ids)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    ms = statistics.median(times)
+    ids_host = ids.cpu().pin_memory()
+    tok_host = torch.empty(1, dtype=torch.int64).pin_memory()
+    times = []
+    for _ in range(3):
+        a, b = ev(), ev()
+        a.record()
+        ids_d = ids_host.to(dev, non_blocking=True)
+        tok_host.copy_(torch.argmax(prefill(ids_d).reshape(-1)).reshape(1), non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    e2e_ms = statistics.median(times)
+    D, Hq, Hkv, W = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.sliding_window_size
+    dense = 2 * P_len * H * (D * (Hq + 2 * Hkv)) + 2 * P_len * (D * Hq) * H
+    attn = sum(4 * D * Hq * (P_len * P_len / 2 if i % 2 else P_len * min(W, P_len)) for i in range(L))
+    moe = 2 * P_len * cfg.num_experts_per_tok * (2 * cfg.intermediate_size * H + H * cfg.intermediate_size)
+    flops = L * (dense + moe) + attn + 2 * H * V
+    res[f"prefill {P_len} tokens"] = {
+        "ms": round(ms, 3), "tokens_per_s": round(P_len / ms * 1e3, 1), "tflops": round(flops / ms / 1e9, 1),
+        "frac_of_bf16_peak": round(flops / ms / 1e9 / tc_peak, 4),
+        "e2e_tokens_per_s": round(P_len / e2e_ms * 1e3, 1),
+        "e2e": "prompt ids copied from pinned host memory, greedy token copied back, inside the timed region",
+        "flops_per_prefill": flops}
+    del pc
+    torch.cuda.empty_cache()
+
+    # ---- decode over a ctx-token context
+    dc = model.create_paged_kv_cache(Bmax, ctx + steps + 8)
+    for s in range(min(distinct, Bmax)):
+        p = torch.randint(0, V, (ctx,), generator=g, device=dev)
+        dc.begin_forward([s], [ctx])
+        model.prefill(model.embed(p), dc)
+    for s in range(distinct, Bmax):
+        for layer in range(L):
+            dc.k[layer][s, :ctx].copy_(dc.k[layer][s % distinct, :ctx])
+            dc.v[layer][s, :ctx].copy_(dc.v[layer][s % distinct, :ctx])
+    torch.cuda.synchronize()
+
+    def restart():
+        dc.lengths.fill_(ctx)
+        dc.rollback_device()
+
+    attn_w = L * 2 * ((D * (Hq + 2 * Hkv)) * (H + 1) + H * (D * Hq + 1) + Hq + H)
+    router_w = L * 2 * (cfg.num_experts * (H + 1) + H)
+    kv_span = [min(ctx + steps // 2, W) if i % 2 == 0 else ctx + steps // 2 for i in range(L)]
+    for B in batches:
+        restart()
+        tokens = torch.randint(0, V, (B,), generator=g, device=dev)
+        routed = _routed_experts(model, dc, tokens, lib)
+        dec = engm.GreedyDecodeGraph(model, dc, B)
+        dec.set_tokens(tokens)
+        for _ in range(warmup):
+            dec.step()
+        restart()
+        dec.set_tokens(tokens)
+        torch.cuda.synchronize()
+        a, b = ev(), ev()
+        a.record()
+        for _ in range(steps):
+            dec.step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / steps
+        # e2e through pinned host buffers, host sync every step
+        restart()
+        th = tokens.cpu().pin_memory()
+        nh = torch.empty_like(th).pin_memory()
+        torch.cuda.synchronize()
+        a, b = ev(), ev()
+        a.record()
+        for _ in range(steps):
+            dec.set_tokens(th.to(dev, non_blocking=True))
+            _, nxt = dec.step()
+            nh.copy_(nxt, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            th.copy_(nh)
+        b.record()
+        torch.cuda.synchronize()
+        e2e_ms = a.elapsed_time(b) / steps
+        dec.close()
+        kv = B * sum(kv_span) * Hkv * D * 2 * 2
+        nbytes = attn_w + router_w + sum(routed) * EXPERT_BYTES + kv + H * V * 2 + B * H * 2 + B * V * (4 + 2 * 2)
+        gbs = nbytes / ms / 1e6
+        res[f"decode batch {B} over {ctx} context"] = {
+            "ms_per_step": round(ms, 4), "tokens_per_s": round(B / ms * 1e3, 1),
+            "e2e_tokens_per_s": round(B / e2e_ms * 1e3, 1), "bytes_per_step": nbytes,
+            "achieved_gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 4),
+            "experts_read_per_layer": round(sum(routed) / L, 2)}
+    del dc
+    model.release()
+    del model
+    torch.cuda.empty_cache()
+    res["note"] = ("random-init weights (seed 0), prompt and decode token ids uniform over the vocabulary; "
+                   "decode = CUDA-graph replays of GreedyDecodeGraph; hbm_frac of the measured copy bandwidth")
+    return res
+
+
+def full_model_only(args):
+    import torch
+    peaks, _ = measured_peaks()
+    names = list(FULL_MODEL_CASES) if args.full_model == "all" else [n for n in FULL_MODEL_CASES
+                                                                      if n.startswith(args.full_model)]
+    dev = torch.device("cuda", 0)
+    out = {n: full_model_bench(dev, peaks, n, steps=args.steps, warmup=args.warmup) for n in names}
+    print(json.dumps({"full_model": out}), flush=True)
+
+
 def cpu_baseline(args):
     """Reference CPU implementation on the host cores, on a bounded sample."""
     cb = importlib.import_module("oracle.cpu_baseline")
@@ -570,12 +792,18 @@ def main():
                     help="expert-parallel row exchange (N > 1): stores into the ranks' IPC-shared buffers or NCCL")
     ap.add_argument("--decode-only", type=int, default=None, choices=range(len(DECODE_CASES)),
                     help="run only this decode case (index into DECODE_CASES) and print its measurement")
+    ap.add_argument("--full-model", default="gpt-oss-20b", choices=["none", "gpt-oss-20b", "gpt-oss-120b", "all"],
+                    help="full-model decode/prefill measurements added to the line (1 GPU)")
+    ap.add_argument("--full-model-only", action="store_true",
+                    help="run only the --full-model measurements and print them")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     TOKENS = args.tokens
     if args.decode_only is not None:
         decode_only(args)
+    elif args.full_model_only and args.impl != "reference":
+        full_model_only(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -37,10 +37,18 @@ def _stream():
 
 
 class KVCache:
-    """Per-layer contiguous KV cache for up to `max_batch` sequences."""
+    """Per-layer contiguous KV cache for up to `max_batch` sequences.
+
+    The host keeps the authoritative sequence lengths (``lengths``); the
+    device keeps a mirror (``dev_lengths``) so that a decode step can plan
+    itself on the device (``begin_decode_on_device``) inside a CUDA graph.
+    The decode-step buffers (positions, slots, kv_len) are allocated once and
+    never move, so a captured graph keeps reading the current values."""
 
     def __init__(self, config: GPTOssConfig, max_batch: int, max_len: int, num_layers: int | None = None,
                  device="cuda"):
+        if max_batch < 1 or max_len < 1 or max_batch * max_len >= 2 ** 31:
+            raise ValueError(f"KVCache: max_batch x max_len = {max_batch} x {max_len} must fit int32 slots")
         self.config = config
         self.max_batch, self.max_len = max_batch, max_len
         L = num_layers if num_layers is not None else config.num_hidden_layers
@@ -49,31 +57,103 @@ class KVCache:
         self.v = [torch.zeros(max_batch, max_len, Hkv, D, dtype=torch.bfloat16, device=device) for _ in range(L)]
         self.lengths = torch.zeros(max_batch, dtype=torch.int32)  # host copy
         self.device = torch.device(device)
+        dev = self.device
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.dev_lengths = torch.zeros(max_batch, **i32)
+        self._seq_base = torch.arange(max_batch, **i32) * max_len
+        self._dec_pos = torch.zeros(max_batch, **i32)
+        self._dec_slot = torch.zeros(max_batch, **i32)
+        self._kv_len = torch.zeros(max_batch, **i32)
+        self._pos = torch.zeros(max_batch, **i32)
+        self._slot = torch.zeros(max_batch, **i32)
         self._cur = None
+
+    def _sync_dev_lengths(self):
+        self.dev_lengths.copy_(self.lengths.to(self.device))
 
     def begin_forward(self, seq_ids, append_lengths):
         """Plan one forward pass (kv_state_begin_forward, engine.py:135-139):
         returns the query positions of the appended tokens."""
         pos, slots = [], []
+        new_len = self.lengths.clone()
         for s, n in zip(seq_ids, append_lengths):
-            start = int(self.lengths[s])
+            if not 0 <= s < self.max_batch:
+                raise ValueError(f"sequence id {s} outside the cache's {self.max_batch} sequences")
+            start = int(new_len[s])
             if start + n > self.max_len:
                 raise ValueError("KV cache full")
-            pos.extend(range(start, start + n))
-            slots.extend(s * self.max_len + start + i for i in range(n))
-            self.lengths[s] = start + n
+            p = torch.arange(start, start + n, dtype=torch.int32)
+            pos.append(p)
+            slots.append(p + s * self.max_len)
+            new_len[s] = start + n
+        self.lengths.copy_(new_len)
         self._cur = (list(seq_ids), list(append_lengths))
-        dev = self.device
-        self.positions = torch.tensor(pos, dtype=torch.int32, device=dev)
-        self.slots = torch.tensor(slots, dtype=torch.int32, device=dev)
-        self.kv_len = torch.tensor([int(self.lengths[s]) for s in seq_ids], dtype=torch.int32, device=dev)
+        pos = torch.cat(pos) if pos else torch.zeros(0, dtype=torch.int32)
+        slots = torch.cat(slots) if slots else torch.zeros(0, dtype=torch.int32)
+        T = pos.numel()
+        if T > self._pos.numel():
+            self._pos = torch.zeros(T, dtype=torch.int32, device=self.device)
+            self._slot = torch.zeros(T, dtype=torch.int32, device=self.device)
+        self._pos[:T].copy_(pos)
+        self._slot[:T].copy_(slots)
+        nb = len(seq_ids)
+        self._kv_len[:nb].copy_(torch.tensor([int(self.lengths[s]) for s in seq_ids], dtype=torch.int32))
+        self._sync_dev_lengths()
+        self.positions, self.slots, self.kv_len = self._pos[:T], self._slot[:T], self._kv_len[:nb]
         return self.positions
+
+    def check_decode(self, batch: int, steps: int = 1):
+        if not 1 <= batch <= self.max_batch:
+            raise ValueError(f"decode batch {batch} outside 1..{self.max_batch}")
+        if int(self.lengths[:batch].max()) + steps > self.max_len:
+            raise ValueError("KV cache full")
+
+    def begin_decode_on_device(self, batch: int):
+        """begin_forward(range(batch), [1] * batch) done by device ops only
+        (capturable in a CUDA graph): position = current length, slot =
+        sequence base + position, length += 1.  The host mirror is advanced
+        by ``commit_decode`` after the step has been issued."""
+        self._cur = (list(range(batch)), [1] * batch)
+        pos, slot, kvl = self._dec_pos[:batch], self._dec_slot[:batch], self._kv_len[:batch]
+        pos.copy_(self.dev_lengths[:batch])
+        torch.add(self._seq_base[:batch], pos, out=slot)
+        self.dev_lengths[:batch].add_(1)
+        kvl.copy_(self.dev_lengths[:batch])
+        self.positions, self.slots, self.kv_len = pos, slot, kvl
+        return pos
+
+    def commit_decode(self, batch: int, steps: int = 1):
+        self.lengths[:batch] += steps
+
+    def rollback_device(self):
+        """Forget device-side steps that were not committed (graph warm-up)."""
+        self._sync_dev_lengths()
 
     def popn(self, seq_id: int, n: int):
         self.lengths[seq_id] = max(0, int(self.lengths[seq_id]) - n)
+        self._sync_dev_lengths()
 
     def clear(self):
         self.lengths.zero_()
+        self._sync_dev_lengths()
+
+    def total_length(self) -> int:
+        return int(self.lengths.sum())
+
+
+class DecodeScratch:
+    """Split-KV partial results of the decode kernel; one buffer can serve
+    every layer of a model (the layers run one after another on one stream).
+    It only grows, and it is sized before a decode step is captured."""
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        self.buf = None
+
+    def get(self, nbytes: int) -> torch.Tensor:
+        if self.buf is None or self.buf.numel() * 4 < nbytes:
+            self.buf = torch.empty(max(nbytes // 4, 1), dtype=torch.float32, device=self.device)
+        return self.buf
 
 
 class AttentionBlock:
@@ -107,7 +187,7 @@ class AttentionBlock:
                   ctypes.byref(conc))
         self._inv_freq = inv
         self._conc = conc.value
-        self._scratch = None
+        self.scratch = DecodeScratch(dev)
 
     PARAM_NAMES = {"sinks": "sinks", "norm.weight": "norm_weight", "qkv.weight": "qkv_weight",
                    "qkv.bias": "qkv_bias", "out.weight": "out_weight", "out.bias": "out_bias"}
@@ -127,9 +207,7 @@ class AttentionBlock:
     def _scratch_for(self, B, max_len):
         nbytes = int(_lib.load().gptoss_attn_decode_scratch_bytes(B, self.num_attention_heads, max_len,
                                                                    self.sliding_window))
-        if self._scratch is None or self._scratch.numel() * 4 < nbytes:
-            self._scratch = torch.empty(max(nbytes // 4, 1), dtype=torch.float32, device=self.device)
-        return self._scratch, nbytes
+        return self.scratch.get(nbytes), nbytes
 
     def forward(self, x: torch.Tensor, kv_cache: KVCache, query_positions: torch.Tensor | None, forward_to: str):
         """x [b, s, hidden] bf16.  prefill / extend: one sequence (b = 1, the

@@ -61,6 +61,7 @@ class MLPBlock:
         self.mlp2_bias = torch.zeros(El, H, dtype=torch.bfloat16, device=dev)
         self._ws = None
         self._ws_tokens = 0
+        self._ws_owner = self
         self.flags = 0            # GPTOSS_MOE_* bits (set by prepare())
         self.allow_f16 = True     # let prepare() enable the f16 GEMM path when it is exact
 
@@ -131,7 +132,17 @@ class MLPBlock:
         w.flags = self.flags
         return w
 
+    def share_workspace(self, owner: "MLPBlock") -> None:
+        """Run on ``owner``'s scratch workspace.  The workspace holds no state
+        between forwards, so the layers of a model (run one after another on
+        one stream) can share one."""
+        if owner is not self:
+            self.free_workspace()
+        self._ws_owner = owner
+
     def workspace(self, tokens: int):
+        if self._ws_owner is not self:
+            return self._ws_owner.workspace(tokens)
         if self._ws is None or tokens > self._ws_tokens:
             self.free_workspace()
             n = max(tokens, 1)
@@ -155,7 +166,8 @@ class MLPBlock:
             pass
 
     def device_error(self) -> int:
-        return int(_lib.load().gptoss_moe_workspace_error(self._ws)) if self._ws is not None else 0
+        o = self._ws_owner
+        return int(_lib.load().gptoss_moe_workspace_error(o._ws)) if o._ws is not None else 0
 
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """x: [b, s, hidden] (or [tokens, hidden]) bf16 CUDA -> x + MoE(norm(x))."""

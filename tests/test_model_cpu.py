@@ -1,0 +1,162 @@
+"""Host-side logic of the full model, no GPU: parameter names and their
+checkpoint keys, the safetensors loader (round trip and its errors), the KV
+cache's planning (host and device-side forms), the Engine's target check and
+top-p sampling."""
+import importlib
+import types
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+
+def mods():
+    return (importlib.import_module("gpt-oss-tvm_b200.model"), importlib.import_module("gpt-oss-tvm_b200.config"),
+            importlib.import_module("gpt-oss-tvm_b200.weights"), importlib.import_module("gpt-oss-tvm_b200.engine"),
+            importlib.import_module("gpt-oss-tvm_b200.attention"))
+
+
+def small_config(cfgm, layers=2):
+    return cfgm.GPTOssConfig(num_hidden_layers=layers, num_experts=4, vocab_size=64, context_window_size=1024)
+
+
+# The tensor names of the gpt-oss safetensors checkpoint for one layer
+# (the names the reference's loader looks up, weights.py:103-122).
+LAYER_KEYS = ["attn.sinks", "attn.norm.scale", "attn.qkv.weight", "attn.qkv.bias", "attn.out.weight",
+              "attn.out.bias", "mlp.norm.scale", "mlp.gate.weight", "mlp.gate.bias", "mlp.mlp1_weight.blocks",
+              "mlp.mlp1_weight.scales", "mlp.mlp1_bias", "mlp.mlp2_weight.blocks", "mlp.mlp2_weight.scales",
+              "mlp.mlp2_bias"]
+
+
+def test_checkpoint_keys_of_every_parameter():
+    modm, cfgm, _, _, _ = mods()
+    cfg = small_config(cfgm)
+    model = modm.GPTOssForCausalLM(cfg, device="cpu")
+    names = [n for n, _ in model.named_parameters()]
+    assert len(names) == len(set(names))
+    keys = [modm.checkpoint_key(n) for n in names]
+    want = ["embedding.weight"] + [f"block.{i}.{k}" for i in range(2) for k in LAYER_KEYS] + ["norm.scale",
+                                                                                               "unembedding.weight"]
+    assert keys == want
+    assert modm.checkpoint_key("model.block.3.mlp.mlp2_weight_scales") == "block.3.mlp.mlp2_weight.scales"
+    shapes = dict(model.named_parameters())
+    H, E, I = 2880, 4, 2880
+    assert tuple(shapes["model.block.0.attn.qkv.weight"].shape) == (64 * 64 + 2 * 8 * 64, H)
+    assert tuple(shapes["model.block.1.mlp.mlp1_weight_blocks"].shape) == (E, 2 * I, 90, 16)
+    assert tuple(shapes["unembedding.weight"].shape) == (64, H)
+
+
+def test_checkpoint_round_trip_and_errors(tmp_path):
+    modm, cfgm, wm, _, _ = mods()
+    cfg = small_config(cfgm, layers=1)
+    a = modm.random_init(modm.GPTOssForCausalLM(cfg, device="cpu"), seed=3, prepare=False)
+    st = wm.save_checkpoint(a, tmp_path)
+    assert st.name == "model.safetensors"
+    b = modm.GPTOssForCausalLM(cfg, device="cpu")
+    wm.load_checkpoint(b, tmp_path, prepare=False)
+    for (n, ta), (_, tb) in zip(a.named_parameters(), b.named_parameters()):
+        assert ta.dtype == tb.dtype and torch.equal(ta, tb), n
+    # the path may also name the file itself
+    c = modm.GPTOssForCausalLM(cfg, device="cpu")
+    wm.load_checkpoint(c, st, prepare=False)
+    assert torch.equal(c.unembedding.weight, a.unembedding.weight)
+    with pytest.raises(FileNotFoundError):
+        wm.load_checkpoint(c, tmp_path / "missing", prepare=False)
+    from safetensors.torch import save_file
+    tensors = {modm.checkpoint_key(n): t.contiguous() for n, t in a.named_parameters()}
+    broken = dict(tensors)
+    del broken["block.0.attn.sinks"]
+    save_file(broken, str(tmp_path / "b.safetensors"))
+    with pytest.raises(KeyError):
+        wm.load_checkpoint(c, tmp_path / "b.safetensors", prepare=False)
+    bad = dict(tensors)
+    bad["norm.scale"] = torch.ones(7, dtype=torch.bfloat16)
+    save_file(bad, str(tmp_path / "c.safetensors"))
+    with pytest.raises(ValueError):
+        wm.load_checkpoint(c, tmp_path / "c.safetensors", prepare=False)
+
+
+def test_random_init_distributions():
+    modm, cfgm, _, _, _ = mods()
+    cfg = small_config(cfgm, layers=1)
+    m = modm.random_init(modm.GPTOssForCausalLM(cfg, device="cpu"), seed=0, prepare=False)
+    blk = m.model.block[0]
+    sc = blk.mlp.mlp1_weight_scales
+    assert int(sc.min()) == 118 and int(sc.max()) == 124
+    nb = blk.mlp.mlp2_weight_blocks
+    assert int(nb.min()) == 0 and int(nb.max()) == 255
+    assert abs(float(m.unembedding.weight.float().std()) - 0.02) < 1e-3
+    assert abs(float(blk.attn.sinks.float().std()) - 1.0) < 0.5
+    assert torch.all(blk.attn.norm_weight == 1) and torch.all(m.model.norm.weight == 1)
+    m2 = modm.random_init(modm.GPTOssForCausalLM(cfg, device="cpu"), seed=0, prepare=False)
+    assert torch.equal(m2.model.embedding.weight, m.model.embedding.weight)
+
+
+def test_kv_cache_planning_host_and_device_forms():
+    _, cfgm, _, _, att = mods()
+    cfg = small_config(cfgm)
+    c = att.KVCache(cfg, max_batch=3, max_len=16, num_layers=2, device="cpu")
+    pos = c.begin_forward([1], [5])
+    assert pos.tolist() == [0, 1, 2, 3, 4]
+    assert c.slots.tolist() == [16, 17, 18, 19, 20]
+    c.begin_forward([0, 2], [2, 1])
+    assert c.positions.tolist() == [0, 1, 0] and c.slots.tolist() == [0, 1, 32]
+    assert c.lengths.tolist() == [2, 5, 1] and c.dev_lengths.tolist() == [2, 5, 1]
+    # device-side decode step of sequences 0..2
+    c.check_decode(3)
+    p = c.begin_decode_on_device(3)
+    assert p.tolist() == [2, 5, 1] and c.slots.tolist() == [2, 21, 33] and c.kv_len.tolist() == [3, 6, 2]
+    assert c.lengths.tolist() == [2, 5, 1]  # host mirror moves on commit only
+    c.commit_decode(3)
+    assert c.lengths.tolist() == [3, 6, 2] and c.dev_lengths.tolist() == [3, 6, 2]
+    # an uncommitted device step is forgotten by rollback
+    c.begin_decode_on_device(2)
+    c.rollback_device()
+    assert c.dev_lengths.tolist() == [3, 6, 2]
+    c.popn(1, 4)
+    assert c.lengths.tolist() == [3, 2, 2] and c.dev_lengths.tolist() == [3, 2, 2]
+    assert c.total_length() == 7
+    with pytest.raises(ValueError):
+        c.begin_forward([0], [14])
+    with pytest.raises(ValueError):
+        c.check_decode(4)
+    c.begin_forward([0], [13])
+    with pytest.raises(ValueError):
+        c.check_decode(1)
+    with pytest.raises(ValueError):
+        c.begin_forward([3], [1])
+    c.clear()
+    assert c.total_length() == 0 and c.dev_lengths.tolist() == [0, 0, 0]
+    with pytest.raises(ValueError):
+        att.KVCache(cfg, max_batch=2 ** 16, max_len=2 ** 16, num_layers=0, device="cpu")
+
+
+def test_engine_rejects_other_targets():
+    _, cfgm, _, engm, _ = mods()
+    for target in ("cpu", "llvm", "vulkan", "metal"):
+        with pytest.raises(ValueError):
+            engm.Engine(None, target, config=small_config(cfgm), seed=0)
+
+
+def _top_p_numpy(z, temperature, top_p, u):
+    p = np.exp((z - z.max()) / temperature)
+    p /= p.sum()
+    order = np.argsort(-p, kind="stable")
+    cum = np.cumsum(p[order])
+    keep = int(np.searchsorted(cum, top_p)) + 1
+    cum_k = cum[:keep] / cum[keep - 1]
+    j = int(np.searchsorted(cum_k, u, side="right"))
+    return int(order[min(j, keep - 1)])
+
+
+@pytest.mark.parametrize("seed", range(5))
+def test_top_p_sampling(seed):
+    _, _, _, engm, _ = mods()
+    rng = np.random.default_rng(seed)
+    z = (rng.standard_normal(500) * 3).astype(np.float32)
+    fake = types.SimpleNamespace(sample_parameters={"temperature": 0.7, "top_p": 0.9, "random_seed": 0.5})
+    got = engm.Engine.sample(fake, torch.from_numpy(z).reshape(1, 1, -1))
+    assert got == _top_p_numpy(z.astype(np.float64), 0.7, 0.9, 0.5)
+    fake.sample_parameters["temperature"] = 0.0
+    assert engm.Engine.sample(fake, torch.from_numpy(z)) == int(np.argmax(z))
