@@ -401,4 +401,39 @@ __device__ __forceinline__ uint32_t e8m0_scale_bf16x2(uint32_t s) {
   return h | (h << 16);
 }
 
+// e2m1 -> f16 decode of 8 nibbles with the hardware converter, scaled by the
+// E8M0 power of two as packed f16 (exact for scale codes 104..140: every
+// product is an f16 normal or subnormal number).
+__device__ __forceinline__ void fp4x8_to_f16x8(uint32_t w, uint32_t scale2, uint32_t& o0, uint32_t& o1, uint32_t& o2,
+                                               uint32_t& o3) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(o0), "=r"(o1), "=r"(o2), "=r"(o3)
+      : "r"(w));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o0) : "r"(scale2));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o1) : "r"(scale2));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o2) : "r"(scale2));
+  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o3) : "r"(scale2));
+}
+
+// 2^(s-127) as an f16 pair (normal for s >= 113, subnormal for 103..112).
+__device__ __forceinline__ uint32_t e8m0_scale_f16x2(uint32_t s) {
+  const uint32_t h = s >= 113u ? ((s - 112u) << 10) : (1u << (s - 103u));
+  return h | (h << 16);
+}
+
+// Clamped SwiGLU of one (glu, linear) pair (model/mlp.py:29-60):
+// min(glu, limit) * sigmoid(alpha * min(glu, limit)) * (clamp(linear, -limit, limit) + 1).
+__device__ __forceinline__ float swiglu_f32(float glu, float lin, float alpha, float limit) {
+  const float g = fminf(glu, limit);
+  const float l = fmaxf(fminf(lin, limit), -limit);
+  // g * sigmoid(alpha * g); a huge denominator gives 0, the limit
+  const float gs = __fdividef(g, 1.0f + __expf(-(alpha * g)));
+  return gs * (l + 1.0f);
+}
+
 }  // namespace gptoss

@@ -34,6 +34,9 @@ struct GemmLaunch {
   int out_bf16 = 0;
 };
 int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream);
+// moe_gemv.cu: the decode-size form of the same GEMMs (f16 path, local outputs)
+bool moe_gemv_supported(const GemmLaunch& L);
+int launch_moe_gemv(int mode, const GemmLaunch& L, cudaStream_t stream);
 
 // moe_route.cu
 int launch_rmsnorm(const uint16_t*, const uint16_t*, int64_t, int32_t, float, uint16_t*, uint32_t*, cudaStream_t);

@@ -186,31 +186,6 @@ __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[
       : "memory");
 }
 
-// e2m1 -> f16 decode of 8 nibbles with the hardware converter, scaled by the
-// E8M0 power of two as packed f16 (exact for scale codes 104..140: every
-// product is an f16 normal or subnormal number).
-__device__ __forceinline__ void fp4x8_to_f16x8(uint32_t w, uint32_t scale2, uint32_t& o0, uint32_t& o1, uint32_t& o2,
-                                               uint32_t& o3) {
-  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
-      : "=r"(o0), "=r"(o1), "=r"(o2), "=r"(o3)
-      : "r"(w));
-  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o0) : "r"(scale2));
-  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o1) : "r"(scale2));
-  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o2) : "r"(scale2));
-  asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(o3) : "r"(scale2));
-}
-
-// 2^(s-127) as an f16 pair (normal for s >= 113, subnormal for 103..112).
-__device__ __forceinline__ uint32_t e8m0_scale_f16x2(uint32_t s) {
-  const uint32_t h = s >= 113u ? ((s - 112u) << 10) : (1u << (s - 103u));
-  return h | (h << 16);
-}
-
 // 16 words (32 elements, one MXFP4 group) of decoded weights.
 template <bool kF16>
 __device__ __forceinline__ void decode_group(const uint4 nb, uint32_t sc, bool row_ok, uint32_t (&r)[16]) {
@@ -261,11 +236,7 @@ __device__ __forceinline__ void epilogue_block(const GemmParams& p, const TileIn
       const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
       const float gl = odd ? recv : mine_lo;
       const float li = odd ? mine_hi : recv;
-      const float g = fminf(gl, p.limit);
-      const float l = fmaxf(fminf(li, p.limit), -p.limit);
-      // g * sigmoid(alpha * g); a huge denominator gives 0, the limit
-      const float gs = __fdividef(g, 1.0f + __expf(-(p.alpha * g)));
-      const float y = gs * (l + 1.0f);
+      const float y = swiglu_f32(gl, li, p.alpha, p.limit);
       const int tok = i + (odd ? 16 : 0);
       tile[tok * 16 + (lane >> 1)] = kF16 ? __half_as_ushort(__float2half_rn(y)) : f32_to_bf16_bits(y);
     }
@@ -821,7 +792,17 @@ static bool pair_enabled() {
   return !(e && e[0] == '0');
 }
 
+// GPTOSS_MOE_GEMV=0 keeps decode-size GEMMs on the tensor-core kernel.
+static bool gemv_enabled() {
+  const char* e = getenv("GPTOSS_MOE_GEMV");
+  return !(e && e[0] == '0');
+}
+
 int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
+  // decode sizes (the same rule as the token-tile plan's small tiles): the
+  // weights are streamed once through the MXFP4 GEMV kernel
+  if (moe_tile_rows_max(L.act_rows, L.E) <= kMoeTileRowsSmall && gemv_enabled() && moe_gemv_supported(L))
+    return launch_moe_gemv(mode, L, stream);
   if (L.K % kBK != 0 || L.K / 32 > kMaxGroups || L.K / 2 < kWRowBytes) return -10;
   {
     // every tile's scale block must be a whole number of 16-byte units

@@ -233,6 +233,45 @@ def test_forced_routing_small_tiles(oracle, f16):
     G.tol_check(G.f32(r["out"][rows]), G.f32(out), what="small-tile output")
 
 
+@pytest.mark.parametrize("case", ["e32-m1", "e32-m8", "e32-m16", "e128-m2", "forced-9-7"])
+def test_decode_gemv_matches_tensor_core_kernel(oracle, case, monkeypatch):
+    """Small decode batches (<= 64 routed rows) on the f16 path run the MXFP4
+    GEMV kernel (registers -> mma.sync, split-K over four warps);
+    GPTOSS_MOE_GEMV=0 runs the tensor-core small-tile kernel on the same
+    rows.  Both multiply the same exactly decoded f16 weights and f16
+    activations with fp32 accumulation, in different orders: the outputs agree
+    to fp32 rounding (h2 within 5e-3 of max|h2|; y within 2^-10 relative plus
+    1e-4 of max|y|) and are within the bf16 tolerance of the oracle.
+    "forced-9-7": experts with 9 rows (a second 8-row pass) and 7 rows."""
+    S = synth()
+    E, M = {"e32-m1": (32, 1), "e32-m8": (32, 8), "e32-m16": (32, 16), "e128-m2": (128, 2),
+            "forced-9-7": (32, 16)}[case]
+    p = S.moe_params(E, seed=4)
+    x = S.activations(M, seed=5)
+    routing = None
+    if case == "forced-9-7":
+        idx = np.zeros((M, 4), np.int32)
+        idx[:9] = [0, 1, 2, 3]
+        idx[9:] = [4, 5, 6, 7]
+        wts = S.bf16_bits(np.tile(np.array([[0.4, 0.3, 0.2, 0.1]], np.float32), (M, 1)))
+        routing = (wts, idx)
+    monkeypatch.setenv("GPTOSS_MOE_GEMV", "1")
+    pieces = G.MoEPieces(p, f16=True)
+    assert pieces.f16
+    a = pieces.run(x, routing=routing)
+    monkeypatch.setenv("GPTOSS_MOE_GEMV", "0")
+    b = pieces.run(x, routing=routing)
+    assert np.max(np.abs(a["h2"] - b["h2"])) <= 5e-3 * np.max(np.abs(b["h2"])), "h2: GEMV vs tensor-core kernel"
+    ya, yb = a["y"].astype(np.float64), b["y"].astype(np.float64)
+    assert np.all(np.abs(ya - yb) <= 2.0 ** -10 * np.abs(yb) + 1e-4 * np.abs(yb).max()), "y: GEMV vs tensor core"
+    G.tol_check(G.f32(a["out"]), G.f32(b["out"]), what="block output GEMV vs tensor core")
+    if routing is None:
+        ref = oracle.moe_forward(x, p, return_all=True)
+        G.tol_check(a["h2"][a["row_of_pair"].reshape(M, 4)].reshape(-1, 2880),
+                    ref["h2"].reshape(-1, 2880), what="GEMV mlp2 vs oracle")
+        G.tol_check(G.f32(a["out"]) - G.f32(x), G.f32(ref["gated"]), what="GEMV gated sum vs oracle")
+
+
 def test_f16_path_disabled_for_out_of_range_scales():
     """A scale code outside 104..140 makes gptoss_moe_weights_prepare clear the
     f16 flag; the exact bf16 path then matches the oracle."""
