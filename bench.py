@@ -548,7 +548,7 @@ def _routed_experts(model, cache, ids, lib):
     return counts
 
 
-def full_model_bench(dev, peaks, name, steps=20, warmup=3):
+def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill=True):
     """Full-model forward (GPTOssForCausalLM, random-init weights from a
     seed): greedy decode at the configuration's batch sizes over its context
     (sequences 0..B-1, one CUDA graph per step: embedding, every layer, final
@@ -571,7 +571,8 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3):
     engm = importlib.import_module("gpt-oss-tvm_b200.engine")
     cfgm = importlib.import_module("gpt-oss-tvm_b200.config")
     lib = importlib.import_module("gpt-oss-tvm_b200._lib")
-    factory, ctx, batches, distinct, P_len = FULL_MODEL_CASES[name]
+    factory, ctx, case_batches, distinct, P_len = FULL_MODEL_CASES[name]
+    batches = tuple(batches) if batches else case_batches
     cfg = getattr(cfgm, factory)()
     L, V, H = cfg.num_hidden_layers, cfg.vocab_size, cfg.hidden_size
     hbm = float(peaks.get("hbm_gbs", 6650.0))
@@ -589,7 +590,9 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3):
         return torch.cuda.Event(enable_timing=True)
 
     # ---- prefill of one P_len-token prompt
-    pc = model.create_paged_kv_cache(1, P_len)
+    if not prefill:
+        P_len = 0
+    pc = model.create_paged_kv_cache(1, max(P_len, 1))
     ids = torch.randint(0, V, (P_len,), generator=g, device=dev)
 
     def prefill(ids_dev):
@@ -598,21 +601,21 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3):
         lg, _ = model.prefill(model.embed(ids_dev), pc)
         return lg
 
-    for _ in range(2):
+    for _ in range(2 if P_len else 0):
         prefill(ids)
     times = []
-    for _ in range(3):
+    for _ in range(3 if P_len else 0):
         a, b = ev(), ev()
         a.record()
         prefill(ids)
         b.record()
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b))
-    ms = statistics.median(times)
+    ms = statistics.median(times) if times else 0.0
     ids_host = ids.cpu().pin_memory()
     tok_host = torch.empty(1, dtype=torch.int64).pin_memory()
     times = []
-    for _ in range(3):
+    for _ in range(3 if P_len else 0):
         a, b = ev(), ev()
         a.record()
         ids_d = ids_host.to(dev, non_blocking=True)
@@ -620,13 +623,13 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3):
         b.record()
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b))
-    e2e_ms = statistics.median(times)
+    e2e_ms = statistics.median(times) if times else 0.0
     D, Hq, Hkv, W = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.sliding_window_size
     dense = 2 * P_len * H * (D * (Hq + 2 * Hkv)) + 2 * P_len * (D * Hq) * H
     attn = sum(4 * D * Hq * (P_len * P_len / 2 if i % 2 else P_len * min(W, P_len)) for i in range(L))
     moe = 2 * P_len * cfg.num_experts_per_tok * (2 * cfg.intermediate_size * H + H * cfg.intermediate_size)
     flops = L * (dense + moe) + attn + 2 * H * V
-    res[f"prefill {P_len} tokens"] = {
+    res[f"prefill {P_len} tokens"] = {} if not P_len else {
         "ms": round(ms, 3), "tokens_per_s": round(P_len / ms * 1e3, 1), "tflops": round(flops / ms / 1e9, 1),
         "frac_of_bf16_peak": round(flops / ms / 1e9 / tc_peak, 4),
         "e2e_tokens_per_s": round(P_len / e2e_ms * 1e3, 1),
@@ -637,7 +640,8 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3):
 
     # ---- decode over a ctx-token context
     dc = model.create_paged_kv_cache(Bmax, ctx + steps + 8)
-    for s in range(min(distinct, Bmax)):
+    distinct = min(distinct, Bmax)
+    for s in range(distinct):
         p = torch.randint(0, V, (ctx,), generator=g, device=dev)
         dc.begin_forward([s], [ctx])
         model.prefill(model.embed(p), dc)
@@ -712,7 +716,9 @@ def full_model_only(args):
     names = list(FULL_MODEL_CASES) if args.full_model == "all" else [n for n in FULL_MODEL_CASES
                                                                       if n.startswith(args.full_model)]
     dev = torch.device("cuda", 0)
-    out = {n: full_model_bench(dev, peaks, n, steps=args.steps, warmup=args.warmup) for n in names}
+    batches = [int(b) for b in args.fm_batches.split(",")] if args.fm_batches else None
+    out = {n: full_model_bench(dev, peaks, n, steps=args.steps, warmup=args.warmup, batches=batches,
+                               prefill=args.fm_prefill) for n in names}
     print(json.dumps({"full_model": out}), flush=True)
 
 
@@ -796,6 +802,9 @@ def main():
                     help="full-model decode/prefill measurements added to the line (1 GPU)")
     ap.add_argument("--full-model-only", action="store_true",
                     help="run only the --full-model measurements and print them")
+    ap.add_argument("--fm-batches", default=None, help="with --full-model-only: comma-separated decode batch sizes")
+    ap.add_argument("--no-fm-prefill", dest="fm_prefill", action="store_false",
+                    help="with --full-model-only: skip the long-prompt prefill measurement")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

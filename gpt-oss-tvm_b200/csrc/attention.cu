@@ -78,30 +78,42 @@ struct RopeTable {
   float inv_freq[128];
 };
 
+// One block per (token, group of kRopeHeads heads): the block computes the
+// D/2 rotation factors of its token once (sincosf of pos * inv_freq[f],
+// times the concentration) and applies them to its heads.
+constexpr int kRopeHeads = 8;
+
 __global__ void qkv_rope_kernel(const uint16_t* __restrict__ qkv, const int32_t* __restrict__ pos,
                                 const int32_t* __restrict__ slot, int64_t S, int32_t Hq, int32_t Hkv, int32_t D,
                                 const RopeTable tab, float conc, uint16_t* __restrict__ q_out,
                                 uint16_t* __restrict__ k_cache, uint16_t* __restrict__ v_cache) {
-  // one block per token; threads over (head, dim) of q, k and v
+  __shared__ float cos_s[128], sin_s[128];
   const int64_t s = blockIdx.x;
   if (s >= S) return;
   const int32_t Ht = Hq + 2 * Hkv;
+  const int32_t h0 = blockIdx.y * kRopeHeads;
+  const int32_t nh = min(kRopeHeads, Ht - h0);
   const uint16_t* row = qkv + s * (int64_t)Ht * D;
   const int32_t half = D / 2;
   const float p = (float)pos[s];
   const int64_t dst_slot = slot ? slot[s] : s;
-  for (int32_t i = threadIdx.x; i < Ht * D; i += blockDim.x) {
-    const int32_t h = i / D, d = i % D;
+  for (int32_t f = threadIdx.x; f < half; f += blockDim.x) {
+    const float ang = __fmul_rn(p, tab.inv_freq[f]);
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    cos_s[f] = __fmul_rn(cs, conc);
+    sin_s[f] = __fmul_rn(sn, conc);
+  }
+  __syncthreads();
+  for (int32_t i = threadIdx.x; i < nh * D; i += blockDim.x) {
+    const int32_t h = h0 + i / D, d = i % D;
     const uint16_t* xr = row + (int64_t)h * D;
     if (h >= Hq + Hkv) {  // v: copy
       v_cache[(dst_slot * Hkv + (h - Hq - Hkv)) * D + d] = xr[d];
       continue;
     }
     const int32_t f = d & (half - 1);
-    const float ang = __fmul_rn(p, tab.inv_freq[f]);
-    float sn, cs;
-    sincosf(ang, &sn, &cs);
-    const float c = __fmul_rn(cs, conc), sv = __fmul_rn(sn, conc);
+    const float c = cos_s[f], sv = sin_s[f];
     float o;
     if (d >= half) o = __fadd_rn(__fmul_rn(bf16_bits_to_f32(xr[d - half]), sv), __fmul_rn(bf16_bits_to_f32(xr[d]), c));
     else o = __fsub_rn(__fmul_rn(bf16_bits_to_f32(xr[d]), c), __fmul_rn(bf16_bits_to_f32(xr[d + half]), sv));
@@ -911,7 +923,8 @@ int launch_qkv_rope(const uint16_t* qkv, const int32_t* pos, const int32_t* slot
   if (D > 256 || D % 2) return -12;
   RopeTable tab;
   for (int i = 0; i < D / 2; ++i) tab.inv_freq[i] = inv_freq[i];
-  qkv_rope_kernel<<<(unsigned)S, 256, 0, s>>>(qkv, pos, slot, S, Hq, Hkv, D, tab, conc, q_out, k_cache, v_cache);
+  const dim3 grid((unsigned)S, (unsigned)((Hq + 2 * Hkv + kRopeHeads - 1) / kRopeHeads));
+  qkv_rope_kernel<<<grid, 256, 0, s>>>(qkv, pos, slot, S, Hq, Hkv, D, tab, conc, q_out, k_cache, v_cache);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

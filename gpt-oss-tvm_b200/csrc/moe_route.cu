@@ -49,9 +49,12 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
   if (ok && threadIdx.x < nrows) {
     const uint4* row = (const uint4*)(rowbuf + (size_t)threadIdx.x * pitch);
     float ss = 0.0f;
+    // the next 8 elements are read while the sum runs through these 8
+    uint4 vn = row[0];
 #pragma unroll 4
     for (int32_t k8 = 0; k8 < H / 8; ++k8) {
-      const uint4 v = row[k8];
+      const uint4 v = vn;
+      if (k8 + 1 < H / 8) vn = row[k8 + 1];
       const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -289,10 +292,15 @@ __global__ void __launch_bounds__(128) router_chain_kernel(const uint16_t* __res
     const uint16_t* trow = ts[buf][tok];
     const uint16_t* wa = ws[buf][p];
     const uint16_t* wb = ws[buf][p + 8];
+    // the next 8 columns are read while the chain runs through these 8
+    uint4 tn = *(const uint4*)trow, an = *(const uint4*)wa, bn = *(const uint4*)wb;
     for (int32_t kk = 0; kk < kn; kk += 8) {
-      const uint4 tv = *(const uint4*)(trow + kk);
-      const uint4 av = *(const uint4*)(wa + kk);
-      const uint4 bv = *(const uint4*)(wb + kk);
+      const uint4 tv = tn, av = an, bv = bn;
+      if (kk + 8 < kn) {
+        tn = *(const uint4*)(trow + kk + 8);
+        an = *(const uint4*)(wa + kk + 8);
+        bn = *(const uint4*)(wb + kk + 8);
+      }
       const uint32_t tw[4] = {tv.x, tv.y, tv.z, tv.w};
       const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
       const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
