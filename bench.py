@@ -17,6 +17,11 @@ value: whole-job tokens/s with inputs resident in HBM; e2e: the same through
 the public MLPBlock API with the input copied from pinned host memory and the
 output copied back inside the timed region.  The 1.7 GB of expert weights per
 GPU exceed the 126 MB L2, so no explicit flush is needed between steps.
+
+At N = 1 the line also carries `full_model`: the whole gpt-oss-20b
+and gpt-oss-120b forwards on random-init weights -- greedy decode
+at batch 1 / 8 / 64 over a 2048-token context and at batch 256 over 4096, one
+CUDA graph per step, plus 4096- and 16384-token prefills (`--full-model`).
 """
 from __future__ import annotations
 
@@ -790,7 +795,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--cpu-tokens", type=int, default=32, help="token sample of the CPU baseline")
+    ap.add_argument("--cpu-tokens", type=int, default=448, help="token sample of the CPU baseline (about 10 s)")
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU (default: the configs[3] 8192)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-decode", dest="decode", action="store_false", help="skip the MoE decode measurements")
@@ -798,7 +803,7 @@ def main():
                     help="expert-parallel row exchange (N > 1): stores into the ranks' IPC-shared buffers or NCCL")
     ap.add_argument("--decode-only", type=int, default=None, choices=range(len(DECODE_CASES)),
                     help="run only this decode case (index into DECODE_CASES) and print its measurement")
-    ap.add_argument("--full-model", default="gpt-oss-20b", choices=["none", "gpt-oss-20b", "gpt-oss-120b", "all"],
+    ap.add_argument("--full-model", default="all", choices=["none", "gpt-oss-20b", "gpt-oss-120b", "all"],
                     help="full-model decode/prefill measurements added to the line (1 GPU)")
     ap.add_argument("--full-model-only", action="store_true",
                     help="run only the --full-model measurements and print them")

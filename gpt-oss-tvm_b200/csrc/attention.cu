@@ -976,9 +976,18 @@ size_t attn_decode_scratch_bytes(int64_t B, int32_t Hq, int64_t max_len, int32_t
   return (size_t)B * Hq * splits * (kAttD + 2) * sizeof(float);
 }
 
-int attn_decode_splits(int64_t max_len, int32_t window) {
+// Key splits per (sequence, kv head): one per kDecSplitKeys keys of the
+// longest span; with few sequences the splits are halved (down to
+// kDecMinSplitKeys keys) until about two CTAs per SM are busy, since a
+// single-token decode is otherwise latency-bound on a few SMs.
+constexpr int64_t kDecTargetCtas = 2 * 148;
+constexpr int64_t kDecMinSplitKeys = 128;
+int attn_decode_splits(int64_t B, int32_t Hq, int64_t max_len, int32_t window) {
   const int64_t span = window > 0 ? min64(max_len, window) : max_len;
-  return (int)max64(1, (span + kDecSplitKeys - 1) / kDecSplitKeys);
+  int64_t splits = max64(1, (span + kDecSplitKeys - 1) / kDecSplitKeys);
+  const int64_t units = max64(1, B) * max64(1, Hq / 8);
+  while (units * splits < kDecTargetCtas && (span + 2 * splits - 1) / (2 * splits) >= kDecMinSplitKeys) splits *= 2;
+  return (int)splits;
 }
 
 int launch_attn_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* kv_len, int64_t B,
@@ -986,7 +995,7 @@ int launch_attn_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc
                        const uint16_t* sinks, float* scratch, uint16_t* o, float* lse, cudaStream_t s) {
   if (B <= 0) return 0;
   if (D != kAttD || Hq % Hkv || Hq / Hkv > 8) return -12;
-  const int splits = attn_decode_splits(max_len, window);
+  const int splits = attn_decode_splits(B, Hq, max_len, window);
   float* part_o = scratch;
   float* part_ml = scratch + (size_t)B * Hq * splits * kAttD;
   const size_t smem = 16 * 128 + kDecWarps * 2 * 2 * kAttBK * 128 + kDecWarps * (16 + 16 + 16 * 64) * 4;

@@ -379,7 +379,7 @@ int gptoss_attn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v,
 }
 
 int64_t gptoss_attn_decode_scratch_bytes(int64_t B, int32_t Hq, int64_t max_len, int32_t window) {
-  return (int64_t)attn_decode_scratch_bytes(B, Hq, max_len, attn_decode_splits(max_len, window));
+  return (int64_t)attn_decode_scratch_bytes(B, Hq, max_len, attn_decode_splits(B, Hq, max_len, window));
 }
 
 int gptoss_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_t* v_cache, const int32_t* kv_len,

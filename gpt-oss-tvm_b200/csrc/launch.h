@@ -77,7 +77,7 @@ int launch_attn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                         int64_t Skv, int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale, uint16_t* o,
                         float* lse, cudaStream_t s);
 size_t attn_decode_scratch_bytes(int64_t B, int32_t Hq, int64_t max_len, int32_t splits);
-int attn_decode_splits(int64_t max_len, int32_t window);
+int attn_decode_splits(int64_t B, int32_t Hq, int64_t max_len, int32_t window);
 int launch_attn_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* kv_len, int64_t B,
                        int64_t max_len, int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale,
                        const uint16_t* sinks, float* scratch, uint16_t* o, float* lse, cudaStream_t s);

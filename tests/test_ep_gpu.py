@@ -41,6 +41,11 @@ def _worker(rank, world, port, E, M, exact, peer, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
+    # one GEMM kernel for every row placement: the decode GEMV (<= 64 routed
+    # rows) adds in a different order than the tensor-core kernel, and only
+    # the latter has the peer-return epilogue, so bit-equality across the
+    # placements is a property of the tensor-core kernel alone
+    os.environ["GPTOSS_MOE_GEMV"] = "0"
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
