@@ -553,7 +553,7 @@ def _routed_experts(model, cache, ids, lib):
     return counts
 
 
-def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill=True):
+def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill=True, ep=False):
     """Full-model forward (GPTOssForCausalLM, random-init weights from a
     seed): greedy decode at the configuration's batch sizes over its context
     (sequences 0..B-1, one CUDA graph per step: embedding, every layer, final
@@ -569,7 +569,14 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
     embedding rows, unembedding weight and the logits.  The >= 13 GB of
     weights read per step exceed the 126 MB L2 (no flush needed).
     e2e: the same steps with each step's input tokens copied from pinned host
-    memory and its greedy tokens copied back (host sync every step)."""
+    memory and its greedy tokens copied back (host sync every step).
+
+    ep (torchrun, one process per GPU): the experts of every layer are sharded
+    over the ranks and each rank runs attention for its own prompts and decode
+    batch (weak scaling); times are the max over ranks, tokens/s count every
+    rank's tokens, and the decode steps run eagerly (their exchanges hold
+    collectives).  The bytes-per-step accounting is single-GPU only."""
+    import torch.distributed as dist
     import numpy as np
     import torch
     modm = importlib.import_module("gpt-oss-tvm_b200.model")
@@ -582,12 +589,22 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
     L, V, H = cfg.num_hidden_layers, cfg.vocab_size, cfg.hidden_size
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     tc_peak = float(peaks.get("bf16_tflops", 1590.0))
+    world = dist.get_world_size() if ep else 1
+    rank = dist.get_rank() if ep else 0
+
+    def slowest(ms):
+        if not ep:
+            return ms
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
     t0 = time.perf_counter()
-    model = modm.random_init(modm.GPTOssForCausalLM(cfg, device=dev), seed=0)
+    model = modm.random_init(modm.GPTOssForCausalLM(cfg, device=dev, expert_parallel=True if ep else None), seed=0)
     Bmax = max(batches)
     model.reserve(max(P_len, Bmax, ctx))
     g = torch.Generator(device=dev)
-    g.manual_seed(7)
+    g.manual_seed(7 + rank)
     res = {"weights_gb": round(sum(t.numel() * t.element_size() for _, t in model.named_parameters()) / 1e9, 2),
            "init_s": round(time.perf_counter() - t0, 1)}
 
@@ -616,7 +633,7 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
         b.record()
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b))
-    ms = statistics.median(times) if times else 0.0
+    ms = slowest(statistics.median(times) if times else 0.0)
     ids_host = ids.cpu().pin_memory()
     tok_host = torch.empty(1, dtype=torch.int64).pin_memory()
     times = []
@@ -628,16 +645,17 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
         b.record()
         torch.cuda.synchronize()
         times.append(a.elapsed_time(b))
-    e2e_ms = statistics.median(times) if times else 0.0
+    e2e_ms = slowest(statistics.median(times) if times else 0.0)
     D, Hq, Hkv, W = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads, cfg.sliding_window_size
     dense = 2 * P_len * H * (D * (Hq + 2 * Hkv)) + 2 * P_len * (D * Hq) * H
     attn = sum(4 * D * Hq * (P_len * P_len / 2 if i % 2 else P_len * min(W, P_len)) for i in range(L))
     moe = 2 * P_len * cfg.num_experts_per_tok * (2 * cfg.intermediate_size * H + H * cfg.intermediate_size)
     flops = L * (dense + moe) + attn + 2 * H * V
     res[f"prefill {P_len} tokens"] = {} if not P_len else {
-        "ms": round(ms, 3), "tokens_per_s": round(P_len / ms * 1e3, 1), "tflops": round(flops / ms / 1e9, 1),
+        "ms": round(ms, 3), "tokens_per_s": round(world * P_len / ms * 1e3, 1),
+        "tflops": round(world * flops / ms / 1e9, 1),
         "frac_of_bf16_peak": round(flops / ms / 1e9 / tc_peak, 4),
-        "e2e_tokens_per_s": round(P_len / e2e_ms * 1e3, 1),
+        "e2e_tokens_per_s": round(world * P_len / e2e_ms * 1e3, 1),
         "e2e": "prompt ids copied from pinned host memory, greedy token copied back, inside the timed region",
         "flops_per_prefill": flops}
     del pc
@@ -655,6 +673,11 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
             dc.k[layer][s, :ctx].copy_(dc.k[layer][s % distinct, :ctx])
             dc.v[layer][s, :ctx].copy_(dc.v[layer][s % distinct, :ctx])
     torch.cuda.synchronize()
+    if ep:
+        # exchange buffers sized for the decode batch (the GEMMs of an
+        # expert-parallel step are launched on the buffer capacity)
+        model.release()
+        model.reserve(Bmax)
 
     def restart():
         dc.lengths.fill_(ctx)
@@ -666,7 +689,7 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
     for B in batches:
         restart()
         tokens = torch.randint(0, V, (B,), generator=g, device=dev)
-        routed = _routed_experts(model, dc, tokens, lib)
+        routed = _routed_experts(model, dc, tokens, lib) if not ep else None
         dec = engm.GreedyDecodeGraph(model, dc, B)
         dec.set_tokens(tokens)
         for _ in range(warmup):
@@ -680,7 +703,7 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
             dec.step()
         b.record()
         torch.cuda.synchronize()
-        ms = a.elapsed_time(b) / steps
+        ms = slowest(a.elapsed_time(b) / steps)
         # e2e through pinned host buffers, host sync every step
         restart()
         th = tokens.cpu().pin_memory()
@@ -696,8 +719,14 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
             th.copy_(nh)
         b.record()
         torch.cuda.synchronize()
-        e2e_ms = a.elapsed_time(b) / steps
+        e2e_ms = slowest(a.elapsed_time(b) / steps)
         dec.close()
+        if ep:
+            res[f"decode batch {B} per GPU over {ctx} context"] = {
+                "ms_per_step": round(ms, 4), "tokens_per_s": round(world * B / ms * 1e3, 1),
+                "e2e_tokens_per_s": round(world * B / e2e_ms * 1e3, 1), "n_gpus": world,
+                "experts_per_gpu": cfg.num_experts // world}
+            continue
         kv = B * sum(kv_span) * Hkv * D * 2 * 2
         nbytes = attn_w + router_w + sum(routed) * EXPERT_BYTES + kv + H * V * 2 + B * H * 2 + B * V * (4 + 2 * 2)
         gbs = nbytes / ms / 1e6
@@ -716,15 +745,32 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
 
 
 def full_model_only(args):
+    """--full-model-only: the full-model measurements alone.  Under torchrun
+    (N > 1), or with --fm-ep, the model runs expert-parallel over the ranks."""
+    import datetime
+
     import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
     peaks, _ = measured_peaks()
     names = list(FULL_MODEL_CASES) if args.full_model == "all" else [n for n in FULL_MODEL_CASES
                                                                       if n.startswith(args.full_model)]
-    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ep = world > 1 or args.fm_ep
+    if ep:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29517")
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=120))
     batches = [int(b) for b in args.fm_batches.split(",")] if args.fm_batches else None
     out = {n: full_model_bench(dev, peaks, n, steps=args.steps, warmup=args.warmup, batches=batches,
-                               prefill=args.fm_prefill) for n in names}
-    print(json.dumps({"full_model": out}), flush=True)
+                               prefill=args.fm_prefill, ep=ep) for n in names}
+    if rank == 0:
+        print(json.dumps({"full_model": out, "n_gpus": world}), flush=True)
+    if ep:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def cpu_baseline(args):
@@ -808,6 +854,8 @@ def main():
     ap.add_argument("--full-model-only", action="store_true",
                     help="run only the --full-model measurements and print them")
     ap.add_argument("--fm-batches", default=None, help="with --full-model-only: comma-separated decode batch sizes")
+    ap.add_argument("--fm-ep", action="store_true",
+                    help="with --full-model-only: expert-parallel model even on one GPU (a one-rank group)")
     ap.add_argument("--no-fm-prefill", dest="fm_prefill", action="store_false",
                     help="with --full-model-only: skip the long-prompt prefill measurement")
     args = ap.parse_args()

@@ -145,10 +145,31 @@ __device__ __forceinline__ void gv_round(const GvLoad& L, float (&acc)[2][2][4],
   }
 }
 
+// The y-th expert (in expert order) that has routed rows, or -1: each warp
+// scans indptr 32 experts at a time with a ballot.
+__device__ __forceinline__ int32_t gv_routed_expert(const int32_t* __restrict__ indptr, int32_t E, int32_t y) {
+  const int lane = threadIdx.x & 31;
+  int32_t seen = 0;
+  for (int32_t base = 0; base < E; base += 32) {
+    const int32_t e = base + lane;
+    const bool has = e < E && __ldg(indptr + e + 1) > __ldg(indptr + e);
+    const uint32_t m = __ballot_sync(0xffffffffu, has);
+    const int32_t n = __popc(m);
+    if (y < seen + n) {
+      uint32_t mm = m;
+      for (int32_t k = 0; k < y - seen; ++k) mm &= mm - 1;  // drop the lower set bits
+      return base + __ffs(mm) - 1;
+    }
+    seen += n;
+  }
+  return -1;
+}
+
 template <int kMode>
 __global__ void __launch_bounds__(kGvWarps * 32) moe_gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(16) uint8_t gv_smem[];
-  const int32_t e = blockIdx.y;
+  const int32_t e = gv_routed_expert(p.indptr, p.E, blockIdx.y);  // grid.y covers the routed experts at most
+  if (e < 0) return;
   const int64_t r0 = __ldg(p.indptr + e), r1 = __ldg(p.indptr + e + 1);
   const int64_t nrows = r1 - r0;
   if (nrows <= 0) return;
@@ -175,9 +196,14 @@ __global__ void __launch_bounds__(kGvWarps * 32) moe_gemv_kernel(const GemvParam
     }
   const int32_t chunks_row = p.K >> 3;
   float* red = (float*)(gv_smem + (size_t)p.tok_cap * S);  // [warp][lane][16]
+  constexpr int kStep = kGvWarps;
   for (int64_t c0 = 0; c0 < nrows; c0 += p.tok_cap) {
     const int nv = (int)min64(p.tok_cap, nrows - c0);
     if (c0 > 0) __syncthreads();  // the previous pass is done with the staged rows
+    // the first round of weights is requested before the token rows are
+    // staged (they do not depend on each other)
+    GvLoad A, B;
+    if (warp < rounds) gv_load(A, wrow, srow, 4 * warp + q, G);
     for (int i = threadIdx.x; i < nv * chunks_row; i += blockDim.x) {
       const int n = i / chunks_row, ch = i - n * chunks_row;
       const uint4 v = __ldg((const uint4*)(p.act + (size_t)(r0 + c0 + n) * p.K) + ch);
@@ -192,9 +218,6 @@ __global__ void __launch_bounds__(kGvWarps * 32) moe_gemv_kernel(const GemvParam
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[mt][nt][j] = 0.f;
     const bool two_n = nv > 8;
-    GvLoad A, B;
-    constexpr int kStep = kGvWarps;
-    if (warp < rounds) gv_load(A, wrow, srow, 4 * warp + q, G);
     for (int32_t r = warp; r < rounds; r += 2 * kStep) {
       const int32_t r1 = r + kStep, r2 = r + 2 * kStep;
       if (r1 < rounds) gv_load(B, wrow, srow, 4 * r1 + q, G);
@@ -300,7 +323,8 @@ int launch_moe_gemv(int mode, const GemmLaunch& L, cudaStream_t stream) {
   p.tok_cap = (int32_t)min64(kGvTokDecode, L.act_rows);
   p.err = L.err;
   const size_t smem = (size_t)p.tok_cap * (2 * (size_t)L.K + 32) + kGvRedBytes;
-  const dim3 grid((unsigned)((L.N + kGvRowsCta - 1) / kGvRowsCta), (unsigned)L.E);
+  // at most act_rows experts have rows: CTAs for the routed experts only
+  const dim3 grid((unsigned)((L.N + kGvRowsCta - 1) / kGvRowsCta), (unsigned)min64(L.E, L.act_rows));
   if (mode == 0) {
     static bool attr = false;
     if (!attr) {

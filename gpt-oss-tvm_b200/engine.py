@@ -217,7 +217,11 @@ class GreedyDecodeGraph:
     launch and the cache-capacity check.  ``logits`` and ``next_ids`` are the
     step's static outputs."""
 
-    def __init__(self, model: GPTOssForCausalLM, cache: KVCache, batch: int, use_graph: bool = True):
+    def __init__(self, model: GPTOssForCausalLM, cache: KVCache, batch: int, use_graph: bool | None = None):
+        """use_graph: capture the step (default: yes, unless the model is
+        expert-parallel -- its steps hold collectives, run eagerly)."""
+        if use_graph is None:
+            use_graph = not model.expert_parallel
         self.model, self.cache, self.B = model, cache, batch
         cache.check_decode(batch)
         self.ids = torch.zeros(batch, dtype=torch.int64, device=model.device)

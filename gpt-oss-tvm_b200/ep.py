@@ -310,6 +310,21 @@ class ExpertParallelMoE:
         self._splits = None
         self._counts_all = None
 
+    def use(self, blk) -> "ExpertParallelMoE":
+        """Run the next forwards on `blk`'s weights (the same expert shard and
+        shapes): one runner, with one set of exchange buffers, serves every MoE
+        layer of a model.  Every rank must switch to the same layer, and the
+        ranks must agree on each layer's GEMM path (flags)."""
+        a, b = self.blk, blk
+        if (a.num_experts, a.num_local_experts, a.expert_offset, a.hidden_size) != \
+                (b.num_experts, b.num_local_experts, b.expert_offset, b.hidden_size):
+            raise ValueError("ExpertParallelMoE.use: a block of another expert shard or shape")
+        self.blk = blk
+        self.backend.blk = blk
+        if hasattr(self.backend, "f16"):
+            self.backend.f16 = 1 if blk.f16_path else 0
+        return self
+
     def _layout(self, counts):
         """All-gather the per-expert row counts and lay out the rows (no host round trip)."""
         counts_all = torch.empty(self.world * counts.numel(), dtype=counts.dtype, device=counts.device)
@@ -348,6 +363,8 @@ class ExpertParallelMoE:
     def forward(self, x, out=None):
         b = self.backend
         x2 = x.reshape(-1, self.blk.hidden_size)
+        if x2.shape[0] > b.max_tokens:
+            raise ValueError(f"ExpertParallelMoE: {x2.shape[0]} tokens exceed max_tokens={b.max_tokens}")
         if out is None:
             out = torch.empty_like(x2)
         out2 = out.reshape(-1, self.blk.hidden_size)

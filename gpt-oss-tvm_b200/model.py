@@ -22,6 +22,12 @@ and the unembedding (a plain bf16 GEMM, cast to fp32 as in _get_logits,
 model/transformer.py:97-102) are torch (cuBLAS) calls.  All the MoE blocks of
 a model share one scratch workspace and all attention blocks one decode
 scratch buffer.
+
+Expert parallelism (``expert_parallel=`` a process group, or True for the
+default group): rank r holds experts [r*E/P, (r+1)*E/P) of every layer and the
+whole of everything else; each rank runs attention for its own sequences and
+every MoE layer exchanges rows with the other ranks through one shared
+ExpertParallelMoE runner (peer-memory buffers, reused by all layers).
 """
 from __future__ import annotations
 
@@ -85,13 +91,28 @@ class Linear:
     __call__ = forward
 
 
+class _ShardedMoE:
+    """The MoE step of one layer on an expert shard: the model's shared
+    expert-parallel runner, switched to this layer's weights."""
+
+    def __init__(self, runner, blk: MLPBlock):
+        self.runner, self.blk = runner, blk
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        return self.runner.use(self.blk).forward(x).reshape(x.shape)
+
+
 class TransformerBlock:
     """model/transformer.py:15-33: x -> attn(x) -> mlp(.)."""
 
-    def __init__(self, config: GPTOssConfig, layer_idx: int, dtype: str | None = None, device="cuda"):
+    def __init__(self, config: GPTOssConfig, layer_idx: int, dtype: str | None = None, device="cuda",
+                 expert_shard: tuple[int, int] | None = None):
         self.layer_idx = layer_idx
         self.attn = AttentionBlock(config, layer_idx, dtype, device)
-        self.mlp = MLPBlock(config, rms_norm_eps=1e-5, dtype=dtype, device=device)
+        off, El = expert_shard if expert_shard is not None else (0, config.num_experts)
+        self.mlp = MLPBlock(config, rms_norm_eps=1e-5, dtype=dtype, device=device, expert_offset=off,
+                            num_local_experts=El)
+        self.moe = None  # set for expert parallelism (_ShardedMoE)
 
     def named_parameters(self):
         for name, attr in AttentionBlock.PARAM_NAMES.items():
@@ -102,7 +123,7 @@ class TransformerBlock:
     def forward(self, x: torch.Tensor, paged_kv_cache: KVCache, query_positions: torch.Tensor | None,
                 forward_to: str):
         x, paged_kv_cache = self.attn(x, paged_kv_cache, query_positions, forward_to)
-        x = self.mlp(x)
+        x = self.moe(x) if self.moe is not None else self.mlp(x)
         return x, paged_kv_cache
 
     __call__ = forward
@@ -111,10 +132,12 @@ class TransformerBlock:
 class Transformer:
     """model/transformer.py:36-66: embedding, ``block`` list, final ``norm``."""
 
-    def __init__(self, config: GPTOssConfig, dtype: str | None = None, device="cuda"):
+    def __init__(self, config: GPTOssConfig, dtype: str | None = None, device="cuda",
+                 expert_shard: tuple[int, int] | None = None):
         self.config = config
         self.embedding = Embedding(config.vocab_size, config.hidden_size, device)
-        self.block = [TransformerBlock(config, i, dtype, device) for i in range(config.num_hidden_layers)]
+        self.block = [TransformerBlock(config, i, dtype, device, expert_shard)
+                      for i in range(config.num_hidden_layers)]
         self.norm = RMSNorm(config.hidden_size, 1e-5, device)
         scratch = DecodeScratch(device)
         for blk in self.block:
@@ -140,13 +163,25 @@ class Transformer:
 class GPTOssForCausalLM:
     """model/transformer.py:69-175."""
 
-    def __init__(self, config: GPTOssConfig, dtype: str | None = None, device="cuda"):
+    def __init__(self, config: GPTOssConfig, dtype: str | None = None, device="cuda", expert_parallel=None):
         self.config = config
         self.dtype = dtype or config.dtype
         if self.dtype != "bfloat16":
             raise ValueError("GPTOssForCausalLM supports bfloat16 only")
         self.device = torch.device(device)
-        self.model = Transformer(config, self.dtype, device)
+        self.ep_group, self.ep_runner = None, None
+        self.ep_exact_return = False  # fp32 expert rows back to their owners (else bf16)
+        self.expert_shard = (0, config.num_experts)
+        self._ep = expert_parallel is not None and expert_parallel is not False
+        if self._ep:
+            import torch.distributed as dist
+            self.ep_group = None if expert_parallel is True else expert_parallel
+            world, rank = dist.get_world_size(self.ep_group), dist.get_rank(self.ep_group)
+            if config.num_experts % world:
+                raise ValueError(f"{config.num_experts} experts do not split over {world} ranks")
+            El = config.num_experts // world
+            self.expert_shard = (rank * El, El)
+        self.model = Transformer(config, self.dtype, device, self.expert_shard)
         self.unembedding = Linear(config.hidden_size, config.vocab_size, device)
         self.hidden_size = config.hidden_size
         self.num_hidden_layers = config.num_hidden_layers
@@ -165,13 +200,41 @@ class GPTOssForCausalLM:
             blk.mlp.prepare()
         return self
 
+    @property
+    def expert_parallel(self) -> bool:
+        return self._ep
+
     def reserve(self, max_tokens: int) -> "GPTOssForCausalLM":
-        """Size the shared MoE workspace for forwards of up to ``max_tokens``
-        tokens (a captured decode graph must not see it move)."""
-        self.model.block[0].mlp.workspace(max_tokens)
+        """Size the shared MoE workspace (or, with expert parallelism, the
+        exchange buffers) for forwards of up to ``max_tokens`` tokens per rank
+        (a captured decode graph must not see them move)."""
+        if not self._ep:
+            self.model.block[0].mlp.workspace(max_tokens)
+            return self
+        if self.ep_runner is not None and self.ep_runner.backend.max_tokens >= max_tokens:
+            return self
+        import torch.distributed as dist
+        from .ep import ExpertParallelMoE
+        blocks = [b.mlp for b in self.model.block]
+        # the ranks agree on each layer's GEMM path (the rows travel in its activation type)
+        f = torch.tensor([b.flags for b in blocks], dtype=torch.int32, device=self.device)
+        dist.all_reduce(f, op=dist.ReduceOp.MIN, group=self.ep_group)
+        for b, v in zip(blocks, f.tolist()):
+            b.flags = int(v)
+        if self.ep_runner is not None:
+            self.ep_runner.close()
+        self.ep_runner = ExpertParallelMoE(blocks[0], max_tokens, group=self.ep_group, peer=True,
+                                           exact_return=self.ep_exact_return)
+        for b in self.model.block:
+            b.moe = _ShardedMoE(self.ep_runner, b.mlp)
         return self
 
     def release(self) -> None:
+        if self.ep_runner is not None:
+            self.ep_runner.close()
+            self.ep_runner = None
+            for b in self.model.block:
+                b.moe = None
         self.model.block[0].mlp.free_workspace()
 
     def create_paged_kv_cache(self, max_batch_size: int, max_total_seq_len: int) -> KVCache:

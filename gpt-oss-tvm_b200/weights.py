@@ -38,6 +38,9 @@ def load_checkpoint(model: GPTOssForCausalLM, path, prepare: bool = True) -> GPT
             t = f.get_tensor(key)
             if "blocks" in key or "scales" in key:
                 t = t.to(torch.uint8)
+            off, El = model.expert_shard
+            if (".mlp.mlp1_" in name or ".mlp.mlp2_" in name) and t.shape[0] != dst.shape[0]:
+                t = t[off:off + El]  # this rank's experts (expert parallelism)
             if tuple(t.shape) != tuple(dst.shape):
                 raise ValueError(f"{key}: checkpoint shape {tuple(t.shape)} != parameter shape {tuple(dst.shape)}")
             dst.copy_(t.to(dst.dtype))

@@ -160,3 +160,48 @@ def test_top_p_sampling(seed):
     assert got == _top_p_numpy(z.astype(np.float64), 0.7, 0.9, 0.5)
     fake.sample_parameters["temperature"] = 0.0
     assert engm.Engine.sample(fake, torch.from_numpy(z)) == int(np.argmax(z))
+
+
+def test_expert_parallel_model_shards_experts_one_rank_gloo():
+    """Construction over a one-rank gloo group: the expert shard of every
+    layer, the same parameter names as the plain model, the loader slice."""
+    import os
+    import socket
+
+    import torch.distributed as dist
+    modm, cfgm, wm, _, _ = mods()
+    sock = socket.socket()
+    sock.bind(("127.0.0.1", 0))
+    port = sock.getsockname()[1]
+    sock.close()
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    try:
+        cfg = small_config(cfgm, layers=1)
+        m = modm.GPTOssForCausalLM(cfg, device="cpu", expert_parallel=True)
+        assert m.expert_parallel and m.expert_shard == (0, 4)
+        assert m.model.block[0].mlp.num_local_experts == 4 and m.model.block[0].mlp.expert_offset == 0
+        p = modm.GPTOssForCausalLM(cfg, device="cpu")
+        assert not p.expert_parallel
+        assert [n for n, _ in m.named_parameters()] == [n for n, _ in p.named_parameters()]
+    finally:
+        dist.destroy_process_group()
+
+
+def test_checkpoint_loader_slices_expert_shard(tmp_path):
+    """A rank of an expert-parallel model takes its experts [off, off + El)
+    out of the full checkpoint tensors."""
+    modm, cfgm, wm, _, _ = mods()
+    cfg = small_config(cfgm, layers=1)
+    full = modm.random_init(modm.GPTOssForCausalLM(cfg, device="cpu"), seed=4, prepare=False)
+    wm.save_checkpoint(full, tmp_path)
+    part = modm.GPTOssForCausalLM(cfg, device="cpu")
+    # a two-rank layout seen from rank 1 (constructed without a process group)
+    part.expert_shard = (2, 2)
+    part.model = modm.Transformer(cfg, "bfloat16", "cpu", (2, 2))
+    wm.load_checkpoint(part, tmp_path, prepare=False)
+    a, b = full.model.block[0].mlp, part.model.block[0].mlp
+    assert torch.equal(b.mlp1_weight_blocks, a.mlp1_weight_blocks[2:4])
+    assert torch.equal(b.mlp2_bias, a.mlp2_bias[2:4])
+    assert torch.equal(b.gate_weight, a.gate_weight)
