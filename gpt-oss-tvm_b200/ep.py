@@ -363,8 +363,9 @@ class ExpertParallelMoE:
     def forward(self, x, out=None):
         b = self.backend
         x2 = x.reshape(-1, self.blk.hidden_size)
-        if x2.shape[0] > b.max_tokens:
-            raise ValueError(f"ExpertParallelMoE: {x2.shape[0]} tokens exceed max_tokens={b.max_tokens}")
+        cap = getattr(b, "max_tokens", None)  # the CUDA backend's buffers hold max_tokens rows
+        if cap is not None and x2.shape[0] > cap:
+            raise ValueError(f"ExpertParallelMoE: {x2.shape[0]} tokens exceed max_tokens={cap}")
         if out is None:
             out = torch.empty_like(x2)
         out2 = out.reshape(-1, self.blk.hidden_size)
