@@ -10,8 +10,10 @@ expert GEMMs, weighted combine, residual) over that batch.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl {b200,reference}]
 
 With N > 1 (torchrun, one process per GPU) the experts are sharded E/N per
-rank (expert parallelism) and every rank routes its own 8192 tokens; the
-token dispatch and combine are NCCL all-to-all exchanges (weak scaling).
+rank (expert parallelism) and every rank routes its own 8192 tokens (weak
+scaling); the rows move through peer memory (stores into the other ranks'
+CUDA-IPC buffers, `--exchange peer`, the default) or NCCL all-to-all-v
+(`--exchange nccl`).
 
 value: whole-job tokens/s with inputs resident in HBM; e2e: the same through
 the public MLPBlock API with the input copied from pinned host memory and the
