@@ -129,6 +129,24 @@ class KVCache:
         """Forget device-side steps that were not committed (graph warm-up)."""
         self._sync_dev_lengths()
 
+    def add_sequence(self, seq_id: int):
+        """Start sequence `seq_id` empty (kv_state_add_sequence, engine.py:112)."""
+        if not 0 <= seq_id < self.max_batch:
+            raise ValueError(f"sequence id {seq_id} outside the cache's {self.max_batch} sequences")
+        self.lengths[seq_id] = 0
+        self._sync_dev_lengths()
+
+    def remove_sequence(self, seq_id: int):
+        """Forget sequence `seq_id` (its rows are reused by the next sequence
+        started in that slot)."""
+        self.add_sequence(seq_id)
+
+    def end_forward(self):
+        """Close the pass planned by begin_forward (kv_state_end_forward,
+        engine.py:141): the appends are already in the cache, nothing is left
+        to do for a contiguous cache."""
+        self._cur = None
+
     def popn(self, seq_id: int, n: int):
         self.lengths[seq_id] = max(0, int(self.lengths[seq_id]) - n)
         self._sync_dev_lengths()

@@ -96,8 +96,7 @@ class Engine:
         if seq_id >= self.max_batch_size:
             raise ValueError(f"the KV cache holds {self.max_batch_size} sequences (max_batch_size)")
         self.__class__.next_seq_id += 1
-        self.paged_kv_cache.lengths[seq_id] = 0
-        self.paged_kv_cache.rollback_device()
+        self.paged_kv_cache.add_sequence(seq_id)
         return seq_id
 
     def popn(self, seq_id: int, n: int):
@@ -128,6 +127,7 @@ class Engine:
             step_mode = mode if c0 == 0 else "extend"
             logits, self.paged_kv_cache = (self.model.prefill if step_mode == "prefill" else self.model.extend)(
                 embed, self.paged_kv_cache)
+            self.paged_kv_cache.end_forward()
         return logits
 
     def prefill(self, input_tokens, sequence_id: int = 0) -> torch.Tensor:
@@ -151,6 +151,7 @@ class Engine:
             raise ValueError("decode takes one token")
         self.paged_kv_cache.begin_forward([0], [1])
         logits, self.paged_kv_cache = self.model.decode(self.model.embed(ids), self.paged_kv_cache)
+        self.paged_kv_cache.end_forward()
         return logits
 
     def decode_batch(self, input_tokens) -> torch.Tensor:

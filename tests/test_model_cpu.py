@@ -126,6 +126,15 @@ def test_kv_cache_planning_host_and_device_forms():
         c.check_decode(1)
     with pytest.raises(ValueError):
         c.begin_forward([3], [1])
+    c.add_sequence(1)
+    assert c.lengths.tolist()[1] == 0 and c.dev_lengths.tolist()[1] == 0
+    c.begin_forward([1], [3])
+    c.end_forward()
+    assert c._cur is None and c.lengths.tolist()[1] == 3
+    c.remove_sequence(1)
+    assert c.lengths.tolist()[1] == 0
+    with pytest.raises(ValueError):
+        c.add_sequence(3)
     c.clear()
     assert c.total_length() == 0 and c.dev_lengths.tolist() == [0, 0, 0]
     with pytest.raises(ValueError):
