@@ -74,6 +74,8 @@ SIGNATURES = {
                                                 _I32, _P]),
     "gptoss_moe_mlp2_peer": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _I32,
                                             _I64, _I32, _P, _P]),
+    "gptoss_dense_gemv_max_tokens": (ctypes.c_int, []),
+    "gptoss_dense_gemv": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _P]),
 }
 
 _lib = None
@@ -97,6 +99,17 @@ def load(path: str | None = None) -> ctypes.CDLL:
     if path is None:
         _lib = lib
     return lib
+
+
+_dense_max = None
+
+
+def dense_max_tokens() -> int:
+    """Token rows up to which gptoss_dense_gemv runs (cached)."""
+    global _dense_max
+    if _dense_max is None:
+        _dense_max = int(load().gptoss_dense_gemv_max_tokens())
+    return _dense_max
 
 
 def check(rc: int) -> None:

@@ -9,8 +9,10 @@ and the same result ``(x + attn, kv_cache)``.
 Kernels (libgptoss_b200.so): RMSNorm; the fused QKV split + YaRN RoPE + cache
 append; FlashAttention-style prefill / extend with the sliding-window or full
 causal mask and the sink rescale fused; split-KV decode.  The two dense
-projections (qkv 5120 x 2880, out 2880 x 4096) are plain bf16 GEMMs through
-torch (cuBLAS); they are outside the MoE/attention hot path.
+projections (qkv 5120 x 2880, out 2880 x 4096) are bf16 GEMMs through torch
+(cuBLAS); with ``DENSE_GEMV = True`` decode sizes (up to
+gptoss_dense_gemv_max_tokens() tokens) use the library's bf16 GEMV instead
+(measured on B200: the same step time as cuBLAS, so cuBLAS stays the default).
 
 The KV cache here is contiguous per sequence ([B, max_len, Hkv, D] per
 layer) instead of the reference's paged cache (PagedKVCache); the attention
@@ -159,6 +161,22 @@ class KVCache:
         return int(self.lengths.sum())
 
 
+DENSE_GEMV = False  # decode-size projections through gptoss_dense_gemv instead of cuBLAS
+
+
+def _linear(x2: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """nn.Linear with bias on [T, K] bf16: cuBLAS, or with DENSE_GEMV the
+    library GEMV for few tokens (a weight stream)."""
+    T = x2.shape[0]
+    if DENSE_GEMV and 0 < T <= _lib.dense_max_tokens():
+        x2 = x2.contiguous()
+        out = torch.empty(T, weight.shape[0], dtype=torch.bfloat16, device=x2.device)
+        _lib.call("gptoss_dense_gemv", _ptr(x2), T, _ptr(weight), _ptr(bias), weight.shape[0], weight.shape[1],
+                  _ptr(out), _stream())
+        return out
+    return F.linear(x2, weight, bias)
+
+
 class DecodeScratch:
     """Split-KV partial results of the decode kernel; one buffer can serve
     every layer of a model (the layers run one after another on one stream).
@@ -238,7 +256,7 @@ class AttentionBlock:
         S = _stream()
         t = torch.empty_like(x2)
         _lib.call("gptoss_rms_norm", _ptr(x2), _ptr(self.norm_weight), T, H, ctypes.c_float(1e-5), _ptr(t), S)
-        qkv = F.linear(t, self.qkv_weight, self.qkv_bias)
+        qkv = _linear(t, self.qkv_weight, self.qkv_bias)
         q = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=x.device)
         kc, vc = kv_cache.k[self.layer_idx], kv_cache.v[self.layer_idx]
         pos = query_positions if query_positions is not None else kv_cache.positions
@@ -263,7 +281,7 @@ class AttentionBlock:
                       nbytes, _ptr(o), None, S)
         else:
             raise ValueError(f"forward_to {forward_to} not supported")
-        out = F.linear(o.reshape(T, Hq * D), self.out_weight, self.out_bias)
+        out = _linear(o.reshape(T, Hq * D), self.out_weight, self.out_bias)
         return (x2 + out).reshape(shape), kv_cache
 
     __call__ = forward

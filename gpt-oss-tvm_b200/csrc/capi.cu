@@ -408,6 +408,17 @@ int gptoss_attn_sink_rescale(uint16_t* o, const float* lse, const uint16_t* sink
   return check_launch(launch_sink_rescale(o, lse, sinks, T, Hq, D, GPTOSS_STREAM(stream)), "sink_rescale");
 }
 
+int gptoss_dense_gemv_max_tokens(void) { return dense_gemv_max_tokens(); }
+
+int gptoss_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* weight, const uint16_t* bias, int32_t N,
+                      int32_t K, uint16_t* out, void* stream) {
+  if (T < 0 || T > dense_gemv_max_tokens() || N <= 0 || K <= 0 || K % 8 || K > 8192)
+    return fail(-1, "gptoss_dense_gemv: T must be 0..%d, K a multiple of 8 up to 8192 (T=%lld N=%d K=%d)",
+                dense_gemv_max_tokens(), (long long)T, N, K);
+  if (((uintptr_t)weight & 15)) return fail(-1, "gptoss_dense_gemv: weight must be 16-byte aligned");
+  return check_launch(launch_dense_gemv(x, T, weight, bias, N, K, out, GPTOSS_STREAM(stream)), "dense_gemv");
+}
+
 }  // extern "C"
 
 // ------------------------------------------------------------- workspace --

@@ -34,6 +34,10 @@ struct GemmLaunch {
   int out_bf16 = 0;
 };
 int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream);
+// dense.cu: y = x W^T + b for at most dense_gemv_max_tokens() token rows
+int dense_gemv_max_tokens();
+int launch_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* W, const uint16_t* bias, int32_t N, int32_t K,
+                      uint16_t* out, cudaStream_t s);
 // moe_gemv.cu: the decode-size form of the same GEMMs (f16 path, local outputs)
 bool moe_gemv_supported(const GemmLaunch& L);
 int launch_moe_gemv(int mode, const GemmLaunch& L, cudaStream_t stream);

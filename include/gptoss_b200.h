@@ -202,6 +202,15 @@ int gptoss_attn_merge(const uint16_t* o1, const float* lse1, const uint16_t* o2,
 int gptoss_attn_sink_rescale(uint16_t* o, const float* lse, const uint16_t* sinks, int64_t T, int32_t Hq, int32_t D,
                              void* stream);
 
+/* The attention block's dense projections, nn.Linear with bias
+ * (model/attention.py:85-92, :206-211, :254), for decode sizes: out [T, N] =
+ * bf16(x [T, K] . weight [N, K]^T + bias [N]), fp32 accumulation, one rounding.
+ * T up to gptoss_dense_gemv_max_tokens(); bias may be NULL; weight 16-byte
+ * aligned, K a multiple of 8 (<= 8192).  Larger T: a library GEMM. */
+int gptoss_dense_gemv_max_tokens(void);
+int gptoss_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* weight, const uint16_t* bias, int32_t N,
+                      int32_t K, uint16_t* out, void* stream);
+
 /* MLPBlock.forward like gptoss_moe_forward, but allocating nothing: no
  * cudaMalloc, no cudaFree, no workspace.  It has no counterpart in the
  * reference.  It is for callers that cannot allocate device memory when the

@@ -277,3 +277,35 @@ def test_attention_block_prefill_then_decode(oracle, layer_idx):
     torch.cuda.synchronize()
     ref1, _, _ = _block_reference(oracle, p, x1, k_all, v_all, T, blk.sliding_window)
     G.tol_check(G.f32(G.host(y1).reshape(1, 2880)) - G.f32(x1), G.f32(ref1) - G.f32(x1), what="block decode attn part")
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 4])
+@pytest.mark.parametrize("NK", [(5120, 2880), (2880, 4096)], ids=["qkv", "out"])
+def test_dense_gemv_matches_fp32_linear(T, NK):
+    """gptoss_dense_gemv (the attention projections at decode sizes) against an
+    fp32 torch nn.Linear rounded once to bf16: within the bf16 tolerance, and
+    at most 2 bf16 ulps apart (only the fp32 summation order differs)."""
+    N, K = NK
+    g = torch.Generator(device="cuda")
+    g.manual_seed(100 * T + N)
+    x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    b = (torch.randn(N, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    for bias in (b, None):
+        out = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+        G.call("gptoss_dense_gemv", G.P(x), T, G.P(w), G.P(bias), N, K, G.P(out), G.S())
+        ref = x.float() @ w.float().T + (bias.float() if bias is not None else 0.0)
+        torch.cuda.synchronize()
+        G.tol_check(out.float().cpu().numpy(), ref.to(torch.bfloat16).float().cpu().numpy(),
+                    what=f"dense gemv T={T} N={N} K={K}")
+        ulp = (ref.abs().clamp_min(1e-30).log2().floor() - 7).exp2()
+        assert torch.all((out.float() - ref).abs() <= 2 * ulp + 1e-6), "more than 2 bf16 ulps from fp32"
+
+
+def test_dense_gemv_rejects_large_batches():
+    lib = G._lib.load()
+    T = lib.gptoss_dense_gemv_max_tokens() + 1
+    x = torch.zeros(T, 64, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(8, 64, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(T, 8, dtype=torch.bfloat16, device="cuda")
+    assert lib.gptoss_dense_gemv(G.P(x), T, G.P(w), None, 8, 64, G.P(out), G.S()) != 0
