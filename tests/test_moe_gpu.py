@@ -359,3 +359,40 @@ def test_router_bit_exact_both_kernels(oracle, E):
                G.S())
         torch.cuda.synchronize()
         np.testing.assert_array_equal(G.host(logits), oracle.router(t, Wg, bg), err_msg=f"M={M} E={E}")
+
+
+def test_empty_inputs_and_oversized_calls(params_e8):
+    """Zero tokens is a valid call everywhere on the path (nothing launched,
+    return code 0, empty outputs); more tokens than a workspace holds is an
+    error with a message, not a launch."""
+    import ctypes
+    import importlib
+    mlp = importlib.import_module("gpt-oss-tvm_b200.mlp")
+    cfg = importlib.import_module("gpt-oss-tvm_b200.config").GPTOssConfig(num_experts=8)
+    blk = mlp.MLPBlock(cfg).load_state(params_e8)
+    x0 = torch.empty(1, 0, 2880, dtype=torch.bfloat16, device="cuda")
+    y0 = blk.forward(x0)
+    torch.cuda.synchronize()
+    assert tuple(y0.shape) == (1, 0, 2880) and blk.device_error() == 0
+    lib = G._lib.load()
+    z = torch.zeros(64, dtype=torch.int32, device="cuda")
+    S = G.S()
+    assert lib.gptoss_attn_prefill(G.P(z), G.P(z), G.P(z), None, 0, 0, 64, 8, 64, 0, ctypes.c_float(0.125),
+                                   G.P(z), None, S) == 0
+    assert lib.gptoss_attn_decode(G.P(z), G.P(z), G.P(z), G.P(z), 0, 16, 64, 8, 64, 0, ctypes.c_float(0.125), None,
+                                  G.P(z), 0, G.P(z), None, S) == 0
+    w = torch.zeros(8, 64, dtype=torch.bfloat16, device="cuda")
+    assert lib.gptoss_dense_gemv(G.P(z), 0, G.P(w), None, 8, 64, G.P(z), S) == 0
+    # a workspace sized for 4 tokens refuses 5
+    ws = lib.gptoss_moe_workspace_create(4, 8, 4, 2880, 2880)
+    assert ws
+    try:
+        wts = blk.c_weights()
+        x5 = torch.zeros(5, 2880, dtype=torch.bfloat16, device="cuda")
+        o5 = torch.empty_like(x5)
+        assert lib.gptoss_moe_forward(G.P(x5), 5, ctypes.byref(wts), ws, G.P(o5), S) != 0
+        assert b"max_tokens" in lib.gptoss_last_error()
+    finally:
+        lib.gptoss_moe_workspace_destroy(ws)
+        blk.free_workspace()
+    torch.cuda.synchronize()
