@@ -54,6 +54,7 @@ SIGNATURES = {
     "gptoss_moe_combine_bf16": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P]),
     "gptoss_mxfp4_dequant": (ctypes.c_int, [_P, _P, _I64, _I32, _P, _P]),
     "gptoss_moe_forward_noalloc": (ctypes.c_int, [_P, _I64, ctypes.POINTER(gptoss_moe_weights), _P, _P]),
+    "gptoss_moe_noalloc_error": (ctypes.c_uint32, []),
     "gptoss_yarn_inv_freq": (ctypes.c_int, [_I32, _F, _F, _F, _F, _I32, _P, _P]),
     "gptoss_rope_yarn": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P, _F, _P, _P]),
     "gptoss_qkv_rope_append": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _F, _P, _P, _P, _P]),
@@ -65,6 +66,8 @@ SIGNATURES = {
     "gptoss_attn_sink_rescale": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P]),
     "gptoss_moe_plan_tiles": (ctypes.c_int, [_P, _I32, _P, _P, _P]),
     "gptoss_moe_segment_copy": (ctypes.c_int, [_P, _P, _P, _I32, _I32, _I64, _I32, _P, _P]),
+    "gptoss_stream_set_flag": (ctypes.c_int, [_P, ctypes.c_uint32, _P]),
+    "gptoss_stream_wait_flag": (ctypes.c_int, [_P, ctypes.c_uint32, ctypes.c_uint32, _P, _P]),
     "gptoss_ipc_alloc": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(_P), _P]),
     "gptoss_ipc_open": (ctypes.c_int, [_P, ctypes.POINTER(_P)]),
     "gptoss_ipc_close": (ctypes.c_int, [_P]),

@@ -1,5 +1,17 @@
 """GPTOssConfig: the reference's configuration fields (model/config.py:12-77),
-used as the source of kernel launch shapes."""
+used as the source of kernel launch shapes.
+
+One deliberate difference in ``__post_init__``: the reference
+(model/config.py:56-75) pairs its ``else:`` with the outer ``if
+context_window_size == 0``, so any non-zero ``context_window_size`` it is
+given is overwritten with 40960, and a zero one with no
+``max_position_embeddings`` / ``max_sequence_length`` in the extra keys stays
+0.  Here a given non-zero value is kept (the KV caches and prefill chunks are
+sized from it, and callers pass the window they want), and only a zero one
+falls back to those keys, then to 40960.  The published checkpoints' config
+files carry ``max_position_embeddings`` and no ``context_window_size``, and
+give 131072 both ways.
+"""
 from __future__ import annotations
 
 import dataclasses

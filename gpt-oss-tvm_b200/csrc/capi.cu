@@ -1,5 +1,6 @@
 // capi.cu -- the extern "C" boundary of libgptoss_b200.so (see include/gptoss_b200.h).
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -36,13 +37,23 @@ static int check_launch(int rc, const char* what) {
   return fail(rc < 0 ? rc : -3, "%s failed (code %d, cuda: %s)", what, rc, cudaGetErrorString(e));
 }
 
+// SM count of the current device, cached per device (atomics: host threads
+// may make their first calls at the same time; they store the same value).
 static int num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+  constexpr int kMaxDev = 64;
+  static std::atomic<int> cached[kMaxDev];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+    (void)cudaGetLastError();
+    return 148;
+  }
+  int n = cached[dev].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      (void)cudaGetLastError();
+      n = 148;
+    }
+    cached[dev].store(n, std::memory_order_relaxed);
   }
   return n;
 }
@@ -200,6 +211,18 @@ int gptoss_moe_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, con
                                            local_experts, rank, dst_base, peer_rows, peer_origin, num_ranks,
                                            cap_rows, to_f16, GPTOSS_STREAM(stream)),
                       "moe_dispatch_peer");
+}
+
+int gptoss_stream_set_flag(uint32_t* flag, uint32_t value, void* stream) {
+  if (!flag || ((uintptr_t)flag & 3)) return fail(-1, "gptoss_stream_set_flag: flag must be a 4-byte aligned device word");
+  return check_launch(launch_set_flag(flag, value, GPTOSS_STREAM(stream)), "stream_set_flag");
+}
+
+int gptoss_stream_wait_flag(const uint32_t* flag, uint32_t value, uint32_t max_polls, uint32_t* err, void* stream) {
+  if (!flag || ((uintptr_t)flag & 3)) return fail(-1, "gptoss_stream_wait_flag: flag must be a 4-byte aligned device word");
+  if (max_polls == 0 || max_polls > (1u << 26))
+    return fail(-1, "gptoss_stream_wait_flag: max_polls must be 1..2^26 (got %u)", max_polls);
+  return check_launch(launch_wait_flag(flag, value, max_polls, err, GPTOSS_STREAM(stream)), "stream_wait_flag");
 }
 
 int gptoss_ipc_alloc(uint64_t bytes, void** ptr, void* handle) {

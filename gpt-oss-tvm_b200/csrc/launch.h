@@ -68,6 +68,8 @@ int launch_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, const i
                          const int32_t* indptr, int64_t rows, int32_t H, int32_t E, int32_t El, int32_t rank,
                          const int32_t* dst_base, void* const* peer_rows, int32_t* const* peer_origin,
                          int32_t num_ranks, int64_t cap_rows, int32_t to_f16, cudaStream_t s);
+int launch_set_flag(uint32_t* flag, uint32_t value, cudaStream_t s);
+int launch_wait_flag(const uint32_t* flag, uint32_t value, uint32_t max_polls, uint32_t* err, cudaStream_t s);
 
 // attention.cu
 int launch_qkv_rope(const uint16_t* qkv, const int32_t* pos, const int32_t* slot, int64_t S, int32_t Hq, int32_t Hkv,

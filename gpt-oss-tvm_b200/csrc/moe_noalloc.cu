@@ -10,11 +10,20 @@
 // library, sized for at most kNoAllocMaxTokens tokens.  Every GPU that loads
 // the library holds that array (about 6.3 MB) until the process exits.
 //
-// The array is shared by every call, and keeps what the last call left in it;
-// nothing in it has to start at zero, because every stage writes all the
-// scratch it later reads.  Calls that overlap on the GPU (two streams, or two
-// host threads) race on it.
+// The array is shared by every call, and keeps what the last call left in it.
+// Only its last 256 bytes must start at zero: the device error word that the
+// router, the permutation and both expert GEMMs set when a bounded wait runs
+// out or an expert index is out of range (static device memory starts zeroed,
+// and gptoss_moe_noalloc_error() clears the word when it reads it).  Every
+// other stage writes all the scratch it later reads before reading it.  Calls
+// that overlap on the GPU (two streams, or two host threads) race on it.
+//
+// The device address of the array is looked up once per device and cached for
+// the life of the process; it does not survive cudaDeviceReset() (the module
+// and its array are reloaded at a new address), so do not reset a device
+// between calls.
 #include <mutex>
+#include <string>
 
 #include "../../include/gptoss_b200.h"
 #include "common.cuh"
@@ -44,7 +53,8 @@ constexpr size_t kOffExp = kOffRev + up256((size_t)kRows * 4);                  
 constexpr size_t kOffAct = kOffExp + up256((size_t)kRows * 4);                                // [M*K, H] bf16
 constexpr size_t kOffY = kOffAct + up256((size_t)kRows * kNoAllocMaxHidden * 2);              // [M*K, I] bf16
 constexpr size_t kOffH2 = kOffY + up256((size_t)kRows * kNoAllocMaxInter * 2);                // [M*K, H] f32
-constexpr size_t kScratchBytes = kOffH2 + up256((size_t)kRows * kNoAllocMaxHidden * 4);
+constexpr size_t kOffErr = kOffH2 + up256((size_t)kRows * kNoAllocMaxHidden * 4);  // error word (256 B)
+constexpr size_t kScratchBytes = kOffErr + 256;
 
 static __device__ __align__(256) uint8_t g_moe_noalloc_scratch[kScratchBytes];
 
@@ -62,6 +72,30 @@ int set_last_error(int code, const char* msg);
 
 static int noalloc_fail(int code, const char* msg) { return gptoss::set_last_error(code, msg); }
 
+// Device address of the scratch array on the current device; the first call
+// on a device (with that device current) looks it up and caches it.
+static int scratch_base(const char* who, uint8_t** base) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    std::string m = std::string(who) + ": no current CUDA device";
+    return noalloc_fail(-4, m.c_str());
+  }
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
+    if (rc != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      std::string m = std::string(who) + ": cudaGetSymbolAddress of the scratch array failed";
+      return noalloc_fail(-4, m.c_str());
+    }
+    g_scratch_addr[dev] = (uint8_t*)p;
+  }
+  *base = g_scratch_addr[dev];
+  return 0;
+}
+
 extern "C" int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gptoss_moe_weights* w, uint16_t* out,
                                           void* stream) {
   if (!w) return noalloc_fail(-1, "gptoss_moe_forward_noalloc: null weights");
@@ -77,26 +111,8 @@ extern "C" int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gp
     return noalloc_fail(-1, "gptoss_moe_forward_noalloc: needs all experts on this device");
   if (M == 0) return 0;
 
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
-    cudaGetLastError();
-    return noalloc_fail(-4, "gptoss_moe_forward_noalloc: no current CUDA device");
-  }
   uint8_t* base = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    if (!g_scratch_addr[dev]) {
-      // first call on this device (this device is current): resolve the device address
-      void* p = nullptr;
-      cudaError_t rc = cudaGetSymbolAddress(&p, g_moe_noalloc_scratch);
-      if (rc != cudaSuccess || p == nullptr) {
-        cudaGetLastError();
-        return noalloc_fail(-4, "gptoss_moe_forward_noalloc: cudaGetSymbolAddress of the scratch array failed");
-      }
-      g_scratch_addr[dev] = (uint8_t*)p;
-    }
-    base = g_scratch_addr[dev];
-  }
+  if (int rc = scratch_base("gptoss_moe_forward_noalloc", &base)) return rc;
 
   uint16_t* t = (uint16_t*)(base + kOffT);
   uint16_t* logits = (uint16_t*)(base + kOffLogits);
@@ -111,23 +127,40 @@ extern "C" int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gp
   uint16_t* act = (uint16_t*)(base + kOffAct);
   uint16_t* y = (uint16_t*)(base + kOffY);
   float* h2 = (float*)(base + kOffH2);
+  uint32_t* err = (uint32_t*)(base + kOffErr);
 
   const int32_t E = w->num_experts, K = w->top_k, H = w->hidden, I = w->intermediate;
   const int32_t f16 = (w->flags & GPTOSS_MOE_F16) ? 1 : 0;
   const int64_t R = M * K;
   int rc;
   if ((rc = gptoss_rms_norm(x, w->norm_weight, M, H, w->rms_eps, t, stream))) return rc;
-  if ((rc = gptoss_moe_router(t, w->gate_weight, w->gate_bias, M, E, H, K, logits, topk_w, topk_idx, nullptr,
+  if ((rc = gptoss_moe_router(t, w->gate_weight, w->gate_bias, M, E, H, K, logits, topk_w, topk_idx, err,
                               stream)))
     return rc;
-  if ((rc = gptoss_moe_permute(topk_idx, M, K, E, indptr, tok, rev, exr, tile_ptr, tile_rows, nullptr, stream)))
+  if ((rc = gptoss_moe_permute(topk_idx, M, K, E, indptr, tok, rev, exr, tile_ptr, tile_rows, err, stream)))
     return rc;
   if ((rc = gptoss_moe_gather(t, tok, R, H, f16, act, stream))) return rc;
   if ((rc = gptoss_moe_mlp1(act, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp1_blocks, w->mlp1_scales,
-                            w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, f16, y, nullptr, stream)))
+                            w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, f16, y, err, stream)))
     return rc;
   if ((rc = gptoss_moe_mlp2(y, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp2_blocks, w->mlp2_scales, w->mlp2_bias,
-                            f16, h2, nullptr, stream)))
+                            f16, h2, err, stream)))
     return rc;
   return gptoss_moe_combine(h2, rev, topk_w, x, M, K, H, out, stream);
+}
+
+extern "C" uint32_t gptoss_moe_noalloc_error(void) {
+  uint8_t* base = nullptr;
+  if (scratch_base("gptoss_moe_noalloc_error", &base)) return 0xFFFFFFFFu;
+  // synchronous copies out of and into the array: no allocation, and they wait
+  // for the device's work that is still in flight
+  uint32_t v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(&v, base + kOffErr, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess ||
+      cudaMemset(base + kOffErr, 0, sizeof(v)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaGetLastError();
+    noalloc_fail(-4, "gptoss_moe_noalloc_error: reading the error word failed");
+    return 0xFFFFFFFFu;
+  }
+  return v;
 }

@@ -115,4 +115,40 @@ int launch_dispatch_peer(const uint16_t* t, const int32_t* token_of_row, const i
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
+// ---------------------------------------------- stream-ordered rank flags --
+// One rank publishes a step number in a 32-bit word (its own memory, or a
+// peer's through an IPC mapping) once its earlier work on the stream is
+// visible system-wide; another rank's stream waits on the device until the
+// word reaches that number.  The wait is bounded: after max_polls polls
+// (about 0.1-0.2 us each) it sets kErrTimeoutFlag in *err and returns, so a
+// rank that never arrives leaves an error bit instead of a stuck stream.
+// The comparison is wrap-safe (the word counts steps modulo 2^32).
+__global__ void set_flag_kernel(uint32_t* flag, uint32_t value) {
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(value) : "memory");
+  }
+}
+
+__global__ void wait_flag_kernel(const uint32_t* flag, uint32_t value, uint32_t max_polls, uint32_t* err) {
+  if (threadIdx.x != 0) return;
+  for (uint32_t i = 0; i < max_polls; ++i) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if ((int32_t)(v - value) >= 0) return;
+    __nanosleep(128);
+  }
+  raise_error(err, kErrTimeoutFlag);
+}
+
+int launch_set_flag(uint32_t* flag, uint32_t value, cudaStream_t s) {
+  set_flag_kernel<<<1, 32, 0, s>>>(flag, value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+int launch_wait_flag(const uint32_t* flag, uint32_t value, uint32_t max_polls, uint32_t* err, cudaStream_t s) {
+  wait_flag_kernel<<<1, 32, 0, s>>>(flag, value, max_polls, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
 }  // namespace gptoss

@@ -222,12 +222,21 @@ int gptoss_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* weight, cons
  * for M <= 64 tokens, <= 128 experts, top_k <= 4 and hidden, intermediate
  * <= 2880; larger sizes are rejected with an error.  All experts must be on
  * this device.  The first call on each device looks up the array's device
- * address (with that device current); make that first call before any
- * stream capture.  Every call shares the array: calls that overlap on the
+ * address (with that device current) and caches it for the process; make
+ * that first call before any stream capture, and do not reset the device
+ * between calls.  Every call shares the array: calls that overlap on the
  * GPU (two streams, or two host threads) race on it, and the array keeps
- * the last call's contents.  x, out: [M, H] bf16 device memory. */
+ * the last call's contents.  Device-side failures (a bounded wait that ran
+ * out, an expert index out of range) set bits in an error word at the end of
+ * the array, read with gptoss_moe_noalloc_error().  x, out: [M, H] bf16
+ * device memory. */
 int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gptoss_moe_weights* w, uint16_t* out,
                                void* stream);
+/* The device error word of gptoss_moe_forward_noalloc on the current device
+ * (the DeviceError bits of gptoss_moe_workspace_error); synchronises the
+ * device, reads the word and clears it, allocating nothing.  No counterpart
+ * in the reference.  Returns 0xFFFFFFFF when the word cannot be read. */
+uint32_t gptoss_moe_noalloc_error(void);
 
 /* --------------------------------------------- expert-parallel helpers
  * The reference runs the MoE block on one device (world_size = 1,
@@ -264,6 +273,21 @@ int gptoss_moe_combine_bf16(const uint16_t* h2, const int32_t* row_of_pair, cons
  * waits on other GPUs).  The caller orders the ranks: every writing call
  * ends with a system-scope fence, and the ranks meet at a collective before
  * the written rows are read or written again. */
+
+/* Stream-ordered flags between ranks (no counterpart in the reference).
+ * gptoss_stream_set_flag: once the stream's earlier work is done, a system-
+ * scope fence and a release store of `value` into the device word `flag`
+ * (this GPU's memory, or a peer's through gptoss_ipc_open).
+ * gptoss_stream_wait_flag: the stream waits on the device until the word
+ * reaches `value` (wrap-safe: (int32_t)(word - value) >= 0), polling at most
+ * max_polls times (1..2^26, about 0.1-0.2 us per poll); when the limit runs
+ * out it sets bit 1 << 5 (timeout of a flag wait) in the device word `err`
+ * (may be NULL) and returns, so later work on the stream still runs.  The
+ * waiting and the setting kernel must run on different GPUs (or the flag be
+ * set before the wait is launched): two launches that wait on one another
+ * are never guaranteed to run at the same time on one GPU. */
+int gptoss_stream_set_flag(uint32_t* flag, uint32_t value, void* stream);
+int gptoss_stream_wait_flag(const uint32_t* flag, uint32_t value, uint32_t max_polls, uint32_t* err, void* stream);
 
 /* cudaMalloc of `bytes` on the current device, zero-filled; its IPC handle
  * (64 bytes) in `handle`.  Free with gptoss_ipc_free. */
