@@ -775,6 +775,65 @@ def full_model_only(args):
         dist.destroy_process_group()
 
 
+def route_bench(dev, iters=10):
+    """RMSNorm + router (logits, top-4, softmax) of the gpt-oss-120b MoE block
+    (128 experts) at the configs[3] prefill size (8192 tokens: router_kernel)
+    and the configs[4] decode batch (256 tokens: router_chain_kernel); CUDA
+    events around each call, 256 MB L2 flush before each.  Inputs resident."""
+    import torch
+    lib = importlib.import_module("gpt-oss-tvm_b200._lib")
+    g = torch_gen(dev, 31)
+    E, K = NUM_EXPERTS, TOP_K
+    P = lambda a: ctypes.c_void_p(a.data_ptr())  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    gw = (torch.randn(E, HIDDEN, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    gb = (torch.randn(E, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    nw = torch.ones(HIDDEN, dtype=torch.bfloat16, device=dev)
+    out = {}
+    for M in (8192, 256):
+        x = torch.randn(M, HIDDEN, generator=g, device=dev).to(torch.bfloat16)
+        t = torch.empty_like(x)
+        logits = torch.empty(M, E, dtype=torch.bfloat16, device=dev)
+        w = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+        idx = torch.empty(M, K, dtype=torch.int32, device=dev)
+        tn, tr = [], []
+        for i in range(iters + 2):
+            flush.zero_()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            ev[0].record()
+            lib.call("gptoss_rms_norm", P(x), P(nw), M, HIDDEN, ctypes.c_float(1e-5), P(t), stream)
+            ev[1].record()
+            lib.call("gptoss_moe_router", P(t), P(gw), P(gb), M, E, HIDDEN, K, P(logits), P(w), P(idx), None, stream)
+            ev[2].record()
+            torch.cuda.synchronize()
+            if i >= 2:
+                tn.append(ev[0].elapsed_time(ev[1]))
+                tr.append(ev[1].elapsed_time(ev[2]))
+        chain_steps = M * E * HIDDEN
+        rt = statistics.median(tr)
+        out[f"{M} tokens x {E} experts"] = {
+            "rmsnorm_ms": round(statistics.median(tn), 4), "router_topk_ms": round(rt, 4),
+            "router_kernel": "router_kernel" if M > 512 else "router_chain_kernel",
+            "chain_steps_per_ns": round(chain_steps / (rt * 1e6), 2)}
+    out["note"] = "L2 flushed before every call; serial bf16 router chains (2880 dependent steps per token and expert)"
+    return out
+
+
+def kernel_case(args):
+    """--kernel-case NAME: one family of kernels alone on cuda:0, printed as
+    JSON (small, self-contained commands for ncu captures)."""
+    import torch
+    peaks, _ = measured_peaks()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    if args.kernel_case == "attention":
+        res = attention_bench(dev, peaks, iters=args.steps)
+    else:
+        res = route_bench(dev, iters=args.steps)
+    print(json.dumps({args.kernel_case: res}), flush=True)
+
+
 def cpu_baseline(args):
     """Reference CPU implementation on the host cores, on a bounded sample."""
     cb = importlib.import_module("oracle.cpu_baseline")
@@ -860,11 +919,15 @@ def main():
                     help="with --full-model-only: expert-parallel model even on one GPU (a one-rank group)")
     ap.add_argument("--no-fm-prefill", dest="fm_prefill", action="store_false",
                     help="with --full-model-only: skip the long-prompt prefill measurement")
+    ap.add_argument("--kernel-case", default=None, choices=["attention", "route"],
+                    help="run only this kernel family (attention prefill/decode, or RMSNorm + router) and print it")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     TOKENS = args.tokens
-    if args.decode_only is not None:
+    if args.kernel_case is not None:
+        kernel_case(args)
+    elif args.decode_only is not None:
         decode_only(args)
     elif args.full_model_only and args.impl != "reference":
         full_model_only(args)

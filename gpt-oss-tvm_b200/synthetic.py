@@ -70,3 +70,38 @@ def attention_inputs(seq: int, n_q: int = 64, n_kv: int = 8, head_dim: int = 64,
     v = normal_bf16(rng, (seq, n_kv, head_dim), 1.0)
     sinks = normal_bf16(rng, (n_q,), 1.0)
     return q, k, v, sinks
+
+
+def decode_inputs(lens, n_q: int = 64, n_kv: int = 8, head_dim: int = 64, seed: int = 3):
+    """One decode query per sequence: q [B, n_q, d] and, per sequence b, its
+    cached keys / values [lens[b], n_kv, d] (bf16 ~ N(0,1)); sinks [n_q]."""
+    rng = np.random.default_rng(seed)
+    q = normal_bf16(rng, (len(lens), n_q, head_dim), 1.0)
+    ks = [normal_bf16(rng, (int(L), n_kv, head_dim), 1.0) for L in lens]
+    vs = [normal_bf16(rng, (int(L), n_kv, head_dim), 1.0) for L in lens]
+    sinks = normal_bf16(rng, (n_q,), 1.0)
+    return q, ks, vs, sinks
+
+
+def merge_inputs(n: int, n_q: int = 64, head_dim: int = 64, seed: int = 4):
+    """Two partial attention states over disjoint keys: o1, o2 [n, n_q, d]
+    bf16 ~ N(0,1) and base-2 log-sum-exps lse1, lse2 [n, n_q] fp32; lse2 - lse1
+    cycles through equal values, small and large gaps of either sign."""
+    rng = np.random.default_rng(seed)
+    o1 = normal_bf16(rng, (n, n_q, head_dim), 1.0)
+    o2 = normal_bf16(rng, (n, n_q, head_dim), 1.0)
+    l1 = rng.uniform(-8.0, 24.0, size=(n, n_q)).astype(np.float32)
+    gaps = np.array([0.0, 0.5, -0.5, 3.0, -3.0, 20.0, -20.0, 1e-3], np.float32)
+    l2 = (l1 + gaps[np.arange(n * n_q).reshape(n, n_q) % len(gaps)]
+          + rng.uniform(-0.25, 0.25, size=(n, n_q)).astype(np.float32) * (np.arange(n)[:, None] % 2))
+    return o1, l1, o2, l2.astype(np.float32)
+
+
+def sink_inputs(n: int, n_q: int = 64, head_dim: int = 64, seed: int = 5):
+    """Attention output o [n, n_q, d] bf16 ~ N(0,1), base-2 lse [n, n_q] fp32
+    uniform in [-6, 26], sinks [n_q] bf16 ~ N(0,1)."""
+    rng = np.random.default_rng(seed)
+    o = normal_bf16(rng, (n, n_q, head_dim), 1.0)
+    lse = rng.uniform(-6.0, 26.0, size=(n, n_q)).astype(np.float32)
+    sinks = normal_bf16(rng, (n_q,), 1.0)
+    return o, lse, sinks

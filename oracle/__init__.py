@@ -77,6 +77,7 @@ def _declare(L):
     L.orc_attention.argtypes = [_P, _P, _P, _I, _I, _I, _I, _I, _I32, _I32, _F, _P, _P]
     L.orc_sink_rescale.argtypes = [_P, _P, _P, _I, _I, _I]
     L.orc_merge_states.argtypes = [_P, _P, _P, _P, _I, _I, _I, _P, _P]
+    L.orc_attention_decode.argtypes = [_P, _P, _P, _P, _I, _I, _I, _I, _I, _I32, _F, _P, _P]
 
 
 def _c(a: np.ndarray, dtype) -> np.ndarray:
@@ -237,6 +238,36 @@ def merge_states(o1, l1, o2, l2):
     lib().orc_merge_states(_p(o1), _p(_c(l1, np.float32)), _p(_c(o2, np.uint16)), _p(_c(l2, np.float32)),
                            T, Hq, D, _p(o), _p(lse))
     return o, lse
+
+
+def attention_decode(q, k_cache, v_cache, kv_len, window=0, sm_scale=0.125):
+    """One decode query per sequence (TVM's online-softmax decode kernel):
+    q [B, Hq, D], caches [B, max_len, Hkv, D] bf16 bits, kv_len [B] int32."""
+    q = _c(q, np.uint16)
+    kc = _c(k_cache, np.uint16)
+    vc = _c(v_cache, np.uint16)
+    lens = _c(kv_len, np.int32)
+    B, Hq, D = q.shape
+    _, max_len, Hkv, _ = kc.shape
+    o = np.empty_like(q)
+    lse = np.empty((B, Hq), np.float32)
+    lib().orc_attention_decode(_p(q), _p(kc), _p(vc), _p(lens), B, max_len, Hq, Hkv, D, int(window), sm_scale,
+                               _p(o), _p(lse))
+    return o, lse
+
+
+def decode_caches(ks, vs):
+    """Per-sequence keys / values [L_b, Hkv, D] -> contiguous caches
+    [B, max(L_b), Hkv, D] (zero padded) and kv_len [B]."""
+    B = len(ks)
+    max_len = max(1, max(len(k) for k in ks))
+    Hkv, D = ks[0].shape[1:]
+    kc = np.zeros((B, max_len, Hkv, D), np.uint16)
+    vc = np.zeros_like(kc)
+    for b, (k, v) in enumerate(zip(ks, vs)):
+        kc[b, :len(k)] = k
+        vc[b, :len(v)] = v
+    return kc, vc, np.array([len(k) for k in ks], np.int32)
 
 
 def attention_block_core(q, k, v, sinks, causal=True, window=0, sm_scale=0.125):

@@ -394,9 +394,11 @@ void orc_sink_rescale(uint16_t* o, const float* lse, const uint16_t* sinks, int6
 }
 
 /* Merge of two partial attention states (o, lse in base 2), the
- * merge_attn_output_inplace step of model/attention.py:225-233:
+ * merge_attn_output_inplace step of model/attention.py:225-233, in the
+ * arithmetic of TVM's CPU merge kernel (_merge_state_inplace_cpu in
+ * tvm/relax/frontend/nn/llm/kv_cache.py, third-party):
  *   m = max(l1, l2); w1 = exp2(l1 - m); w2 = exp2(l2 - m);
- *   o = (o1*w1 + o2*w2)/(w1 + w2); lse = m + log2(w1 + w2). */
+ *   o = o1 * (w1/(w1 + w2)) + o2 * (w2/(w1 + w2)); lse = log2(w1 + w2) + m. */
 void orc_merge_states(const uint16_t* o1, const float* l1, const uint16_t* o2, const float* l2,
                       int64_t T, int64_t Hq, int64_t D, uint16_t* o, float* lse) {
 #pragma omp parallel for schedule(static)
@@ -405,13 +407,56 @@ void orc_merge_states(const uint16_t* o1, const float* l1, const uint16_t* o2, c
       float a = l1[t * Hq + h], b = l2[t * Hq + h];
       float m = a > b ? a : b;
       float wa = exp2f(a - m), wb = exp2f(b - m);
-      float den = wa + wb;
+      float sa = wa / (wa + wb), sb = wb / (wa + wb);
       for (int64_t d = 0; d < D; ++d) {
         int64_t ix = (t * Hq + h) * D + d;
-        float v = (bf16_to_f32(o1[ix]) * wa + bf16_to_f32(o2[ix]) * wb) / den;
+        float v = (bf16_to_f32(o1[ix]) * sa) + (bf16_to_f32(o2[ix]) * sb);
         o[ix] = f32_to_bf16(v);
       }
-      lse[t * Hq + h] = m + log2f(den);
+      lse[t * Hq + h] = log2f(wa + wb) + m;
+    }
+  }
+}
+
+/* One decode query per sequence over its cached keys, in the arithmetic of
+ * TVM's CPU decode kernel (_attention_decode_cpu in kv_cache.py, the
+ * cross_attention of model/attention.py:221-224): an online softmax over
+ * the keys in order,
+ *   s = (q.k) * (sm_scale * log2 e);  m' = max(m, s);
+ *   d = d * exp2(m - m') + exp2(s - m');  o = o * exp2(m - m') + v * exp2(s - m');
+ * from m = -5e4, d = 1, o = 0; output bf16(o / d), lse = m + log2(d).
+ * Sequence b has kv_len[b] keys; a window W > 0 reads only the last W of
+ * them (the sliding-window variant, whose chunk starts at the window
+ * offset).  q [B, Hq, D]; caches [B, max_len, Hkv, D] bf16; o [B, Hq, D]. */
+void orc_attention_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* kv_len,
+                          int64_t B, int64_t max_len, int64_t Hq, int64_t Hkv, int64_t D, int32_t window,
+                          float sm_scale, uint16_t* o, float* lse) {
+  const int64_t group = Hq / Hkv;
+  const float scale = sm_scale * 1.4426950408889634f;
+#pragma omp parallel for collapse(2) schedule(dynamic, 1)
+  for (int64_t b = 0; b < B; ++b) {
+    for (int64_t h = 0; h < Hq; ++h) {
+      const int64_t hk = h / group, L = kv_len[b];
+      const int64_t j0 = (window > 0 && L > window) ? L - window : 0;
+      float* acc = (float*)calloc((size_t)D, sizeof(float));
+      float m = -5e4f, den = 1.0f;
+      for (int64_t j = j0; j < L; ++j) {
+        const uint16_t* kr = kc + ((b * max_len + j) * Hkv + hk) * D;
+        const uint16_t* vr = vc + ((b * max_len + j) * Hkv + hk) * D;
+        float sc = 0.0f;
+        for (int64_t d = 0; d < D; ++d) sc = sc + bf16_to_f32(q[(b * Hq + h) * D + d]) * bf16_to_f32(kr[d]);
+        sc = sc * scale;
+        const float mn = m > sc ? m : sc;
+        den = (den * exp2f(m - mn)) + exp2f(sc - mn);
+        const float so = exp2f(m - mn);
+        for (int64_t d = 0; d < D; ++d) acc[d] = acc[d] * so;
+        m = mn;
+        const float f = exp2f(sc - m);
+        for (int64_t d = 0; d < D; ++d) acc[d] = acc[d] + bf16_to_f32(vr[d]) * f;
+      }
+      for (int64_t d = 0; d < D; ++d) o[(b * Hq + h) * D + d] = f32_to_bf16(acc[d] / den);
+      lse[b * Hq + h] = m + log2f(den);
+      free(acc);
     }
   }
 }

@@ -98,12 +98,8 @@ class RefHarness:
         spec.loader.exec_module(mod)
         return mod
 
-    def compile(self, module, spec, tag, out_dir=None):
-        """export_tvm -> tvm.compile(target c) -> gcc (fix 2) -> Relax VM."""
+    def _fcompile(self):
         from tvm.contrib import cc as _cc
-
-        mod, params = module.export_tvm(spec=spec)
-        ex = self.tvm.compile(mod, target="c")
 
         def _fix(path):
             s = open(path).read()
@@ -119,10 +115,54 @@ class RefHarness:
             return _cc.create_shared(output, objects, options=(options or []) + ["-O2", "-ffp-contract=off"], **kw)
 
         fcompile.output_format = "so"
+        return fcompile
+
+    def compile(self, module, spec, tag, out_dir=None):
+        """export_tvm -> tvm.compile(target c) -> gcc (fix 2) -> Relax VM."""
+        mod, params = module.export_tvm(spec=spec)
+        ex = self.tvm.compile(mod, target="c")
         so = os.path.join(out_dir or self.tmpdir, tag + ".so")
-        ex.export_library(so, fcompile=fcompile)
+        ex.export_library(so, fcompile=self._fcompile())
         vm = self.relax.VirtualMachine(self.tvm.runtime.load_module(so), self.tvm.cpu())
         return vm, [n for n, _ in params]
+
+    def compile_tir(self, funcs: dict, tag: str):
+        """TIR prim_funcs {name: prim_func} -> C target -> gcc (fix 2) -> a
+        runtime module whose functions are called by name."""
+        mod = self.tvm.IRModule({n: f.with_attr("global_symbol", n) for n, f in funcs.items()})
+        ex = self.tvm.compile(mod, target="c")
+        so = os.path.join(self.tmpdir, tag + ".so")
+        ex.export_library(so, fcompile=self._fcompile())
+        return self.tvm.runtime.load_module(so)
+
+    def patched_kv_cache(self, ref_root: str):
+        """TVM's kv_cache.py (the attention kernels of the paged KV cache, from
+        the TVM build bundled with tilelang) with the reference's own fix
+        applied: the kv_cache.py section of tvm_fix.patch (the sliding-window
+        predicate of the ragged prefill kernels), patched into a temporary
+        copy with `patch -p1`.  Returns the patched module."""
+        import shutil
+        import subprocess
+
+        import tvm.relax.frontend.nn.llm as llm
+        rel = "python/tvm/relax/frontend/nn/llm/kv_cache.py"
+        root = tempfile.mkdtemp(prefix="gptoss_kvcache_")
+        os.makedirs(os.path.join(root, os.path.dirname(rel)))
+        shutil.copy(os.path.join(os.path.dirname(llm.__file__), "kv_cache.py"), os.path.join(root, rel))
+        text = open(os.path.join(ref_root, "tvm_fix.patch")).read()
+        section = [p for p in re.split(r"(?m)^(?=diff --git )", text) if p.startswith("diff --git a/" + rel)]
+        if len(section) != 1:
+            raise RuntimeError("tvm_fix.patch has no kv_cache.py section")
+        r = subprocess.run(["patch", "-p1", "-d", root], input=section[0], text=True, capture_output=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"patch failed: {r.stdout} {r.stderr}")
+        name = "tvm.relax.frontend.nn.llm._kv_cache_reference_patched"
+        spec = importlib.util.spec_from_file_location(name, os.path.join(root, rel))
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules[name] = mod
+        spec.loader.exec_module(mod)
+        self.patch_log = r.stdout.strip()
+        return mod
 
     # numpy <-> tvm (bf16 carried as uint16 bits)
     def _aligned(self, a):

@@ -140,3 +140,54 @@ def test_rope_yarn_bit_exact(oracle):
     assert _sha(q) == str(f["q_sha"]) and _sha(k) == str(f["k_sha"])
     np.testing.assert_array_equal(oracle.rope_yarn(q, f["pos"]), f["q_out"])
     np.testing.assert_array_equal(oracle.rope_yarn(k, f["pos"]), f["k_out"])
+
+
+# ------------------------------------------------------------ attention ---
+# tests/golden/attention.npz: outputs of TVM's own attention kernels (the
+# paged KV cache's CPU kernels, with the reference's tvm_fix.patch applied)
+# and of the reference's sink rescale, made by tests/golden/make_attn_golden.py.
+def _attn_fixture():
+    return golden("attention.npz")
+
+
+@pytest.mark.parametrize("tag,window", [("full", 0), ("win", 128)])
+def test_attention_prefill_bit_exact_vs_tvm(oracle, tag, window):
+    f = _attn_fixture()
+    S = synth()
+    heads = f["heads_kept"]
+    q, k, v, _ = S.attention_inputs(int(f["pf_seq"]), seed=int(f["pf_seed"]))
+    assert _sha(q, k, v) == str(f["pf_sha"]), "attention input generator drifted"
+    o, lse = oracle.attention(q, k, v, causal=True, window=window, sm_scale=float(f["sm_scale"]))
+    np.testing.assert_array_equal(o[:, heads], f[f"pf_{tag}_o"])
+    np.testing.assert_array_equal(lse.view(np.uint32), f[f"pf_{tag}_lse"].view(np.uint32))
+    q, k, v, _ = S.attention_inputs(int(f["tail_kv"]), seed=int(f["tail_seed"]))
+    assert _sha(q, k, v) == str(f["tail_sha"])
+    qo = int(f["tail_qo"])
+    o, lse = oracle.attention(q[-qo:], k, v, causal=True, window=window, sm_scale=float(f["sm_scale"]))
+    np.testing.assert_array_equal(o, f[f"tail_{tag}_o"])
+    np.testing.assert_array_equal(lse.view(np.uint32), f[f"tail_{tag}_lse"].view(np.uint32))
+
+
+@pytest.mark.parametrize("tag,window", [("full", 0), ("win", 128)])
+def test_attention_decode_bit_exact_vs_tvm(oracle, tag, window):
+    f = _attn_fixture()
+    lens = tuple(int(x) for x in f["dec_lens"])
+    q, ks, vs, _ = synth().decode_inputs(lens, seed=int(f["dec_seed"]))
+    assert _sha(q, *ks, *vs) == str(f["dec_sha"])
+    kc, vc, kl = oracle.decode_caches(ks, vs)
+    o, lse = oracle.attention_decode(q, kc, vc, kl, window=window, sm_scale=float(f["sm_scale"]))
+    np.testing.assert_array_equal(o, f[f"dec_{tag}_o"])
+    np.testing.assert_array_equal(lse.view(np.uint32), f[f"dec_{tag}_lse"].view(np.uint32))
+
+
+def test_attention_merge_and_sink_bit_exact_vs_tvm(oracle):
+    f = _attn_fixture()
+    S = synth()
+    o1, l1, o2, l2 = S.merge_inputs(int(f["merge_n"]), seed=int(f["merge_seed"]))
+    assert _sha(o1, l1, o2, l2) == str(f["merge_sha"])
+    o, lse = oracle.merge_states(o1, l1, o2, l2)
+    np.testing.assert_array_equal(o, f["merge_o"])
+    np.testing.assert_array_equal(lse.view(np.uint32), f["merge_lse"].view(np.uint32))
+    so, slse, sinks = S.sink_inputs(int(f["sink_n"]), seed=int(f["sink_seed"]))
+    assert _sha(so, slse, sinks) == str(f["sink_sha"])
+    np.testing.assert_array_equal(oracle.sink_rescale(so, slse, sinks), f["sink_o"])
