@@ -68,12 +68,14 @@ class ClockSampler:
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
 
-    def __init__(self, gpu_index: int, period_s: float = 0.02):
+    def __init__(self, gpu_index: int, period_s: float = 0.002):
         self.gpu, self.period = gpu_index, period_s
         self.samples, self.reasons, self.max_mhz = [], set(), None
         self._stop = threading.Event()
 
     def __enter__(self):
+        # re-entering accumulates: the timed regions of one line share the record
+        self._stop.clear()
         try:
             import pynvml
             pynvml.nvmlInit()
@@ -249,10 +251,11 @@ def run_b200(args):
     if world > 1:
         dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    run_e2e(args.steps)
-    e1.record()
-    torch.cuda.synchronize()
+    with sampler:
+        e0.record()
+        run_e2e(args.steps)
+        e1.record()
+        torch.cuda.synchronize()
     assert torch.equal(out_host[(args.steps - 1) % 2], od[(args.steps - 1) % 2].cpu())
     e2e_ms = e0.elapsed_time(e1)
     if world > 1:
@@ -316,12 +319,39 @@ def run_b200(args):
                                   for n in names}
         if args.cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(args)
-        print(json.dumps(line), flush=True)
+        print(json.dumps(with_headlines(line)), flush=True)
     if runner is not None:
         runner.close()
     blk.free_workspace()
     if world > 1:
         dist.destroy_process_group()
+
+
+def with_headlines(line: dict) -> dict:
+    """The same line with compact copies of the decode and attention
+    measurements placed right after `e2e` (the long per-stage records stay
+    at the end): ms, achieved GB/s or TFLOP/s and the roofline fraction."""
+    head = {}
+    for name, d in (line.get("decode") or {}).items():
+        key = "configs4_moe_decode_256tok" if "256" in name else "configs0_moe_decode_1tok"
+        head[key] = {"ms": d["ms_per_step"], "achieved_gbs": d["achieved_gbs"], "hbm_frac": d["hbm_frac"]}
+    att = {}
+    for name, d in (line.get("attention") or {}).items():
+        if not isinstance(d, dict):
+            continue
+        key = ("prefill4096_full" if "full causal" in name else "prefill4096_window128" if "window" in name
+               else "decode_b32_kv8192")
+        att[key] = {"ms": d["ms"], **({"tflops": d["tflops"], "bf16_frac": d["frac"]} if "tflops" in d
+                                      else {"achieved_gbs": d["achieved_gbs"], "hbm_frac": d["hbm_frac"]})}
+    out = {}
+    for k, v in line.items():
+        out[k] = v
+        if k == "e2e":
+            if head:
+                out["decode_headline"] = head
+            if att:
+                out["attention_headline"] = att
+    return out
 
 
 def _random_block(mlp, cfgm, E, dev, seed):
@@ -837,7 +867,7 @@ def kernel_case(args):
 def cpu_baseline(args):
     """Reference CPU implementation on the host cores, on a bounded sample."""
     cb = importlib.import_module("oracle.cpu_baseline")
-    return cb.measure(tokens=args.cpu_tokens, num_experts=NUM_EXPERTS)
+    return cb.measure(seconds=args.cpu_seconds, num_experts=NUM_EXPERTS)
 
 
 def run_reference(args):
@@ -850,46 +880,44 @@ def run_reference(args):
     rr = importlib.import_module("oracle.ref_runner")
     if rr.available(NUM_EXPERTS):
         pool = rr.RefPool(NUM_EXPERTS)
-        kind, cores = "reference", pool.procs
-        sample = (f"{pool.procs} tokens per step (1 per process) of the {NUM_EXPERTS}-expert MoE block, "
-                  f"the reference's model/mlp.py compiled by TVM (C target), one process per core")
-
-        def step():
-            return pool.step(1)
+        for _ in range(args.warmup):
+            pool.step(rr.TOKENS_PER_PROC)
+        cb = rr.measure_pool(pool, steps=args.steps)
+        pool.close()
     else:
         import oracle
         oracle.build()
         synth = importlib.import_module("gpt-oss-tvm_b200.synthetic")
         p = synth.moe_params(NUM_EXPERTS, seed=0)
         cores = len(os.sched_getaffinity(0))
-        kind, pool = "port", None
-        sample = f"{cores} tokens per step of the {NUM_EXPERTS}-expert MoE block, C restatement (OpenMP)"
-
-        def step():
-            x = synth.activations(cores, seed=1)
+        for _ in range(args.warmup):
+            oracle.moe_forward(synth.activations(cores, seed=1), p)
+        tot_t, tot_n = 0.0, 0
+        for k in range(args.steps):
+            x = synth.activations(cores, seed=2 + k)
             t0 = time.perf_counter()
             oracle.moe_forward(x, p)
-            return time.perf_counter() - t0, cores
-    for _ in range(args.warmup):
-        step()
-    tot_t, tot_n = 0.0, 0
-    for _ in range(args.steps):
-        dt, n = step()
-        tot_t += dt
-        tot_n += n
-    if pool is not None:
-        pool.close()
+            tot_t += time.perf_counter() - t0
+            tot_n += cores
+        cb = {"value": tot_n / tot_t, "unit": "tokens/s", "cores": cores, "kind": "port",
+              "extrapolated_from_tokens": tot_n, "measured_seconds": round(tot_t, 3), "measured_steps": args.steps,
+              "sample": f"{args.steps} steps of {cores} tokens of the {NUM_EXPERTS}-expert MoE block, C restatement "
+                        f"(OpenMP)"}
+    tot_t, tot_n = cb["measured_seconds"], cb["extrapolated_from_tokens"]
     value = tot_n / tot_t
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(TOKENS / value * 1e3, 1),
+        "ms_per_step_note": (f"extrapolated to the {TOKENS}-token step from {tot_n} tokens measured in "
+                             f"{tot_t:.2f} s ({args.steps} steps of {tot_n // max(args.steps, 1)} tokens)"),
+        "extrapolated_from_tokens": tot_n, "measured_seconds": round(tot_t, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "fp32 accumulate over bf16 activations and MXFP4 weights (reference CPU path)",
         "data": "synthetic (seeded; BASELINE configs[3] distributions)",
         "config": {"workload": "gpt-oss-120b MoE layer prefill (configs[3])", "tokens_per_gpu": TOKENS,
                    "num_experts": NUM_EXPERTS, "top_k": TOP_K, "hidden": HIDDEN, "intermediate": INTER,
                    "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": cores, "kind": kind, "sample": sample},
+        "cpu_baseline": {k: (round(v, 3) if k == "value" else v) for k, v in cb.items()},
         "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -902,7 +930,7 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--cpu-tokens", type=int, default=448, help="token sample of the CPU baseline (about 10 s)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="measured seconds of the CPU baseline sample")
     ap.add_argument("--tokens", type=int, default=TOKENS, help="tokens per GPU (default: the configs[3] 8192)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--no-decode", dest="decode", action="store_false", help="skip the MoE decode measurements")

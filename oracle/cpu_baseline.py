@@ -36,11 +36,11 @@ def _params(num_experts: int):
     return _PARAMS[num_experts]
 
 
-def measure(tokens: int = 32, num_experts: int = 128) -> dict:
+def measure(seconds: float = 10.0, num_experts: int = 128, tokens: int = 32) -> dict:
     ref = importlib.import_module("oracle.ref_runner")
     if ref.available(num_experts):
         try:
-            return ref.measure(tokens=tokens, num_experts=num_experts)
+            return ref.measure(seconds=seconds, num_experts=num_experts)
         except Exception:  # the TVM runtime could not start here: fall back to the C restatement
             pass
     import oracle
@@ -54,5 +54,6 @@ def measure(tokens: int = 32, num_experts: int = 128) -> dict:
     oracle.moe_forward(x, p)
     dt = time.perf_counter() - t0
     return {"value": tokens / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "extrapolated_from_tokens": tokens, "measured_seconds": round(dt, 3),
             "sample": f"{tokens} tokens of the {num_experts}-expert MoE block (full MLPBlock.forward arithmetic, "
                       f"C restatement, OpenMP over token x expert pairs)", "seconds": dt}

@@ -99,14 +99,34 @@ class RefPool:
         shutil.rmtree(self.shm, ignore_errors=True)
 
 
-def measure(tokens: int = 32, num_experts: int = 128, wseed: int = 0) -> dict:
-    procs = max(1, min(len(os.sched_getaffinity(0)), tokens))
-    pool = RefPool(num_experts, procs, wseed)
+TOKENS_PER_PROC = 2  # token rows each worker runs per step (both CPU measurements use it)
+
+
+def measure_pool(pool: "RefPool", steps: int | None = None, seconds: float | None = None,
+                 tokens_per_proc: int = TOKENS_PER_PROC) -> dict:
+    """Times `pool` the one way both CPU measurements use: steps of
+    procs x tokens_per_proc tokens (each step's time is its slowest shard),
+    either a fixed number of steps or until `seconds` have been measured.
+    Returns tokens/s over everything measured, with the sample described."""
+    tot_t, tot_n, k = 0.0, 0, 0
+    while (steps is not None and k < steps) or (steps is None and tot_t < (seconds or 10.0)):
+        dt, n = pool.step(tokens_per_proc, seed=1 + k)
+        tot_t += dt
+        tot_n += n
+        k += 1
+    return {"value": tot_n / tot_t, "unit": "tokens/s", "cores": pool.procs, "kind": "reference",
+            "extrapolated_from_tokens": tot_n, "measured_seconds": round(tot_t, 3), "measured_steps": k,
+            "sample": f"{k} steps of {pool.procs} processes x {tokens_per_proc} tokens of the {pool.num_experts}-expert "
+                      f"MoE block: the reference's model/mlp.py compiled by TVM (C target), one process per core; "
+                      f"tokens/s = tokens measured / seconds measured"}
+
+
+def measure(seconds: float = 10.0, num_experts: int = 128, wseed: int = 0) -> dict:
+    """The cpu_baseline of bench.py: about `seconds` of the reference block on
+    every host core, after one warm-up step."""
+    pool = RefPool(num_experts, None, wseed)
     try:
-        pool.step(1)  # warm-up
-        dt, n = pool.step(max(1, tokens // procs))
+        pool.step(TOKENS_PER_PROC)  # warm-up (worker start-up and first-touch of the weights)
+        return measure_pool(pool, seconds=seconds)
     finally:
         pool.close()
-    return {"value": n / dt, "unit": "tokens/s", "cores": procs, "kind": "reference",
-            "sample": f"{n} tokens of the {num_experts}-expert MoE block: the reference's model/mlp.py compiled by "
-                      f"TVM (C target), {procs} processes x {n // procs}-token shards", "seconds": dt}
