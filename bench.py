@@ -457,7 +457,8 @@ def decode_bench(dev, E, M, steps, peaks):
             "achieved_gbs": round(gbs, 1), "hbm_peak_gbs": peaks.get("hbm_gbs"),
             "hbm_frac": round(gbs / float(peaks.get("hbm_gbs", 6650.0)), 4),
             "l2": "flushed before every step (256 MB write)", "cuda_graph": True,
-            "stages_ms": stages, "stages_note": "kernels launched one by one (not graph-replayed), L2 flushed"}
+            "stages_ms": stages, "expert_path": st.get("expert_path"),
+            "stages_note": "kernels launched one by one (not graph-replayed), L2 flushed"}
 
 
 def attention_bench(dev, peaks, iters=10):

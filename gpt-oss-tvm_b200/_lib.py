@@ -49,6 +49,11 @@ SIGNATURES = {
     "gptoss_moe_gather": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P, _P]),
     "gptoss_moe_mlp1": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _F, _F, _I32, _P, _P, _P]),
     "gptoss_moe_mlp2": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P]),
+    "gptoss_moe_quantize_mx": (ctypes.c_int, [_P, _I32, _P, _I64, _I32, _P, _P, _P]),
+    "gptoss_moe_mlp1_mx": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _F, _F, _P, _P,
+                                          _P]),
+    "gptoss_moe_mlp2_mx": (ctypes.c_int, [_P, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P]),
+    "gptoss_moe_uses_block_scaled": (ctypes.c_int, [_I64, ctypes.POINTER(gptoss_moe_weights)]),
     "gptoss_moe_weights_prepare": (ctypes.c_int, [ctypes.POINTER(gptoss_moe_weights), _P]),
     "gptoss_moe_combine": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P]),
     "gptoss_moe_combine_bf16": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P]),
@@ -77,6 +82,11 @@ SIGNATURES = {
                                                 _I32, _P]),
     "gptoss_moe_mlp2_peer": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _I32,
                                             _I64, _I32, _P, _P]),
+    "gptoss_moe_weights_init_dl": (ctypes.c_int, [ctypes.POINTER(gptoss_moe_weights), _P, _P, _P, _P, _P, _P, _P, _P,
+                                                  _P, _I32, _F, _F, _I32, _P]),
+    "gptoss_moe_forward_dl": (ctypes.c_int, [_P, ctypes.POINTER(gptoss_moe_weights), _P, _P, _P]),
+    "gptoss_attn_prefill_dl": (ctypes.c_int, [_P, _P, _P, _P, _I32, _F, _P, _P, _P]),
+    "gptoss_attn_decode_dl": (ctypes.c_int, [_P, _P, _P, _P, _I32, _F, _P, _P, _P, _P, _P]),
     "gptoss_dense_gemv_max_tokens": (ctypes.c_int, []),
     "gptoss_dense_gemv": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _P]),
 }
@@ -102,6 +112,72 @@ def load(path: str | None = None) -> ctypes.CDLL:
     if path is None:
         _lib = lib
     return lib
+
+
+_capsule_ptr = ctypes.pythonapi.PyCapsule_GetPointer
+_capsule_ptr.restype = ctypes.c_void_p
+_capsule_ptr.argtypes = [ctypes.py_object, ctypes.c_char_p]
+_capsule_valid = ctypes.pythonapi.PyCapsule_IsValid
+_capsule_valid.restype = ctypes.c_int
+_capsule_valid.argtypes = [ctypes.py_object, ctypes.c_char_p]
+# DLManagedTensorVersioned: DLPackVersion (8 bytes), manager_ctx, deleter, flags, then the DLTensor
+_VERSIONED_DLTENSOR_OFFSET = 32
+
+
+class DLTensorView(ctypes.Structure):
+    """The leading fields of DLPack's DLTensor (read-only view)."""
+    _fields_ = [("data", ctypes.c_void_p), ("device_type", ctypes.c_int32), ("device_id", ctypes.c_int32),
+                ("ndim", ctypes.c_int32), ("dtype_code", ctypes.c_uint8), ("dtype_bits", ctypes.c_uint8),
+                ("dtype_lanes", ctypes.c_uint16), ("shape", ctypes.POINTER(ctypes.c_int64)),
+                ("strides", ctypes.POINTER(ctypes.c_int64)), ("byte_offset", ctypes.c_uint64)]
+
+
+class DLArg:
+    """A DLTensor* for the *_dl entry points from any DLPack producer (a torch
+    tensor, a TVM runtime Tensor, a DLPack capsule); holds the capsule (and
+    with it the producer's tensor) alive while the object lives.  None gives
+    a NULL pointer."""
+
+    def __init__(self, obj):
+        self.capsule = None
+        self.ptr = None
+        if obj is None:
+            return
+        cap = obj
+        if type(obj).__name__ != "PyCapsule":
+            try:
+                import torch
+                if isinstance(obj, torch.Tensor):
+                    cap = torch.utils.dlpack.to_dlpack(obj)
+                else:
+                    cap = obj.__dlpack__()
+            except ImportError:
+                cap = obj.__dlpack__()
+        if _capsule_valid(cap, b"dltensor"):
+            self.ptr = _capsule_ptr(cap, b"dltensor")
+        elif _capsule_valid(cap, b"dltensor_versioned"):
+            self.ptr = _capsule_ptr(cap, b"dltensor_versioned") + _VERSIONED_DLTENSOR_OFFSET
+        else:
+            raise GptossError("not a DLPack tensor (no unconsumed dltensor capsule)")
+        self.capsule = cap
+
+    @property
+    def _as_parameter_(self):
+        return ctypes.c_void_p(self.ptr)
+
+    @property
+    def view(self) -> DLTensorView:
+        return DLTensorView.from_address(self.ptr)
+
+    @property
+    def shape(self) -> tuple:
+        v = self.view
+        return tuple(v.shape[i] for i in range(v.ndim))
+
+    @property
+    def address(self) -> int:
+        v = self.view
+        return (v.data or 0) + v.byte_offset
 
 
 _dense_max = None

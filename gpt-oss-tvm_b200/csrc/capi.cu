@@ -155,6 +155,68 @@ int gptoss_moe_mlp2(const uint16_t* y, int64_t act_rows, const int32_t* indptr, 
                      act_f16, err, stream);
 }
 
+int gptoss_moe_quantize_mx(const uint16_t* src, int32_t src_f16, const int32_t* row_index, int64_t rows,
+                           int32_t K, uint8_t* q, uint8_t* scales, void* stream) {
+  if (rows < 0 || K <= 0 || K % 32 || K > 3072)
+    return fail(-1, "gptoss_moe_quantize_mx: K must be a positive multiple of 32 up to 3072 (got %d)", K);
+  if (rows && (!src || !q || !scales)) return fail(-1, "gptoss_moe_quantize_mx: null pointer");
+  if (((uintptr_t)src & 15) || ((uintptr_t)q & 15))
+    return fail(-1, "gptoss_moe_quantize_mx: src and q must be 16-byte aligned");
+  return check_launch(launch_quantize_mx(src, src_f16, row_index, rows, K, q, scales, GPTOSS_STREAM(stream)),
+                      "moe_quantize_mx");
+}
+
+static int gemm_mx_common(int mode, const uint8_t* q, const uint8_t* act_scales, int64_t act_rows,
+                          const int32_t* indptr, const int32_t* tile_ptr, const int32_t* tile_rows, int32_t E,
+                          int32_t N, int32_t K, const uint8_t* blocks, const uint8_t* scales, const uint16_t* bias,
+                          float alpha, float limit, void* out, int32_t ldo, uint32_t* err, void* stream) {
+  if (act_rows <= 0) return 0;
+  if (!moe_mx_supported(act_rows, E, N, K, blocks))
+    return fail(-1,
+                "moe gemm (block-scaled): needs decode-size tiles (rows <= 8 x experts), K a multiple of 64 in "
+                "128..3072, 32-byte aligned blocks (rows=%lld E=%d N=%d K=%d)",
+                (long long)act_rows, E, N, K);
+  if (((uintptr_t)q & 15) || ((uintptr_t)act_scales & 15) || ((uintptr_t)scales & 15))
+    return fail(-1, "moe gemm (block-scaled): q, act_scales and scales must be 16-byte aligned");
+  GemmLaunch L;
+  L.act = nullptr;
+  L.act_rows = act_rows;
+  L.blocks = blocks;
+  L.scales = scales;
+  L.bias = bias;
+  L.indptr = indptr;
+  L.tile_ptr = tile_ptr;
+  L.tile_rows = tile_rows;
+  L.out = out;
+  L.E = E;
+  L.N = N;
+  L.K = K;
+  L.ldo = ldo;
+  L.alpha = alpha;
+  L.limit = limit;
+  L.err = err;
+  L.grid = num_sms();
+  L.f16 = 1;
+  return check_launch(launch_moe_gemm_mx(mode, L, q, act_scales, GPTOSS_STREAM(stream)),
+                      mode == 0 ? "moe_mlp1_mx" : "moe_mlp2_mx");
+}
+
+int gptoss_moe_mlp1_mx(const uint8_t* q, const uint8_t* act_scales, int64_t act_rows, const int32_t* indptr,
+                       const int32_t* tile_ptr, const int32_t* tile_rows, int32_t E, int32_t H, int32_t I,
+                       const uint8_t* blocks, const uint8_t* scales, const uint16_t* bias, float alpha, float limit,
+                       uint16_t* y, uint32_t* err, void* stream) {
+  return gemm_mx_common(0, q, act_scales, act_rows, indptr, tile_ptr, tile_rows, E, 2 * I, H, blocks, scales, bias,
+                        alpha, limit, y, I, err, stream);
+}
+
+int gptoss_moe_mlp2_mx(const uint8_t* q, const uint8_t* act_scales, int64_t act_rows, const int32_t* indptr,
+                       const int32_t* tile_ptr, const int32_t* tile_rows, int32_t E, int32_t H, int32_t I,
+                       const uint8_t* blocks, const uint8_t* scales, const uint16_t* bias, float* h2, uint32_t* err,
+                       void* stream) {
+  return gemm_mx_common(1, q, act_scales, act_rows, indptr, tile_ptr, tile_rows, E, H, I, blocks, scales, bias, 0.f,
+                        0.f, h2, H, err, stream);
+}
+
 int gptoss_moe_mlp2_peer(const uint16_t* y, int64_t act_rows, const int32_t* indptr, const int32_t* tile_ptr,
                          const int32_t* tile_rows, int32_t E, int32_t H, int32_t I, const uint8_t* blocks,
                          const uint8_t* scales, const uint16_t* bias, int32_t act_f16, const int32_t* origin,
@@ -463,10 +525,65 @@ struct gptoss_moe_workspace {
   uint16_t* act;
   uint16_t* y;
   float* h2;
+  uint8_t* qs;  // [max_tokens * top_k, 192] exponents of the block-scaled GEMMs' activation terms
   uint32_t* err;
 };
 
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+namespace gptoss {
+// Decode-size expert GEMMs run on the block-scaled tensor cores unless
+// GPTOSS_MOE_MX=0 (GPTOSS_MOE_MX=1 forces them wherever they apply).
+bool moe_mx_enabled() {
+  const char* e = getenv("GPTOSS_MOE_MX");
+  if (e && e[0] == '0') return false;
+  if (e && e[0] == '1') return true;
+  return kMoeMxDefault;
+}
+}  // namespace gptoss
+
+// The expert part of the block for M routed tokens (t normalised, the
+// permutation and token tiles already planned): gather + both grouped GEMMs.
+// Decode-size tiles whose GEMMs fit the block-scaled kernel quantize the
+// activations into `act` (two e4m3 terms per value, exponents in `qs`) and
+// run moe_gemm_mx_kernel; everything else gathers f16 / bf16 rows into `act`
+// for the decode GEMV or the kind::f16 kernels.  h2 receives the fp32 expert
+// outputs; y is the SwiGLU output (f16 on the f16 and block-scaled paths).
+static bool experts_block_scaled(int64_t M, const gptoss_moe_weights* w) {
+  const int64_t R = M * w->top_k;
+  const bool gemv = (w->flags & GPTOSS_MOE_F16) && R <= 64;
+  return !gemv && moe_mx_enabled() && moe_mx_supported(R, w->num_experts, 2 * w->intermediate, w->hidden, w->mlp1_blocks) &&
+         moe_mx_supported(R, w->num_experts, w->hidden, w->intermediate, w->mlp2_blocks);
+}
+
+extern "C" int gptoss_moe_uses_block_scaled(int64_t M, const gptoss_moe_weights* w) {
+  return (w && M > 0 && experts_block_scaled(M, w)) ? 1 : 0;
+}
+
+int gptoss::moe_experts_forward(const uint16_t* t, int64_t M, const gptoss_moe_weights* w, const int32_t* indptr,
+                                const int32_t* tile_ptr, const int32_t* tile_rows, const int32_t* token_of_row,
+                                uint16_t* act, uint16_t* y, float* h2, uint8_t* qs, uint32_t* err, void* stream) {
+  const int32_t E = w->num_experts, K = w->top_k, H = w->hidden, I = w->intermediate;
+  const int32_t f16 = (w->flags & GPTOSS_MOE_F16) ? 1 : 0;
+  const int64_t R = M * K;
+  int rc;
+  if (experts_block_scaled(M, w)) {
+    uint8_t* q = (uint8_t*)act;  // R x 2K bytes: the same size as the f16 rows
+    if ((rc = gptoss_moe_quantize_mx(t, 0, token_of_row, R, H, q, qs, stream))) return rc;
+    if ((rc = gptoss_moe_mlp1_mx(q, qs, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp1_blocks, w->mlp1_scales,
+                                 w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, y, err, stream)))
+      return rc;
+    if ((rc = gptoss_moe_quantize_mx(y, 1, nullptr, R, I, q, qs, stream))) return rc;
+    return gptoss_moe_mlp2_mx(q, qs, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp2_blocks, w->mlp2_scales,
+                              w->mlp2_bias, h2, err, stream);
+  }
+  if ((rc = gptoss_moe_gather(t, token_of_row, R, H, f16, act, stream))) return rc;
+  if ((rc = gptoss_moe_mlp1(act, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp1_blocks, w->mlp1_scales, w->mlp1_bias,
+                            w->swiglu_alpha, w->swiglu_limit, f16, y, err, stream)))
+    return rc;
+  return gptoss_moe_mlp2(y, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp2_blocks, w->mlp2_scales, w->mlp2_bias, f16,
+                         h2, err, stream);
+}
 
 extern "C" {
 
@@ -498,6 +615,7 @@ gptoss_moe_workspace* gptoss_moe_workspace_create(int64_t max_tokens, int32_t nu
   off[i++] = o; o = align256(o + (size_t)R * hidden * 2);        // act
   off[i++] = o; o = align256(o + (size_t)R * intermediate * 2);  // y
   off[i++] = o; o = align256(o + (size_t)R * hidden * 4);        // h2
+  off[i++] = o; o = align256(o + (size_t)R * 192);               // qs
   off[i++] = o; o = align256(o + 256);                           // err
   ws->bytes = o;
   if (cudaMalloc(&ws->base, o) != cudaSuccess) {
@@ -521,6 +639,7 @@ gptoss_moe_workspace* gptoss_moe_workspace_create(int64_t max_tokens, int32_t nu
   ws->act = (uint16_t*)(b + off[i++]);
   ws->y = (uint16_t*)(b + off[i++]);
   ws->h2 = (float*)(b + off[i++]);
+  ws->qs = (uint8_t*)(b + off[i++]);
   ws->err = (uint32_t*)(b + off[i++]);
   cudaMemset(ws->err, 0, 256);
   return ws;
@@ -552,9 +671,7 @@ int gptoss_moe_forward(const uint16_t* x, int64_t M, const gptoss_moe_weights* w
   if (w->num_local_experts != w->num_experts || w->expert_offset != 0)
     return fail(-1, "gptoss_moe_forward: expert-parallel weights need the dispatch/combine path");
   if (M == 0) return 0;
-  const int32_t E = w->num_experts, K = w->top_k, H = w->hidden, I = w->intermediate;
-  const int32_t f16 = (w->flags & GPTOSS_MOE_F16) ? 1 : 0;
-  const int64_t R = M * K;
+  const int32_t E = w->num_experts, K = w->top_k, H = w->hidden;
   int rc;
   if ((rc = gptoss_rms_norm(x, w->norm_weight, M, H, w->rms_eps, ws->t, stream))) return rc;
   if ((rc = gptoss_moe_router(ws->t, w->gate_weight, w->gate_bias, M, E, H, K, ws->logits, ws->topk_w, ws->topk_idx,
@@ -563,13 +680,8 @@ int gptoss_moe_forward(const uint16_t* x, int64_t M, const gptoss_moe_weights* w
   if ((rc = gptoss_moe_permute(ws->topk_idx, M, K, E, ws->indptr, ws->token_of_row, ws->row_of_pair,
                                ws->expert_of_row, ws->tile_ptr, ws->tile_rows, ws->err, stream)))
     return rc;
-  if ((rc = gptoss_moe_gather(ws->t, ws->token_of_row, R, H, f16, ws->act, stream))) return rc;
-  if ((rc = gptoss_moe_mlp1(ws->act, R, ws->indptr, ws->tile_ptr, ws->tile_rows, E, H, I, w->mlp1_blocks,
-                            w->mlp1_scales, w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, f16, ws->y, ws->err,
-                            stream)))
-    return rc;
-  if ((rc = gptoss_moe_mlp2(ws->y, R, ws->indptr, ws->tile_ptr, ws->tile_rows, E, H, I, w->mlp2_blocks,
-                            w->mlp2_scales, w->mlp2_bias, f16, ws->h2, ws->err, stream)))
+  if ((rc = moe_experts_forward(ws->t, M, w, ws->indptr, ws->tile_ptr, ws->tile_rows, ws->token_of_row, ws->act,
+                                 ws->y, ws->h2, ws->qs, ws->err, stream)))
     return rc;
   return gptoss_moe_combine(ws->h2, ws->row_of_pair, ws->topk_w, x, M, K, H, out, stream);
 }

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/gptoss_b200.h"
+
 namespace gptoss {
 
 // Ranks of one expert-parallel group whose memory the peer kernels address.
@@ -41,6 +43,16 @@ int launch_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* W, const uin
 // moe_gemv.cu: the decode-size form of the same GEMMs (f16 path, local outputs)
 bool moe_gemv_supported(const GemmLaunch& L);
 int launch_moe_gemv(int mode, const GemmLaunch& L, cudaStream_t stream);
+
+// Default of the block-scaled decode GEMMs (environment GPTOSS_MOE_MX overrides).
+constexpr bool kMoeMxDefault = false;
+bool moe_mx_enabled();
+
+// moe_mx.cu: decode-size GEMMs on the block-scaled tensor cores (quantized activations)
+bool moe_mx_supported(int64_t act_rows, int32_t E, int32_t N, int32_t K, const void* blocks);
+int launch_quantize_mx(const uint16_t* src, int src_f16, const int32_t* idx, int64_t rows, int32_t K, uint8_t* q,
+                       uint8_t* sc, cudaStream_t stream);
+int launch_moe_gemm_mx(int mode, const GemmLaunch& L, const uint8_t* q, const uint8_t* act_sc, cudaStream_t stream);
 
 // moe_route.cu
 int launch_rmsnorm(const uint16_t*, const uint16_t*, int64_t, int32_t, float, uint16_t*, uint32_t*, cudaStream_t);
@@ -91,6 +103,13 @@ int launch_attn_merge(const uint16_t* o1, const float* l1, const uint16_t* o2, c
                       int32_t D, uint16_t* o, float* lse, cudaStream_t s);
 int launch_sink_rescale(uint16_t* o, const float* lse, const uint16_t* sinks, int64_t T, int32_t Hq, int32_t D,
                         cudaStream_t s);
+
+// capi.cu: the expert part of the MoE block (gather or quantize, both grouped
+// GEMMs) on the path the sizes and GPTOSS_MOE_MX select; shared by the
+// workspace and the no-allocation forwards
+int moe_experts_forward(const uint16_t* t, int64_t M, const gptoss_moe_weights* w, const int32_t* indptr,
+                        const int32_t* tile_ptr, const int32_t* tile_rows, const int32_t* token_of_row, uint16_t* act,
+                        uint16_t* y, float* h2, uint8_t* qs, uint32_t* err, void* stream);
 
 // capi.cu: records a message for gptoss_last_error()
 int set_last_error(int code, const char* msg);

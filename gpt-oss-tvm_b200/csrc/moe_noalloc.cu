@@ -27,6 +27,7 @@
 
 #include "../../include/gptoss_b200.h"
 #include "common.cuh"
+#include "launch.h"
 
 namespace {
 
@@ -53,7 +54,8 @@ constexpr size_t kOffExp = kOffRev + up256((size_t)kRows * 4);                  
 constexpr size_t kOffAct = kOffExp + up256((size_t)kRows * 4);                                // [M*K, H] bf16
 constexpr size_t kOffY = kOffAct + up256((size_t)kRows * kNoAllocMaxHidden * 2);              // [M*K, I] bf16
 constexpr size_t kOffH2 = kOffY + up256((size_t)kRows * kNoAllocMaxInter * 2);                // [M*K, H] f32
-constexpr size_t kOffErr = kOffH2 + up256((size_t)kRows * kNoAllocMaxHidden * 4);  // error word (256 B)
+constexpr size_t kOffQs = kOffH2 + up256((size_t)kRows * kNoAllocMaxHidden * 4);   // [M*K, 192] exponents
+constexpr size_t kOffErr = kOffQs + up256((size_t)kRows * 192);                      // error word (256 B)
 constexpr size_t kScratchBytes = kOffErr + 256;
 
 static __device__ __align__(256) uint8_t g_moe_noalloc_scratch[kScratchBytes];
@@ -127,11 +129,10 @@ extern "C" int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gp
   uint16_t* act = (uint16_t*)(base + kOffAct);
   uint16_t* y = (uint16_t*)(base + kOffY);
   float* h2 = (float*)(base + kOffH2);
+  uint8_t* qs = base + kOffQs;
   uint32_t* err = (uint32_t*)(base + kOffErr);
 
-  const int32_t E = w->num_experts, K = w->top_k, H = w->hidden, I = w->intermediate;
-  const int32_t f16 = (w->flags & GPTOSS_MOE_F16) ? 1 : 0;
-  const int64_t R = M * K;
+  const int32_t E = w->num_experts, K = w->top_k, H = w->hidden;
   int rc;
   if ((rc = gptoss_rms_norm(x, w->norm_weight, M, H, w->rms_eps, t, stream))) return rc;
   if ((rc = gptoss_moe_router(t, w->gate_weight, w->gate_bias, M, E, H, K, logits, topk_w, topk_idx, err,
@@ -139,12 +140,7 @@ extern "C" int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gp
     return rc;
   if ((rc = gptoss_moe_permute(topk_idx, M, K, E, indptr, tok, rev, exr, tile_ptr, tile_rows, err, stream)))
     return rc;
-  if ((rc = gptoss_moe_gather(t, tok, R, H, f16, act, stream))) return rc;
-  if ((rc = gptoss_moe_mlp1(act, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp1_blocks, w->mlp1_scales,
-                            w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, f16, y, err, stream)))
-    return rc;
-  if ((rc = gptoss_moe_mlp2(y, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp2_blocks, w->mlp2_scales, w->mlp2_bias,
-                            f16, h2, err, stream)))
+  if ((rc = gptoss::moe_experts_forward(t, M, w, indptr, tile_ptr, tile_rows, tok, act, y, h2, qs, err, stream)))
     return rc;
   return gptoss_moe_combine(h2, rev, topk_w, x, M, K, H, out, stream);
 }

@@ -213,7 +213,13 @@ def profile_moe_stages(blk: "MLPBlock", x: torch.Tensor, repeats: int = 3, flush
     out = torch.empty_like(x2)
     err = torch.zeros(4, **i32)
     S = _stream()
-    names = ["norm", "router", "permute", "gather", "mlp1", "mlp2", "combine"]
+    wts = blk.c_weights()
+    mx = bool(_lib.load().gptoss_moe_uses_block_scaled(M, ctypes.byref(wts)))
+    if mx:  # block-scaled decode GEMMs: e4m3 activation terms and their exponents
+        q = torch.empty(R, 2 * max(H, I), dtype=torch.uint8, device=dev)
+        qs = torch.empty(R, 192, dtype=torch.uint8, device=dev)
+        y = torch.empty(R, I, dtype=torch.float16, device=dev)
+    names = ["norm", "router", "permute", "gather", "mlp1", "quant2", "mlp2", "combine"]
     best = None
     for _ in range(repeats):
         if flush is not None:
@@ -228,18 +234,32 @@ def profile_moe_stages(blk: "MLPBlock", x: torch.Tensor, repeats: int = 3, flush
         _lib.call("gptoss_moe_permute", _ptr(idx), M, k, E, _ptr(indptr), _ptr(tok), _ptr(rev), _ptr(exr),
                   _ptr(tile_ptr), _ptr(tile_rows), _ptr(err), S)
         ev[3].record()
-        _lib.call("gptoss_moe_gather", _ptr(t), _ptr(tok), R, H, f16, _ptr(act), S)
-        ev[4].record()
-        _lib.call("gptoss_moe_mlp1", _ptr(act), R, _ptr(indptr), _ptr(tile_ptr), _ptr(tile_rows), E, H, I,
-                  _ptr(blk.mlp1_weight_blocks), _ptr(blk.mlp1_weight_scales), _ptr(blk.mlp1_bias),
-                  ctypes.c_float(blk.swiglu_alpha), ctypes.c_float(blk.swiglu_limit), f16, _ptr(y), _ptr(err), S)
-        ev[5].record()
-        _lib.call("gptoss_moe_mlp2", _ptr(y), R, _ptr(indptr), _ptr(tile_ptr), _ptr(tile_rows), E, H, I,
-                  _ptr(blk.mlp2_weight_blocks), _ptr(blk.mlp2_weight_scales), _ptr(blk.mlp2_bias), f16, _ptr(h2),
-                  _ptr(err), S)
-        ev[6].record()
-        _lib.call("gptoss_moe_combine", _ptr(h2), _ptr(rev), _ptr(w), _ptr(x2), M, k, H, _ptr(out), S)
+        if mx:
+            _lib.call("gptoss_moe_quantize_mx", _ptr(t), 0, _ptr(tok), R, H, _ptr(q), _ptr(qs), S)
+            ev[4].record()
+            _lib.call("gptoss_moe_mlp1_mx", _ptr(q), _ptr(qs), R, _ptr(indptr), _ptr(tile_ptr), _ptr(tile_rows), E, H,
+                      I, _ptr(blk.mlp1_weight_blocks), _ptr(blk.mlp1_weight_scales), _ptr(blk.mlp1_bias),
+                      ctypes.c_float(blk.swiglu_alpha), ctypes.c_float(blk.swiglu_limit), _ptr(y), _ptr(err), S)
+            ev[5].record()
+            _lib.call("gptoss_moe_quantize_mx", _ptr(y), 1, None, R, I, _ptr(q), _ptr(qs), S)
+            ev[6].record()
+            _lib.call("gptoss_moe_mlp2_mx", _ptr(q), _ptr(qs), R, _ptr(indptr), _ptr(tile_ptr), _ptr(tile_rows), E, H,
+                      I, _ptr(blk.mlp2_weight_blocks), _ptr(blk.mlp2_weight_scales), _ptr(blk.mlp2_bias), _ptr(h2),
+                      _ptr(err), S)
+        else:
+            _lib.call("gptoss_moe_gather", _ptr(t), _ptr(tok), R, H, f16, _ptr(act), S)
+            ev[4].record()
+            _lib.call("gptoss_moe_mlp1", _ptr(act), R, _ptr(indptr), _ptr(tile_ptr), _ptr(tile_rows), E, H, I,
+                      _ptr(blk.mlp1_weight_blocks), _ptr(blk.mlp1_weight_scales), _ptr(blk.mlp1_bias),
+                      ctypes.c_float(blk.swiglu_alpha), ctypes.c_float(blk.swiglu_limit), f16, _ptr(y), _ptr(err), S)
+            ev[5].record()
+            ev[6].record()
+            _lib.call("gptoss_moe_mlp2", _ptr(y), R, _ptr(indptr), _ptr(tile_ptr), _ptr(tile_rows), E, H, I,
+                      _ptr(blk.mlp2_weight_blocks), _ptr(blk.mlp2_weight_scales), _ptr(blk.mlp2_bias), f16, _ptr(h2),
+                      _ptr(err), S)
         ev[7].record()
+        _lib.call("gptoss_moe_combine", _ptr(h2), _ptr(rev), _ptr(w), _ptr(x2), M, k, H, _ptr(out), S)
+        ev[8].record()
         torch.cuda.synchronize()
         times = {f"{n}_ms": ev[i].elapsed_time(ev[i + 1]) for i, n in enumerate(names)}
         if best is None or times["mlp1_ms"] < best["mlp1_ms"]:
@@ -251,7 +271,9 @@ def profile_moe_stages(blk: "MLPBlock", x: torch.Tensor, repeats: int = 3, flush
     best["gemm_flops"] = best["mlp1_flops"] + best["mlp2_flops"]
     best["gemm_ms"] = best["mlp1_ms"] + best["mlp2_ms"]
     best["total_ms"] = sum(best[f"{n}_ms"] for n in names)
-    best["launches_per_step"] = 9  # norm, router, topk, count/scan, place, gather, mlp1, mlp2, combine
+    # norm, router, topk, count/scan, place, gather (or quantize), mlp1, [quantize,] mlp2, combine
+    best["launches_per_step"] = 10 if mx else 9
+    best["expert_path"] = "block-scaled (kind::mxf8f6f4)" if mx else "kind::f16 / decode GEMV"
     return best
 
 

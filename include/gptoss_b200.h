@@ -136,6 +136,33 @@ int gptoss_moe_mlp2(const uint16_t* y, int64_t act_rows, const int32_t* indptr, 
                     const uint8_t* scales, const uint16_t* bias, int32_t act_f16, float* h2, uint32_t* err,
                     void* stream);
 
+/* The same two grouped GEMMs for decode-size token tiles (rows <= 8 x E) on
+ * the block-scaled tensor cores (tcgen05.mma kind::mxf8f6f4): the MXFP4
+ * weights and their E8M0 scales feed the MMA as stored; the activations are
+ * carried as two e4m3 terms per value with E8M0 exponents per 32 values
+ * (the sum is within 2^-8 relative of the bf16/f16 value).  Same semantics
+ * as run_einsum / swiglu (model/mlp.py:238-326, :29-60, :395).
+ * gptoss_moe_quantize_mx: row r of q [rows, 2K] (K hi codes, then K lo codes)
+ * and scales [rows, 192] (hi exponents, then at byte 96 lo exponents; K/32 <= 96)
+ * from source row row_index[r] (or r) of src [*, K] (f16 if src_f16, else bf16).
+ * gptoss_moe_mlp1_mx -> y [rows, I] f16; gptoss_moe_mlp2_mx -> h2 [rows, H] fp32.
+ * blocks must be 32-byte aligned, K a multiple of 64 in 128..3072. */
+int gptoss_moe_quantize_mx(const uint16_t* src, int32_t src_f16, const int32_t* row_index, int64_t rows, int32_t K,
+                           uint8_t* q, uint8_t* scales, void* stream);
+int gptoss_moe_mlp1_mx(const uint8_t* q, const uint8_t* act_scales, int64_t act_rows, const int32_t* indptr,
+                       const int32_t* tile_ptr, const int32_t* tile_rows, int32_t E, int32_t H, int32_t I,
+                       const uint8_t* blocks, const uint8_t* scales, const uint16_t* bias, float alpha, float limit,
+                       uint16_t* y, uint32_t* err, void* stream);
+int gptoss_moe_mlp2_mx(const uint8_t* q, const uint8_t* act_scales, int64_t act_rows, const int32_t* indptr,
+                       const int32_t* tile_ptr, const int32_t* tile_rows, int32_t E, int32_t H, int32_t I,
+                       const uint8_t* blocks, const uint8_t* scales, const uint16_t* bias, float* h2, uint32_t* err,
+                       void* stream);
+
+/* 1 when gptoss_moe_forward of M tokens with these weights runs the experts
+ * on the block-scaled path above (decode-size tiles, GPTOSS_MOE_MX not 0),
+ * 0 when it runs the decode GEMV or the kind::f16 kernels. */
+int gptoss_moe_uses_block_scaled(int64_t M, const gptoss_moe_weights* w);
+
 /* run_gating + residual (model/mlp.py:328-369, :398-402):
  * out[m] = bf16(x[m] + bf16(sum_r h2[row_of_pair[m,r]] * w[m,r])). */
 int gptoss_moe_combine(const float* h2, const int32_t* row_of_pair, const uint16_t* topk_weights,

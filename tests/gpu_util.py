@@ -55,8 +55,11 @@ class MoEPieces:
     """Runs the MoE block step by step through the C ABI (device buffers
     allocated here with torch) so each stage can be compared with the oracle."""
 
-    def __init__(self, p: dict, k: int = 4, f16: bool | None = None):
-        """f16: GEMM path (None = what gptoss_moe_weights_prepare allows)."""
+    def __init__(self, p: dict, k: int = 4, f16: bool | None = None, mx: bool = False):
+        """f16: GEMM path (None = what gptoss_moe_weights_prepare allows);
+        mx: the block-scaled decode GEMMs (activations quantized into two e4m3
+        terms; y is f16 on that path)."""
+        self.mx = mx
         self.p = {kk: dev(v) for kk, v in p.items()}
         self.E = p["gate_weight"].shape[0]
         self.H = p["gate_weight"].shape[1]
@@ -106,12 +109,25 @@ class MoEPieces:
             idx.copy_(dev(routing[1]))
         call("gptoss_moe_permute", P(idx), M, k, E, P(indptr), P(tok), P(rev), P(exp_), P(tile_ptr), P(tile_rows),
              P(self.err), S())
-        call("gptoss_moe_gather", P(t), P(tok), R, H, f16, P(act), S())
-        call("gptoss_moe_mlp1", P(act), R, P(indptr), P(tile_ptr), P(tile_rows), E, H, I, P(p["mlp1_weight_blocks"]),
-             P(p["mlp1_weight_scales"]), P(p["mlp1_bias"]), ctypes.c_float(1.702), ctypes.c_float(7.0), f16, P(y),
-             P(self.err), S())
-        call("gptoss_moe_mlp2", P(y), R, P(indptr), P(tile_ptr), P(tile_rows), E, H, I, P(p["mlp2_weight_blocks"]),
-             P(p["mlp2_weight_scales"]), P(p["mlp2_bias"]), f16, P(h2), P(self.err), S())
+        if self.mx:
+            y = torch.empty(R, I, dtype=torch.float16, device="cuda")
+            q = torch.empty(R, 2 * max(H, I), dtype=torch.uint8, device="cuda")
+            qs = torch.zeros(R, 192, dtype=torch.uint8, device="cuda")
+            call("gptoss_moe_quantize_mx", P(t), 0, P(tok), R, H, P(q), P(qs), S())
+            call("gptoss_moe_mlp1_mx", P(q), P(qs), R, P(indptr), P(tile_ptr), P(tile_rows), E, H, I,
+                 P(p["mlp1_weight_blocks"]), P(p["mlp1_weight_scales"]), P(p["mlp1_bias"]), ctypes.c_float(1.702),
+                 ctypes.c_float(7.0), P(y), P(self.err), S())
+            call("gptoss_moe_quantize_mx", P(y), 1, None, R, I, P(q), P(qs), S())
+            call("gptoss_moe_mlp2_mx", P(q), P(qs), R, P(indptr), P(tile_ptr), P(tile_rows), E, H, I,
+                 P(p["mlp2_weight_blocks"]), P(p["mlp2_weight_scales"]), P(p["mlp2_bias"]), P(h2), P(self.err), S())
+        else:
+            call("gptoss_moe_gather", P(t), P(tok), R, H, f16, P(act), S())
+            call("gptoss_moe_mlp1", P(act), R, P(indptr), P(tile_ptr), P(tile_rows), E, H, I,
+                 P(p["mlp1_weight_blocks"]), P(p["mlp1_weight_scales"]), P(p["mlp1_bias"]), ctypes.c_float(1.702),
+                 ctypes.c_float(7.0), f16, P(y), P(self.err), S())
+            call("gptoss_moe_mlp2", P(y), R, P(indptr), P(tile_ptr), P(tile_rows), E, H, I,
+                 P(p["mlp2_weight_blocks"]), P(p["mlp2_weight_scales"]), P(p["mlp2_bias"]), f16, P(h2), P(self.err),
+                 S())
         call("gptoss_moe_combine", P(h2), P(rev), P(w), P(x), M, k, H, P(out), S())
         torch.cuda.synchronize()
         assert int(self.err.cpu()[0]) == 0, f"device error word {int(self.err.cpu()[0]):#x}"

@@ -46,6 +46,7 @@ def _worker(rank, world, port, E, M, exact, peer, q):
     # the latter has the peer-return epilogue, so bit-equality across the
     # placements is a property of the tensor-core kernel alone
     os.environ["GPTOSS_MOE_GEMV"] = "0"
+    os.environ["GPTOSS_MOE_MX"] = "0"
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))

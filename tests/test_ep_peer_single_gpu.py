@@ -43,6 +43,7 @@ def _worker(port, E, M, exact, q):
     # the latter has the peer-return epilogue, so bit-equality across the
     # placements is a property of the tensor-core kernel alone
     os.environ["GPTOSS_MOE_GEMV"] = "0"
+    os.environ["GPTOSS_MOE_MX"] = "0"
     dev = torch.device("cuda", 0)
     dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev, timeout=datetime.timedelta(seconds=60))
     try:

@@ -37,6 +37,7 @@ def _worker(port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["GPTOSS_MOE_GEMV"] = "0"
+    os.environ["GPTOSS_MOE_MX"] = "0"
     torch.cuda.set_device(0)
     dev = torch.device("cuda", 0)
     dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev, timeout=datetime.timedelta(seconds=60))
