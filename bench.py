@@ -702,9 +702,7 @@ def full_model_bench(dev, peaks, name, steps=20, warmup=3, batches=None, prefill
         dc.begin_forward([s], [ctx])
         model.prefill(model.embed(p), dc)
     for s in range(distinct, Bmax):
-        for layer in range(L):
-            dc.k[layer][s, :ctx].copy_(dc.k[layer][s % distinct, :ctx])
-            dc.v[layer][s, :ctx].copy_(dc.v[layer][s % distinct, :ctx])
+        dc.copy_sequence(s % distinct, s)
     torch.cuda.synchronize()
     if ep:
         # exchange buffers sized for the decode batch (the GEMMs of an

@@ -67,6 +67,9 @@ SIGNATURES = {
     "gptoss_attn_decode_scratch_bytes": (ctypes.c_int64, [_I64, _I32, _I64, _I32]),
     "gptoss_attn_decode": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I32, _I32, _I32, _I32, _F, _P, _P, _I64, _P,
                                           _P, _P]),
+    "gptoss_attn_decode_paged": (ctypes.c_int, [_P, _P, _P, _P, _I32, _P, _I64, _I32, _I32, _I32, _I32, _F, _P, _P,
+                                                _I64, _P, _P, _P]),
+    "gptoss_kv_pages_copy": (ctypes.c_int, [_P, _P, _I32, _I32, _P, _I32, _I32, _I64, _I64, _P, _P, _I32, _P]),
     "gptoss_attn_merge": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I32, _I32, _P, _P, _P]),
     "gptoss_attn_sink_rescale": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _P]),
     "gptoss_moe_plan_tiles": (ctypes.c_int, [_P, _I32, _P, _P, _P]),
@@ -87,6 +90,13 @@ SIGNATURES = {
     "gptoss_moe_forward_dl": (ctypes.c_int, [_P, ctypes.POINTER(gptoss_moe_weights), _P, _P, _P]),
     "gptoss_attn_prefill_dl": (ctypes.c_int, [_P, _P, _P, _P, _I32, _F, _P, _P, _P]),
     "gptoss_attn_decode_dl": (ctypes.c_int, [_P, _P, _P, _P, _I32, _F, _P, _P, _P, _P, _P]),
+    "gptoss_ep_unique_id": (ctypes.c_int, [_P]),
+    "gptoss_ep_init": (_P, [_P, _I32, _I32, _I64, _I32, _I32, _I32, _I32, _I32, _P]),
+    "gptoss_ep_dispatch": (ctypes.c_int, [_P, _P, _I64, ctypes.POINTER(gptoss_moe_weights), _P]),
+    "gptoss_ep_combine": (ctypes.c_int, [_P, _P, _I64, ctypes.POINTER(gptoss_moe_weights), _P, _P]),
+    "gptoss_ep_forward": (ctypes.c_int, [_P, _P, _I64, ctypes.POINTER(gptoss_moe_weights), _P, _P]),
+    "gptoss_ep_error": (ctypes.c_uint32, [_P]),
+    "gptoss_ep_destroy": (None, [_P]),
     "gptoss_dense_gemv_max_tokens": (ctypes.c_int, []),
     "gptoss_dense_gemv": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _P]),
 }

@@ -678,13 +678,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 constexpr int kDecWarps = 4;
 constexpr int kDecSplitKeys = 1024;
 
+// Cache row of key j of sequence b: contiguous caches hold it at row
+// b * max_len + j; a paged cache (table != NULL) at row
+// table[b * tstride + (j / 16) % tstride] * 16 + j % 16 of its page pool (a
+// ring of tstride pages when tstride pages do not cover the sequence).
+__device__ __forceinline__ int64_t kv_row(const int32_t* __restrict__ table, int32_t tstride, int64_t max_len, int b,
+                                          int64_t j) {
+  if (table == nullptr) return (int64_t)b * max_len + j;
+  const int64_t lp = (j >> 4) % tstride;
+  return (int64_t)__ldg(table + (int64_t)b * tstride + lp) * 16 + (j & 15);
+}
+
 __global__ void __launch_bounds__(128) attn_decode_kernel(const uint16_t* __restrict__ q,
                                                            const uint16_t* __restrict__ kc,
                                                            const uint16_t* __restrict__ vc,
                                                            const int32_t* __restrict__ kv_len, int64_t max_len,
                                                            int32_t Hq, int32_t Hkv, int32_t window, float sm_scale,
                                                            int32_t splits, float* __restrict__ part_o,
-                                                           float* __restrict__ part_ml) {
+                                                           float* __restrict__ part_ml,
+                                                           const int32_t* __restrict__ table, int32_t tstride) {
   extern __shared__ __align__(128) uint8_t dsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bg = blockIdx.x;  // b * Hkv + g
@@ -719,7 +731,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const uint16_t* __rest
       const int r = c >> 3, ch = c & 7;
       const int64_t kj = j0 + r;
       const bool ok = kj < s_hi;
-      const int64_t src = (((int64_t)b * max_len + (ok ? kj : 0)) * Hkv + gk) * kAttD + ch * 8;
+      const int64_t src = (kv_row(table, tstride, max_len, b, ok ? kj : s_lo) * Hkv + gk) * kAttD + ch * 8;
       cp_async16(smem_u32(kb) + swz(r, ch), kc + src, ok);
       cp_async16(smem_u32(vb) + swz(r, ch), vc + src, ok);
     }
@@ -992,7 +1004,8 @@ int attn_decode_splits(int64_t B, int32_t Hq, int64_t max_len, int32_t window) {
 
 int launch_attn_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* kv_len, int64_t B,
                        int64_t max_len, int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale,
-                       const uint16_t* sinks, float* scratch, uint16_t* o, float* lse, cudaStream_t s) {
+                       const uint16_t* sinks, float* scratch, uint16_t* o, float* lse, cudaStream_t s,
+                       const int32_t* table, int32_t tstride) {
   if (B <= 0) return 0;
   if (D != kAttD || Hq % Hkv || Hq / Hkv > 8) return -12;
   const int splits = attn_decode_splits(B, Hq, max_len, window);
@@ -1006,10 +1019,47 @@ int launch_attn_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc
   }
   dim3 grid((unsigned)(B * Hkv), (unsigned)splits);
   attn_decode_kernel<<<grid, 128, smem, s>>>(q, kc, vc, kv_len, max_len, Hq, Hkv, window, sm_scale, splits, part_o,
-                                             part_ml);
+                                             part_ml, table, tstride);
   const int64_t BH = B * Hq;
   attn_decode_merge_kernel<<<(unsigned)((BH * 32 + 255) / 256), 256, 0, s>>>(part_o, part_ml, BH, Hq, splits, sinks,
                                                                                o, lse);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+
+// Rows of a paged K/V cache <-> contiguous rows: row i of buf_k / buf_v
+// ([n, row_elems] bf16) is key position pos0 + i of sequence `seq`, at pool
+// row table[seq * tstride + (p / 16) % tstride] * 16 + p % 16.  to_pages: buf
+// -> pool, else pool -> buf.  One warp per row, 16-byte pieces.
+__global__ void kv_rows_copy_kernel(uint16_t* __restrict__ pool_k, uint16_t* __restrict__ pool_v,
+                                    const int32_t* __restrict__ table, int32_t tstride, int32_t seq, int64_t pos0,
+                                    int64_t n, int32_t row_elems, uint16_t* __restrict__ buf_k,
+                                    uint16_t* __restrict__ buf_v, int32_t to_pages) {
+  const int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (i >= n) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = kv_row(table, tstride, 0, seq, pos0 + i);
+  uint4* pk = (uint4*)(pool_k + row * row_elems);
+  uint4* pv = (uint4*)(pool_v + row * row_elems);
+  uint4* bk = (uint4*)(buf_k + i * row_elems);
+  uint4* bv = (uint4*)(buf_v + i * row_elems);
+  for (int c = lane; c < row_elems / 8; c += 32) {
+    if (to_pages) {
+      pk[c] = bk[c];
+      pv[c] = bv[c];
+    } else {
+      bk[c] = pk[c];
+      bv[c] = pv[c];
+    }
+  }
+}
+
+int launch_kv_rows_copy(uint16_t* pool_k, uint16_t* pool_v, const int32_t* table, int32_t tstride, int32_t seq,
+                        int64_t pos0, int64_t n, int32_t row_elems, uint16_t* buf_k, uint16_t* buf_v, int32_t to_pages,
+                        cudaStream_t s) {
+  if (n <= 0) return 0;
+  if (row_elems % 8 || !table || tstride <= 0) return -12;
+  kv_rows_copy_kernel<<<(unsigned)((n + 7) / 8), 256, 0, s>>>(pool_k, pool_v, table, tstride, seq, pos0, n, row_elems,
+                                                              buf_k, buf_v, to_pages);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 

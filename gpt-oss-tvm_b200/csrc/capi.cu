@@ -174,7 +174,7 @@ static int gemm_mx_common(int mode, const uint8_t* q, const uint8_t* act_scales,
   if (!moe_mx_supported(act_rows, E, N, K, blocks))
     return fail(-1,
                 "moe gemm (block-scaled): needs decode-size tiles (rows <= 8 x experts), K a multiple of 64 in "
-                "128..3072, 32-byte aligned blocks (rows=%lld E=%d N=%d K=%d)",
+                "256..3072, 32-byte aligned blocks (rows=%lld E=%d N=%d K=%d)",
                 (long long)act_rows, E, N, K);
   if (((uintptr_t)q & 15) || ((uintptr_t)act_scales & 15) || ((uintptr_t)scales & 15))
     return fail(-1, "moe gemm (block-scaled): q, act_scales and scales must be 16-byte aligned");
@@ -479,6 +479,35 @@ int gptoss_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_
   return check_launch(launch_attn_decode(q, k_cache, v_cache, kv_len, B, max_len, Hq, Hkv, D, window, sm_scale, sinks,
                                          scratch, o, lse, GPTOSS_STREAM(stream)),
                       "attn_decode");
+}
+
+int gptoss_attn_decode_paged(const uint16_t* q, const uint16_t* k_pages, const uint16_t* v_pages,
+                             const int32_t* page_table, int32_t table_stride, const int32_t* kv_len, int64_t B,
+                             int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale, const uint16_t* sinks,
+                             float* scratch, int64_t scratch_bytes, uint16_t* o, float* lse, void* stream) {
+  if (D != 64) return fail(-1, "gptoss_attn_decode_paged: head_dim must be 64");
+  if (B < 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || Hq / Hkv > 8 || table_stride <= 0)
+    return fail(-1, "gptoss_attn_decode_paged: bad shape (Hq/Hkv must be <= 8, table_stride > 0)");
+  if (B > 0 && !page_table) return fail(-1, "gptoss_attn_decode_paged: page_table is required");
+  const int64_t max_len = (int64_t)table_stride * 16;
+  if (scratch_bytes < gptoss_attn_decode_scratch_bytes(B, Hq, max_len, window))
+    return fail(-1, "gptoss_attn_decode_paged: scratch smaller than gptoss_attn_decode_scratch_bytes(B, Hq, "
+                    "16 * table_stride, window)");
+  return check_launch(launch_attn_decode(q, k_pages, v_pages, kv_len, B, max_len, Hq, Hkv, D, window, sm_scale, sinks,
+                                         scratch, o, lse, GPTOSS_STREAM(stream), page_table, table_stride),
+                      "attn_decode_paged");
+}
+
+int gptoss_kv_pages_copy(uint16_t* k_pages, uint16_t* v_pages, int32_t Hkv, int32_t D, const int32_t* page_table,
+                         int32_t table_stride, int32_t seq, int64_t pos0, int64_t n, uint16_t* k_rows,
+                         uint16_t* v_rows, int32_t to_pages, void* stream) {
+  if (n < 0 || pos0 < 0 || seq < 0 || Hkv <= 0 || D <= 0 || (Hkv * D) % 8 || table_stride <= 0)
+    return fail(-1, "gptoss_kv_pages_copy: bad arguments");
+  if (n > 0 && (!page_table || !k_pages || !v_pages || !k_rows || !v_rows))
+    return fail(-1, "gptoss_kv_pages_copy: null pointer");
+  return check_launch(launch_kv_rows_copy(k_pages, v_pages, page_table, table_stride, seq, pos0, n, Hkv * D, k_rows,
+                                          v_rows, to_pages, GPTOSS_STREAM(stream)),
+                      "kv_pages_copy");
 }
 
 int gptoss_attn_merge(const uint16_t* o1, const float* lse1, const uint16_t* o2, const float* lse2, int64_t T,

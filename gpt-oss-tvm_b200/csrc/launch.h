@@ -98,7 +98,11 @@ size_t attn_decode_scratch_bytes(int64_t B, int32_t Hq, int64_t max_len, int32_t
 int attn_decode_splits(int64_t B, int32_t Hq, int64_t max_len, int32_t window);
 int launch_attn_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc, const int32_t* kv_len, int64_t B,
                        int64_t max_len, int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale,
-                       const uint16_t* sinks, float* scratch, uint16_t* o, float* lse, cudaStream_t s);
+                       const uint16_t* sinks, float* scratch, uint16_t* o, float* lse, cudaStream_t s,
+                       const int32_t* table = nullptr, int32_t tstride = 0);
+int launch_kv_rows_copy(uint16_t* pool_k, uint16_t* pool_v, const int32_t* table, int32_t tstride, int32_t seq,
+                        int64_t pos0, int64_t n, int32_t row_elems, uint16_t* buf_k, uint16_t* buf_v, int32_t to_pages,
+                        cudaStream_t s);
 int launch_attn_merge(const uint16_t* o1, const float* l1, const uint16_t* o2, const float* l2, int64_t T, int32_t Hq,
                       int32_t D, uint16_t* o, float* lse, cudaStream_t s);
 int launch_sink_rescale(uint16_t* o, const float* lse, const uint16_t* sinks, int64_t T, int32_t Hq, int32_t D,

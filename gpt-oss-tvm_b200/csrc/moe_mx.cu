@@ -26,16 +26,17 @@
 //     differs from x by at most 2^-8 of |x| (one extra bf16-sized rounding of
 //     each activation), well inside the bf16 tolerance of the block, while the
 //     weights stay exact.
-// No warp decodes a weight: the roles are a weight TMA producer, a
-// scale-factor builder (which also expands the 64-code row tails), an
-// activation TMA producer, the MMA issuer (owns TMEM) and four epilogue warps.
+// No warp decodes a weight: the roles are a weight TMA producer, two
+// scale-factor builders (which also expand the 64-code row tails), an
+// activation TMA producer, two MMA issuers (one owns TMEM) and four epilogue
+// warps.
 #include "common.cuh"
 #include "launch.h"
 #include "moe_tile.cuh"
 
 namespace gptoss {
 
-constexpr int kMxThreads = 256;                  // 8 warps
+constexpr int kMxThreads = 320;                  // 10 warps
 constexpr int kMxBK = 128;                       // K codes per stage (one 128-byte smem row)
 constexpr int kMxStages = 6;
 constexpr int kMxMaxN = kMoeTileRowsSmall;       // token rows per tile (32)
@@ -44,12 +45,19 @@ constexpr int kMxActBytes = kMxMaxN * kMxBK;     // 4 KB: one activation term of
 constexpr int kMxSfBytes = 512;                  // one scale-factor chunk: 128 rows x 4 K-blocks
 constexpr int kMxMaxGroups = 96;                 // K / 32 <= 96 (K <= 3072)
 constexpr int kMxScRow = 2 * kMxMaxGroups;       // bytes per row of the activation scales: hi, then lo
-constexpr int kMxWarpW = 0, kMxWarpSf = 1, kMxWarpAct = 2, kMxWarpMma = 3, kMxWarpEpi0 = 4;
-// TMEM columns: two 32-column accumulators, then per pipeline stage its three
-// scale-factor chunks (4 columns each), so that copying the chunks of stage
-// s + 1 never writes columns the MMAs of stage s still read
+// Two scale-factor builders and two MMA issuers, each taking the stages of one
+// parity (stage counter & 1): a single thread issuing 3 tcgen05.cp and 8
+// tcgen05.mma per 128-code stage was the pace (measured: ~600 cycles of issue
+// per stage, above the ~370 cycles the weights take to stream at HBM rate).
+constexpr int kMxWarpW = 0, kMxWarpSf = 1, kMxWarpAct = 2, kMxWarpMma = 3, kMxWarpEpi0 = 4, kMxWarpSf1 = 8,
+              kMxWarpMma1 = 9;
+// TMEM columns: two accumulator buffers (tile i / i + 1), each a pair of
+// 32-column accumulators (even / odd stages: one per MMA issuer, summed by the
+// epilogue), then per pipeline stage its three scale-factor chunks (4 columns
+// each), so that copying the chunks of one stage never writes columns the MMAs
+// of another stage still read
 constexpr int kMxAccCols = 32;
-constexpr int kMxSfCol0 = 2 * kMxAccCols, kMxSfStageCols = 12;
+constexpr int kMxSfCol0 = 4 * kMxAccCols, kMxSfStageCols = 12;
 constexpr int kMxTmemCols = 256;
 static_assert(kMxSfCol0 + kMxStages * kMxSfStageCols <= kMxTmemCols, "TMEM budget");
 
@@ -239,11 +247,11 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&scfull_bar[s], 1);
-      mbar_init(&scempty_bar[s], 1);
-      mbar_init(&accfull_bar[s], 1);
+      mbar_init(&scempty_bar[s], 2);   // both scale-factor builders
+      mbar_init(&accfull_bar[s], 2);   // both MMA issuers
       mbar_init(&accempty_bar[s], 4);
     }
-    mbar_init(drain_bar, 1);
+    mbar_init(drain_bar, 2);  // both MMA issuers commit once at the end
     *abort_s = 0;
     fence_mbar_init();
   }
@@ -324,8 +332,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         if (!ok) { *abort_s = 1; break; }
       }
     }
-  } else if (warp == kMxWarpSf) {
-    // ----------------- scale-factor chunks of every stage, and the 64-code tails
+  } else if (warp == kMxWarpSf || warp == kMxWarpSf1) {
+    // ------ scale-factor chunks of the stages of this warp's parity, and the 64-code tails
+    const uint32_t par = warp == kMxWarpSf ? 0u : 1u;
     uint32_t it = 0, tl = 0;
     for (int32_t t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       TileInfo ti;
@@ -338,6 +347,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       const uint8_t* sca = smem + kMxOffScA + sb * kMxMaxN * kMxScRow;   // [32][192]
       const int32_t frows = min(kBM, p.N - ti.f0);
       for (int32_t j = 0; j < nst && ok; ++j, ++it) {
+        if ((it & 1u) != par) continue;
         const uint32_t s = it % kMxStages, ph = (it / kMxStages) & 1;
         ok = mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty);
         if (!ok) break;
@@ -400,8 +410,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       if (lane == 0) mbar_arrive(&scempty_bar[sb]);
       if (!ok) { *abort_s = 1; break; }
     }
-  } else if (warp == kMxWarpMma) {
-    // ------------------------------------------------------- MMA issuer
+  } else if (warp == kMxWarpMma || warp == kMxWarpMma1) {
+    // ---------------------------- MMA issuer of the stages of this warp's parity
+    const uint32_t par = warp == kMxWarpMma ? 0u : 1u;
     if (elect_one()) {
       uint32_t it = 0, tl = 0;
       bool ok = true;
@@ -415,8 +426,10 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         const uint32_t ab = tl & 1, aph = (tl >> 1) & 1;
         if (!mbar_wait(&accempty_bar[ab], aph ^ 1, p.err, kErrTimeoutAccum)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + ab * kMxAccCols;
+        const uint32_t d_tmem = tmem_base + (2 * ab + par) * kMxAccCols;
+        bool first = true;  // this issuer's first stage of the tile starts its accumulator
         for (int32_t j = 0; j < nst; ++j, ++it) {
+          if ((it & 1u) != par) continue;
           const uint32_t s = it % kMxStages, ph = (it / kMxStages) & 1;
           if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) { ok = false; break; }
           tc_fence_after();
@@ -433,10 +446,11 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             const uint64_t ldesc = ldesc0 + (uint64_t)((uint32_t)(s * kMxActBytes + kb * 32) >> 4);
             const uint32_t idesc = make_idesc_mx(n_mma, (uint32_t)kb);
             const uint32_t byte = (uint32_t)kb << 30;
-            tc_mma_mx(d_tmem, adesc, hdesc, idesc, sfa | byte, sfbh | byte, (j > 0 || kb > 0) ? 1u : 0u);
+            tc_mma_mx(d_tmem, adesc, hdesc, idesc, sfa | byte, sfbh | byte, (!first || kb > 0) ? 1u : 0u);
             tc_mma_mx(d_tmem, adesc, ldesc, idesc, sfa | byte, sfbl | byte, 1u);
           }
           tc_commit(&empty_bar[s]);
+          first = false;
         }
         if (!ok) break;
         tc_commit(&accfull_bar[ab]);
@@ -464,9 +478,12 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       if (!mbar_wait(&accfull_bar[ab], aph, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
       __syncwarp();
       tc_fence_after();
-      uint32_t v[32];
-      tmem_ld_x32(tmem_base + lane_base + ab * kMxAccCols, v);
+      uint32_t v[32], v1[32];
+      tmem_ld_x32(tmem_base + lane_base + (2 * ab) * kMxAccCols, v);
+      tmem_ld_x32(tmem_base + lane_base + (2 * ab + 1) * kMxAccCols, v1);
       tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) + __uint_as_float(v1[i]));
       epilogue_block<kMode, true>(p, ti, v, 0, q, lane, bias, row_ok, frow, (uint16_t*)(smem + kMxOffEpi) + q * 1024);
       tc_fence_before();
       __syncwarp();
@@ -529,7 +546,7 @@ static int mx_tmap(CUtensorMap* map, const void* base, CUtensorMapDataType dtype
 bool moe_mx_supported(int64_t act_rows, int32_t E, int32_t N, int32_t K, const void* blocks) {
   const int32_t G = K / 32;
   const int32_t last = N % kBM ? N % kBM : kBM;
-  return act_rows > 0 && moe_tile_rows_max(act_rows, E) <= kMxMaxN && K >= kMxBK && K % 64 == 0 &&
+  return act_rows > 0 && moe_tile_rows_max(act_rows, E) <= kMxMaxN && K >= 2 * kMxBK && K % 64 == 0 &&
          G <= kMxMaxGroups && ((uintptr_t)blocks & 31) == 0 && ((int64_t)kBM * G) % 16 == 0 &&
          ((int64_t)last * G) % 16 == 0 && ((int64_t)N * G) % 16 == 0;
 }

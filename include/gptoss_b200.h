@@ -146,7 +146,7 @@ int gptoss_moe_mlp2(const uint16_t* y, int64_t act_rows, const int32_t* indptr, 
  * and scales [rows, 192] (hi exponents, then at byte 96 lo exponents; K/32 <= 96)
  * from source row row_index[r] (or r) of src [*, K] (f16 if src_f16, else bf16).
  * gptoss_moe_mlp1_mx -> y [rows, I] f16; gptoss_moe_mlp2_mx -> h2 [rows, H] fp32.
- * blocks must be 32-byte aligned, K a multiple of 64 in 128..3072. */
+ * blocks must be 32-byte aligned, K a multiple of 64 in 256..3072. */
 int gptoss_moe_quantize_mx(const uint16_t* src, int32_t src_f16, const int32_t* row_index, int64_t rows, int32_t K,
                            uint8_t* q, uint8_t* scales, void* stream);
 int gptoss_moe_mlp1_mx(const uint8_t* q, const uint8_t* act_scales, int64_t act_rows, const int32_t* indptr,
@@ -218,6 +218,29 @@ int gptoss_attn_decode(const uint16_t* q, const uint16_t* k_cache, const uint16_
                        int64_t B, int64_t max_len, int32_t Hq, int32_t Hkv, int32_t D, int32_t window,
                        float sm_scale, const uint16_t* sinks, float* scratch, int64_t scratch_bytes, uint16_t* o,
                        float* lse, void* stream);
+
+/* The paged KV cache (the reference's PagedKVCache with page size 16,
+ * engine.py:93-104; page windowing tvm_fix.patch:194-281).  A layer's keys
+ * and values live in page pools k_pages / v_pages [num_pages * 16, Hkv, D]
+ * bf16; key position j of sequence b is row
+ *   page_table[b * table_stride + (j / 16) % table_stride] * 16 + j % 16.
+ * Full-attention layers give each sequence table_stride >= ceil(len / 16)
+ * pages; sliding-window layers may give it a ring of table_stride pages
+ * (>= ceil(window / 16) + 1) that holds the last keys only.
+ * gptoss_attn_decode_paged: gptoss_attn_decode over such a cache (kv_len[b]
+ * keys, window as there); scratch as gptoss_attn_decode_scratch_bytes(B, Hq,
+ * 16 * table_stride, window). */
+int gptoss_attn_decode_paged(const uint16_t* q, const uint16_t* k_pages, const uint16_t* v_pages,
+                             const int32_t* page_table, int32_t table_stride, const int32_t* kv_len, int64_t B,
+                             int32_t Hq, int32_t Hkv, int32_t D, int32_t window, float sm_scale, const uint16_t* sinks,
+                             float* scratch, int64_t scratch_bytes, uint16_t* o, float* lse, void* stream);
+/* Rows of positions pos0 .. pos0 + n - 1 of sequence `seq` between the page
+ * pools and contiguous rows k_rows / v_rows [n, Hkv, D]: to_pages != 0 writes
+ * the pages (append_mha_kv of a prefill chunk), else reads them (the cached
+ * keys an extend attends to). */
+int gptoss_kv_pages_copy(uint16_t* k_pages, uint16_t* v_pages, int32_t Hkv, int32_t D, const int32_t* page_table,
+                         int32_t table_stride, int32_t seq, int64_t pos0, int64_t n, uint16_t* k_rows,
+                         uint16_t* v_rows, int32_t to_pages, void* stream);
 
 /* merge_attn_output_inplace (model/attention.py:231-233): two partial
  * attention states over disjoint keys -> one (o bf16 [T, Hq, D], lse). */
@@ -361,6 +384,42 @@ int gptoss_moe_mlp2_peer(const uint16_t* y, int64_t act_rows, const int32_t* ind
                          const uint8_t* scales, const uint16_t* bias, int32_t act_f16, const int32_t* origin,
                          void* const* peer_back, int32_t num_ranks, int64_t back_rows, int32_t back_bf16,
                          uint32_t* err, void* stream);
+
+/* ------------------------------- expert parallelism at the C boundary
+ * No counterpart in the reference (it runs the block on one device).  The
+ * experts of an MLPBlock are sharded over `world` ranks of one node, one
+ * process per GPU: rank r owns experts [r E / world, (r + 1) E / world) and
+ * routes its own tokens.  NCCL (libnccl.so.2, loaded at run time) carries the
+ * per-expert row counts and two one-word orderings per step; the token rows
+ * and expert outputs move by plain stores into the other ranks' CUDA IPC
+ * buffers (NVLink; no multicast, no device-side waits on other GPUs).  Every
+ * rank makes the same calls in the same order on its stream. */
+typedef struct gptoss_ep gptoss_ep;
+/* A new group's NCCL unique id (128 bytes); rank 0 creates it and sends it to
+ * the other ranks over any host channel. */
+int gptoss_ep_unique_id(void* id);
+/* Joins the group (collective): NCCL communicator, this rank's scratch and
+ * IPC buffers for max_tokens tokens per rank, the other ranks' buffers
+ * mapped.  exact_return: expert outputs travel back in fp32 (the block is
+ * then bit-equal to one GPU's) instead of bf16 (half the bytes).  NULL on
+ * failure (gptoss_last_error()). */
+gptoss_ep* gptoss_ep_init(const void* id, int32_t rank, int32_t world, int64_t max_tokens, int32_t num_experts,
+                          int32_t top_k, int32_t hidden, int32_t intermediate, int32_t exact_return, void* stream);
+/* Dispatch: RMSNorm, router, top-k and permutation of this rank's tokens x
+ * [M, H]; rows stored into the owners' activation matrices.  w: this rank's
+ * shard (num_local_experts = E / world, expert_offset = rank E / world). */
+int gptoss_ep_dispatch(gptoss_ep* ep, const uint16_t* x, int64_t M, const gptoss_moe_weights* w, void* stream);
+/* Combine: the grouped GEMMs on this rank's experts, outputs returned to the
+ * tokens' ranks, out [M, H] = x + weighted sum of each token's experts. */
+int gptoss_ep_combine(gptoss_ep* ep, const uint16_t* x, int64_t M, const gptoss_moe_weights* w, uint16_t* out,
+                      void* stream);
+/* gptoss_ep_dispatch then gptoss_ep_combine: MLPBlock.forward (model/mlp.py:371-402). */
+int gptoss_ep_forward(gptoss_ep* ep, const uint16_t* x, int64_t M, const gptoss_moe_weights* w, uint16_t* out,
+                      void* stream);
+/* The group's device error word (bounded-wait expiry, bad routing); synchronises and clears it. */
+uint32_t gptoss_ep_error(gptoss_ep* ep);
+/* Leaves the group (after every rank's last step has completed). */
+void gptoss_ep_destroy(gptoss_ep* ep);
 
 #ifdef __cplusplus
 }

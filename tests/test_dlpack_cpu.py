@@ -35,7 +35,8 @@ def test_dlarg_reads_tvm_tensors():
     pytest.importorskip("tilelang")
     import tvm
     x = np.arange(12, dtype=np.int32).reshape(3, 4)
-    t = tvm.runtime.from_dlpack(torch.from_numpy(x))
+    # torch's CPU allocator aligns to 64 bytes, as TVM's from_dlpack requires; numpy's may not
+    t = tvm.runtime.from_dlpack(torch.arange(12, dtype=torch.int32).reshape(3, 4))
     a = L.DLArg(t)
     assert a.shape == (3, 4) and a.view.dtype_code == 0 and a.view.dtype_bits == 32
     got = np.ctypeslib.as_array(ctypes.cast(ctypes.c_void_p(a.address), ctypes.POINTER(ctypes.c_int32)), (12,))

@@ -94,19 +94,28 @@ def test_random_init_distributions():
 
 
 def test_kv_cache_planning_host_and_device_forms():
+    """Paged planning: full-attention layers take pages (16 tokens) from a free
+    list as sequences grow; sliding-window layers use a fixed ring of 9 pages
+    per sequence; the decode step computes the same rows on the device."""
     _, cfgm, _, _, att = mods()
     cfg = small_config(cfgm)
-    c = att.KVCache(cfg, max_batch=3, max_len=16, num_layers=2, device="cpu")
+    c = att.KVCache(cfg, max_batch=3, max_len=32, num_layers=2, device="cpu")
+    assert c.windowed == [True, False] and c.pages_per_seq == 2 and c.window_pages == 9
+    assert c.k[0].shape[0] == 3 * 9 * 16 and c.k[1].shape[0] == 3 * 2 * 16
     pos = c.begin_forward([1], [5])
     assert pos.tolist() == [0, 1, 2, 3, 4]
-    assert c.slots.tolist() == [16, 17, 18, 19, 20]
+    assert c.slots.tolist() == [0, 1, 2, 3, 4]                      # sequence 1, first free page: 0
+    assert c.slots_win.tolist() == [144, 145, 146, 147, 148]         # ring of sequence 1: pages 9..17
     c.begin_forward([0, 2], [2, 1])
-    assert c.positions.tolist() == [0, 1, 0] and c.slots.tolist() == [0, 1, 32]
+    assert c.positions.tolist() == [0, 1, 0] and c.slots.tolist() == [16, 17, 32]
+    assert c.slots_win.tolist() == [0, 1, 288]
     assert c.lengths.tolist() == [2, 5, 1] and c.dev_lengths.tolist() == [2, 5, 1]
+    assert c.table_full.tolist()[:3] == [[1, 0], [0, 0], [2, 0]]
     # device-side decode step of sequences 0..2
     c.check_decode(3)
     p = c.begin_decode_on_device(3)
-    assert p.tolist() == [2, 5, 1] and c.slots.tolist() == [2, 21, 33] and c.kv_len.tolist() == [3, 6, 2]
+    assert p.tolist() == [2, 5, 1] and c.slots.tolist() == [18, 5, 33] and c.kv_len.tolist() == [3, 6, 2]
+    assert c.slots_win.tolist() == [2, 149, 289]
     assert c.lengths.tolist() == [2, 5, 1]  # host mirror moves on commit only
     c.commit_decode(3)
     assert c.lengths.tolist() == [3, 6, 2] and c.dev_lengths.tolist() == [3, 6, 2]
@@ -114,20 +123,25 @@ def test_kv_cache_planning_host_and_device_forms():
     c.begin_decode_on_device(2)
     c.rollback_device()
     assert c.dev_lengths.tolist() == [3, 6, 2]
-    c.popn(1, 4)
-    assert c.lengths.tolist() == [3, 2, 2] and c.dev_lengths.tolist() == [3, 2, 2]
-    assert c.total_length() == 7
+    # growing past a page boundary takes a new page (the next free one: 3)
+    c.begin_forward([1], [12])
+    assert c.table_full.tolist()[1] == [0, 3] and c.slots.tolist()[-2:] == [48, 49]
+    assert c.slots_win.tolist()[-2:] == [160, 161]                  # ring page 1 of sequence 1
+    c.popn(1, 4)                                                    # 18 -> 14 tokens: page 3 goes back
+    assert c.lengths.tolist() == [3, 14, 2] and c.dev_lengths.tolist() == [3, 14, 2]
+    assert c._pages[1] == [0] and c._free[-1] == 3
+    assert c.total_length() == 19
     with pytest.raises(ValueError):
-        c.begin_forward([0], [14])
+        c.begin_forward([0], [30])
     with pytest.raises(ValueError):
         c.check_decode(4)
-    c.begin_forward([0], [13])
+    c.begin_forward([0], [29])
     with pytest.raises(ValueError):
         c.check_decode(1)
     with pytest.raises(ValueError):
         c.begin_forward([3], [1])
     c.add_sequence(1)
-    assert c.lengths.tolist()[1] == 0 and c.dev_lengths.tolist()[1] == 0
+    assert c.lengths.tolist()[1] == 0 and c.dev_lengths.tolist()[1] == 0 and c._pages[1] == []
     c.begin_forward([1], [3])
     c.end_forward()
     assert c._cur is None and c.lengths.tolist()[1] == 3
@@ -137,8 +151,35 @@ def test_kv_cache_planning_host_and_device_forms():
         c.add_sequence(3)
     c.clear()
     assert c.total_length() == 0 and c.dev_lengths.tolist() == [0, 0, 0]
+    assert sorted(c._free) == list(range(6))
     with pytest.raises(ValueError):
         att.KVCache(cfg, max_batch=2 ** 16, max_len=2 ** 16, num_layers=0, device="cpu")
+
+
+def test_kv_cache_window_ring_keeps_the_window_and_limits_popn():
+    """The sliding-window ring holds the last 9 pages: a popn may only go back
+    as far as the ring still covers the new window; the pool of a window layer
+    is ~max_len / 144 times smaller than a full layer's."""
+    _, cfgm, _, _, att = mods()
+    cfg = small_config(cfgm)
+    c = att.KVCache(cfg, max_batch=2, max_len=4096, num_layers=2, device="cpu")
+    assert c.k[1].shape[0] == 2 * 4096 and c.k[0].shape[0] == 2 * 144
+    c.begin_forward([0], [1000])
+    # positions 1000 - 144 .. 999 are in the ring (pages 54..62 of 16 tokens)
+    k, v = c.read_rows(0, 0, 1000 - 128, 128)
+    assert k.shape == (128, 8, 64)
+    c.popn(0, 8)                      # window after the pop starts at 864 >= 864 (page 54): fine
+    with pytest.raises(ValueError):
+        c.popn(0, 9)                  # would need position 863 (page 53, overwritten by page 62)
+    assert int(c.lengths[0]) == 992
+    c.begin_forward([0], [30])        # re-append to 1022: page 63 overwrites page 54 in the ring
+    with pytest.raises(ValueError):
+        c.popn(0, 30)                 # back to 992 would need position 864 (page 54)
+    c.popn(0, 14)                     # back to 1008 needs 880 (page 55): still there
+    assert int(c.lengths[0]) == 1008
+    c.add_sequence(0)
+    c.begin_forward([0], [100])
+    c.popn(0, 99)                     # a short sequence: everything is still in the ring
 
 
 def test_engine_rejects_other_targets():

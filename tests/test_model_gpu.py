@@ -75,8 +75,9 @@ def chain(oracle, model, cache, ids, seq, mode):
         cache.begin_forward([seq], [T])
     for i, blk in enumerate(model.model.block):
         x_in = G.host(x).reshape(T, H)
-        k_prev = G.host(cache.k[i][seq, :pos0])
-        v_prev = G.host(cache.v[i][seq, :pos0])
+        lo = max(0, pos0 - cache.window) if cache.windowed[i] else 0  # a window layer keeps its window only
+        kp, vp = cache.read_rows(i, seq, lo, pos0 - lo)
+        k_prev, v_prev = G.host(kp), G.host(vp)
         x, _ = blk.attn(x, cache, cache.positions, mode)
         torch.cuda.synchronize()
         got = G.host(x).reshape(T, H)
