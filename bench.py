@@ -849,6 +849,65 @@ def route_bench(dev, iters=10):
     return out
 
 
+DENSE_SHAPES = {"qkv 5120x2880": (5120, 2880, True), "out 2880x4096": (2880, 4096, True),
+                "unembedding 201088x2880": (201088, 2880, False)}
+
+
+def dense_bench(dev, peaks, iters=10, tokens=(1, 8, 64, 256, 4096)):
+    """The attention block's projections and the unembedding (bf16, fp32
+    accumulation): gptoss_dense_gemm (tcgen05) beside torch's nn.Linear
+    (cuBLAS) on the same inputs; CUDA events per call after a 256 MB L2
+    flush, median of `iters`.  Inputs resident."""
+    import torch
+    import torch.nn.functional as F
+    lib = importlib.import_module("gpt-oss-tvm_b200._lib")
+    g = torch_gen(dev, 41)
+    P = lambda a: ctypes.c_void_p(a.data_ptr()) if a is not None else None  # noqa: E731
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    tc_peak = float(peaks.get("bf16_tflops", 1590.0))
+    res = {}
+    for name, (N, K, has_bias) in DENSE_SHAPES.items():
+        w = (torch.randn(N, K, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        b = (torch.randn(N, generator=g, device=dev) * 0.02).to(torch.bfloat16) if has_bias else None
+        for T in tokens:
+            if T > 256 and not has_bias:
+                continue  # the unembedding only sees the last token of each sequence
+            x = torch.randn(T, K, generator=g, device=dev).to(torch.bfloat16)
+            out = torch.empty(T, N, dtype=torch.bfloat16, device=dev)
+
+            def ours():
+                lib.call("gptoss_dense_gemm", P(x), T, P(w), P(b), N, K, P(out), None, stream)
+
+            def theirs():
+                F.linear(x, w, b)
+
+            times = {}
+            for tag, fn in (("gptoss_dense_gemm", ours), ("cublas", theirs)):
+                ts = []
+                for i in range(iters + 2):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    fn()
+                    e1.record()
+                    torch.cuda.synchronize()
+                    if i >= 2:
+                        ts.append(e0.elapsed_time(e1))
+                times[tag] = statistics.median(ts)
+            bytes_ = N * K * 2 + T * K * 2 + T * N * 2
+            flops = 2.0 * T * N * K
+            ms = times["gptoss_dense_gemm"]
+            res[f"{name} T={T}"] = {
+                "ms": round(ms, 4), "cublas_ms": round(times["cublas"], 4),
+                "speedup_vs_cublas": round(times["cublas"] / ms, 3),
+                "achieved_gbs": round(bytes_ / ms / 1e6, 1), "hbm_frac": round(bytes_ / ms / 1e6 / hbm, 4),
+                "tflops": round(flops / ms / 1e9, 1), "tensor_frac": round(flops / ms / 1e9 / tc_peak, 4)}
+    res["note"] = "L2 flushed (256 MB write) before every call; bytes = weights + inputs + outputs once"
+    return res
+
+
 def kernel_case(args):
     """--kernel-case NAME: one family of kernels alone on cuda:0, printed as
     JSON (small, self-contained commands for ncu captures)."""
@@ -858,6 +917,8 @@ def kernel_case(args):
     torch.cuda.set_device(0)
     if args.kernel_case == "attention":
         res = attention_bench(dev, peaks, iters=args.steps)
+    elif args.kernel_case == "dense":
+        res = dense_bench(dev, peaks, iters=args.steps)
     else:
         res = route_bench(dev, iters=args.steps)
     print(json.dumps({args.kernel_case: res}), flush=True)
@@ -946,8 +1007,9 @@ def main():
                     help="with --full-model-only: expert-parallel model even on one GPU (a one-rank group)")
     ap.add_argument("--no-fm-prefill", dest="fm_prefill", action="store_false",
                     help="with --full-model-only: skip the long-prompt prefill measurement")
-    ap.add_argument("--kernel-case", default=None, choices=["attention", "route"],
-                    help="run only this kernel family (attention prefill/decode, or RMSNorm + router) and print it")
+    ap.add_argument("--kernel-case", default=None, choices=["attention", "route", "dense"],
+                    help="run only this kernel family (attention prefill/decode, RMSNorm + router, or the dense "
+                         "projections) and print it")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -99,6 +99,7 @@ SIGNATURES = {
     "gptoss_ep_destroy": (None, [_P]),
     "gptoss_dense_gemv_max_tokens": (ctypes.c_int, []),
     "gptoss_dense_gemv": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _P]),
+    "gptoss_dense_gemm": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _P, _P]),
 }
 
 _lib = None

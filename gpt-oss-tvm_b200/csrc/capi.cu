@@ -58,6 +58,10 @@ static int num_sms() {
   return n;
 }
 
+namespace gptoss {
+int device_sm_count() { return num_sms(); }
+}  // namespace gptoss
+
 #define GPTOSS_STREAM(s) ((cudaStream_t)(s))
 
 extern "C" {
@@ -531,6 +535,16 @@ int gptoss_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* weight, cons
                 dense_gemv_max_tokens(), (long long)T, N, K);
   if (((uintptr_t)weight & 15)) return fail(-1, "gptoss_dense_gemv: weight must be 16-byte aligned");
   return check_launch(launch_dense_gemv(x, T, weight, bias, N, K, out, GPTOSS_STREAM(stream)), "dense_gemv");
+}
+
+int gptoss_dense_gemm(const uint16_t* x, int64_t T, const uint16_t* weight, const uint16_t* bias, int32_t N,
+                      int32_t K, uint16_t* out, uint32_t* err, void* stream) {
+  if (T < 0 || T > 0x7FFFFFFF || N <= 0 || K <= 0 || K % 8)
+    return fail(-1, "gptoss_dense_gemm: T must be >= 0, N > 0, K a positive multiple of 8 (T=%lld N=%d K=%d)",
+                (long long)T, N, K);
+  if (((uintptr_t)x & 15) || ((uintptr_t)weight & 15) || ((uintptr_t)out & 15))
+    return fail(-1, "gptoss_dense_gemm: x, weight and out must be 16-byte aligned");
+  return check_launch(launch_dense_gemm(x, T, weight, bias, N, K, out, err, GPTOSS_STREAM(stream)), "dense_gemm");
 }
 
 }  // extern "C"

@@ -40,12 +40,17 @@ int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream);
 int dense_gemv_max_tokens();
 int launch_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* W, const uint16_t* bias, int32_t N, int32_t K,
                       uint16_t* out, cudaStream_t s);
+// SM count of the current device (cached per device)
+int device_sm_count();
+// dense_tc.cu: the same product at any T on the tensor cores
+int launch_dense_gemm(const uint16_t* x, int64_t T, const uint16_t* W, const uint16_t* bias, int32_t N, int32_t K,
+                      uint16_t* out, uint32_t* err, cudaStream_t s);
 // moe_gemv.cu: the decode-size form of the same GEMMs (f16 path, local outputs)
 bool moe_gemv_supported(const GemmLaunch& L);
 int launch_moe_gemv(int mode, const GemmLaunch& L, cudaStream_t stream);
 
 // Default of the block-scaled decode GEMMs (environment GPTOSS_MOE_MX overrides).
-constexpr bool kMoeMxDefault = false;
+constexpr bool kMoeMxDefault = true;
 bool moe_mx_enabled();
 
 // moe_mx.cu: decode-size GEMMs on the block-scaled tensor cores (quantized activations)

@@ -261,6 +261,18 @@ int gptoss_dense_gemv_max_tokens(void);
 int gptoss_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* weight, const uint16_t* bias, int32_t N,
                       int32_t K, uint16_t* out, void* stream);
 
+/* The same projections at every size on the tensor cores (tcgen05.mma
+ * kind::f16, TMA-fed, fp32 in TMEM), and the unembedding without bias
+ * (model/transformer.py:99-104): out [T, N] = bf16(x [T, K] . weight [N, K]^T
+ * (+ bias [N])), one rounding.  T <= 256 streams the weight rows as the MMA's
+ * M side (clusters of CTAs split K when the weight tiles are few; the split
+ * partials are added in a fixed order, so results are deterministic); larger
+ * T runs persistent 128 x 256 tiles.  x, weight and out 16-byte aligned, K a
+ * multiple of 8; bias may be NULL; err: optional device word that records a
+ * pipeline wait that ran out (the call then leaves out incomplete). */
+int gptoss_dense_gemm(const uint16_t* x, int64_t T, const uint16_t* weight, const uint16_t* bias, int32_t N,
+                      int32_t K, uint16_t* out, uint32_t* err, void* stream);
+
 /* MLPBlock.forward like gptoss_moe_forward, but allocating nothing: no
  * cudaMalloc, no cudaFree, no workspace.  It has no counterpart in the
  * reference.  It is for callers that cannot allocate device memory when the

@@ -55,10 +55,12 @@ class MoEPieces:
     """Runs the MoE block step by step through the C ABI (device buffers
     allocated here with torch) so each stage can be compared with the oracle."""
 
-    def __init__(self, p: dict, k: int = 4, f16: bool | None = None, mx: bool = False):
+    def __init__(self, p: dict, k: int = 4, f16: bool | None = None, mx: bool | None = False):
         """f16: GEMM path (None = what gptoss_moe_weights_prepare allows);
         mx: the block-scaled decode GEMMs (activations quantized into two e4m3
-        terms; y is f16 on that path)."""
+        terms; y is f16 on that path); None = the expert path that
+        gptoss_moe_forward takes for the same token count
+        (gptoss_moe_uses_block_scaled)."""
         self.mx = mx
         self.p = {kk: dev(v) for kk, v in p.items()}
         self.E = p["gate_weight"].shape[0]
@@ -72,9 +74,12 @@ class MoEPieces:
         w.norm_weight = self.p["norm_weight"].data_ptr()
         w.mlp1_scales = self.p["mlp1_weight_scales"].data_ptr()
         w.mlp2_scales = self.p["mlp2_weight_scales"].data_ptr()
+        w.mlp1_blocks = self.p["mlp1_weight_blocks"].data_ptr()
+        w.mlp2_blocks = self.p["mlp2_weight_blocks"].data_ptr()
         call("gptoss_moe_weights_prepare", ctypes.byref(w), S())
         allowed = bool(w.flags & _lib.MOE_F16)
         self.f16 = allowed if f16 is None else (f16 and allowed)
+        self.w = w
 
     def run(self, x_bits: np.ndarray, routing=None):
         """routing: optional (weights bf16 bits [M,k], indices int32 [M,k])
@@ -83,6 +88,9 @@ class MoEPieces:
         x = dev(x_bits)
         M = x.shape[0]
         R = M * k
+        mx = self.mx
+        if mx is None:
+            mx = bool(_lib.load().gptoss_moe_uses_block_scaled(M, ctypes.byref(self.w)))
         i32 = dict(dtype=torch.int32, device="cuda")
         t = torch.empty_like(x)
         logits = torch.empty(M, E, dtype=torch.bfloat16, device="cuda")
@@ -109,7 +117,7 @@ class MoEPieces:
             idx.copy_(dev(routing[1]))
         call("gptoss_moe_permute", P(idx), M, k, E, P(indptr), P(tok), P(rev), P(exp_), P(tile_ptr), P(tile_rows),
              P(self.err), S())
-        if self.mx:
+        if mx:
             y = torch.empty(R, I, dtype=torch.float16, device="cuda")
             q = torch.empty(R, 2 * max(H, I), dtype=torch.uint8, device="cuda")
             qs = torch.zeros(R, 192, dtype=torch.uint8, device="cuda")

@@ -81,7 +81,7 @@ def test_moe_forward_entry_point_matches_pieces(params_e8):
     blk = mlp.MLPBlock(cfg).load_state(params_e8)
     x = synth().activations(64, seed=7)
     out = blk.forward(G.dev(x).reshape(1, 64, 2880))
-    r = G.MoEPieces(params_e8).run(x)
+    r = G.MoEPieces(params_e8, mx=None).run(x)
     np.testing.assert_array_equal(G.host(out).reshape(64, 2880), r["out"])
     assert blk.device_error() == 0
 
