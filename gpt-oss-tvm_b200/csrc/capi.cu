@@ -83,7 +83,7 @@ int gptoss_moe_router(const uint16_t* t, const uint16_t* gate_weight, const uint
   if (M < 0 || E <= 0 || E > 256 || E % 8 || K < 1 || K > 8 || K > E || H <= 0)
     return fail(-1, "gptoss_moe_router: unsupported shape M=%lld E=%d H=%d K=%d (E must be a multiple of 8, <= 256)",
                 (long long)M, E, H, K);
-  int rc = launch_router(t, gate_weight, gate_bias, M, E, H, logits, GPTOSS_STREAM(stream));
+  int rc = launch_router(t, gate_weight, gate_bias, M, E, H, logits, err, GPTOSS_STREAM(stream));
   if (rc) return check_launch(rc, "router");
   return check_launch(launch_topk_softmax(logits, M, E, K, topk_weights, topk_indices, err, GPTOSS_STREAM(stream)),
                       "topk_softmax");

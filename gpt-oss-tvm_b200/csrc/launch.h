@@ -40,6 +40,10 @@ int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream);
 int dense_gemv_max_tokens();
 int launch_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* W, const uint16_t* bias, int32_t N, int32_t K,
                       uint16_t* out, cudaStream_t s);
+// router_bf16.cu: router logits on the bf16 FMA pipe, stage-checked against
+// the double-rounding case (bit-exact to launch_router's serial fp32 chains)
+int launch_router_bf16(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H,
+                       uint16_t* logits, uint32_t* err, cudaStream_t s);
 // SM count of the current device (cached per device)
 int device_sm_count();
 // dense_tc.cu: the same product at any T on the tensor cores
@@ -62,7 +66,7 @@ int launch_moe_gemm_mx(int mode, const GemmLaunch& L, const uint8_t* q, const ui
 // moe_route.cu
 int launch_rmsnorm(const uint16_t*, const uint16_t*, int64_t, int32_t, float, uint16_t*, uint32_t*, cudaStream_t);
 int launch_router(const uint16_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t, uint16_t*,
-                  cudaStream_t);
+                  uint32_t* err, cudaStream_t);
 int launch_topk_softmax(const uint16_t*, int64_t, int32_t, int32_t, uint16_t*, int32_t*, uint32_t*, cudaStream_t);
 int launch_permute(const int32_t*, int64_t, int32_t, int32_t, int32_t*, int32_t*, int32_t*, int32_t*, int32_t*,
                    int32_t*, uint32_t*, cudaStream_t);

@@ -8,6 +8,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "launch.h"
 
 namespace gptoss {
 
@@ -700,9 +701,17 @@ static int launch_router_tiles(int egroups, dim3 grid, size_t smem, cudaStream_t
   return 0;
 }
 
+// GPTOSS_ROUTER_BF16=0 keeps the router on the fp32-FMA chain kernels below
+// (same bits, slower); otherwise router_bf16.cu's kernels run.
+static bool router_bf16_enabled() {
+  const char* e = getenv("GPTOSS_ROUTER_BF16");
+  return !(e && e[0] == '0');
+}
+
 int launch_router(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H,
-                  uint16_t* logits, cudaStream_t s) {
+                  uint16_t* logits, uint32_t* err, cudaStream_t s) {
   if (M <= 0) return 0;
+  if (router_bf16_enabled()) return launch_router_bf16(t, W, b, M, E, H, logits, err, s);
   if (E % kRTE != 0 || E > 1024 || H % 8 || ((uintptr_t)t & 15) || ((uintptr_t)W & 15)) return -12;
   if (M <= kRouterChainMaxTokens) {
     dim3 grid((unsigned)((E + kChainExp - 1) / kChainExp), (unsigned)((M + kChainTok - 1) / kChainTok));

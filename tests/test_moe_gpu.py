@@ -342,9 +342,13 @@ def test_rmsnorm_bit_exact_odd_sizes(oracle):
 
 
 @pytest.mark.parametrize("E", [8, 32, 128])
-def test_router_bit_exact_both_kernels(oracle, E):
+@pytest.mark.parametrize("fma", ["bf16", "fp32"])
+def test_router_bit_exact_both_kernels(oracle, E, fma, monkeypatch):
     """Router logits at token counts served by the per-chain kernel (<= 512
-    tokens) and by the register-tiled kernel (> 512), bit-exact."""
+    tokens) and by the register-tiled kernel (> 512), bit-exact; both on the
+    bf16 FMA pipe (the default) and on fp32 FMA + conversion
+    (GPTOSS_ROUTER_BF16=0)."""
+    monkeypatch.setenv("GPTOSS_ROUTER_BF16", "1" if fma == "bf16" else "0")
     rng = np.random.default_rng(40 + E)
     S = synth()
     Wg = S.bf16_bits(rng.standard_normal((E, 2880)).astype(np.float32) * 0.02)
