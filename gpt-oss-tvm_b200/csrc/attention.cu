@@ -724,14 +724,31 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const uint16_t* __rest
   }
   cp_async_commit();
   const int64_t ntile_all = s_hi > s_lo ? (s_hi - s_lo + kAttBK - 1) / kAttBK : 0;
+  // a lane copies one 16-byte piece (ch) of rows lane / 8 + 4 i; the page of a
+  // row is found from the tile's first page (one modulo per tile) plus its
+  // page offset within the tile (at most 4)
+  const int* trow_tab = table ? table + (int64_t)b * tstride : nullptr;
   auto load = [&](int buf, int64_t j0) {
     uint8_t* kb = wbuf + buf * (2 * kAttBK * 128);
     uint8_t* vb = kb + kAttBK * 128;
-    for (int c = lane; c < kAttBK * 8; c += 32) {
-      const int r = c >> 3, ch = c & 7;
+    const int ch = lane & 7;
+    const int64_t p0 = j0 >> 4;
+    const int32_t lp0 = trow_tab ? (int32_t)(p0 % tstride) : 0;
+#pragma unroll 4
+    for (int i = 0; i < kAttBK / 4; ++i) {
+      const int r = (lane >> 3) + 4 * i;
       const int64_t kj = j0 + r;
       const bool ok = kj < s_hi;
-      const int64_t src = (kv_row(table, tstride, max_len, b, ok ? kj : s_lo) * Hkv + gk) * kAttD + ch * 8;
+      const int64_t jj = ok ? kj : j0;  // j0 < s_hi: a valid row to point the skipped copy at
+      int64_t row;
+      if (trow_tab) {
+        int32_t lp = lp0 + (int32_t)((jj >> 4) - p0);
+        if (lp >= tstride) lp -= tstride;
+        row = (int64_t)__ldg(trow_tab + lp) * 16 + (jj & 15);
+      } else {
+        row = (int64_t)b * max_len + jj;
+      }
+      const int64_t src = (row * Hkv + gk) * kAttD + ch * 8;
       cp_async16(smem_u32(kb) + swz(r, ch), kc + src, ok);
       cp_async16(smem_u32(vb) + swz(r, ch), vc + src, ok);
     }
