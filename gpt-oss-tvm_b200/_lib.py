@@ -100,6 +100,9 @@ SIGNATURES = {
     "gptoss_dense_gemv_max_tokens": (ctypes.c_int, []),
     "gptoss_dense_gemv": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _P]),
     "gptoss_dense_gemm": (ctypes.c_int, [_P, _I64, _P, _P, _I32, _I32, _P, _P, _P]),
+    "gptoss_sample_top_p_scratch_bytes": (_I64, [_I64, _I64]),
+    "gptoss_sample_top_p_from_logits": (ctypes.c_int, [_P, _I64, _I64, ctypes.c_double, ctypes.c_double, _P,
+                                                        ctypes.c_double, _P, _I64, _P, _P]),
 }
 
 _lib = None

@@ -537,6 +537,27 @@ int gptoss_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* weight, cons
   return check_launch(launch_dense_gemv(x, T, weight, bias, N, K, out, GPTOSS_STREAM(stream)), "dense_gemv");
 }
 
+int64_t gptoss_sample_top_p_scratch_bytes(int64_t B, int64_t V) {
+  return (B > 0 && V > 0) ? B * sample_top_p_scratch_bytes_per_row(V) : 0;
+}
+
+int gptoss_sample_top_p_from_logits(const float* logits, int64_t B, int64_t V, double temperature, double top_p,
+                                    const double* uniform, double uniform0, void* scratch, int64_t scratch_bytes,
+                                    int32_t* tokens, void* stream) {
+  if (B < 0 || V <= 0 || V > 0x7FFFFFFF || !(top_p > 0.0) || top_p > 1.0)
+    return fail(-1, "gptoss_sample_top_p_from_logits: need B >= 0, 0 < V < 2^31, 0 < top_p <= 1 (B=%lld V=%lld top_p=%g)",
+                (long long)B, (long long)V, top_p);
+  if (!uniform && !(uniform0 >= 0.0 && uniform0 < 1.0))
+    return fail(-1, "gptoss_sample_top_p_from_logits: the uniform draw must be in [0, 1) (got %g)", uniform0);
+  if (B && (!logits || !tokens)) return fail(-1, "gptoss_sample_top_p_from_logits: null pointer");
+  if (B && temperature >= 1e-6 && (!scratch || scratch_bytes < sample_top_p_scratch_bytes_per_row(V)))
+    return fail(-1, "gptoss_sample_top_p_from_logits: scratch of at least %lld bytes (one row) is required",
+                (long long)sample_top_p_scratch_bytes_per_row(V));
+  return check_launch(launch_sample_top_p(logits, B, V, temperature, top_p, uniform, uniform0, scratch,
+                                          scratch_bytes, tokens, GPTOSS_STREAM(stream)),
+                      "sample_top_p");
+}
+
 int gptoss_dense_gemm(const uint16_t* x, int64_t T, const uint16_t* weight, const uint16_t* bias, int32_t N,
                       int32_t K, uint16_t* out, uint32_t* err, void* stream) {
   if (T < 0 || T > 0x7FFFFFFF || N <= 0 || K <= 0 || K % 8)

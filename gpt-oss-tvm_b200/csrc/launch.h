@@ -44,6 +44,11 @@ int launch_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* W, const uin
 // the double-rounding case (bit-exact to launch_router's serial fp32 chains)
 int launch_router_bf16(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H,
                        uint16_t* logits, uint32_t* err, cudaStream_t s);
+// sample.cu: top-p sampling from fp32 logits, one CTA per row
+int64_t sample_top_p_scratch_bytes_per_row(int64_t V);
+int launch_sample_top_p(const float* logits, int64_t B, int64_t V, double temperature, double top_p,
+                        const double* uniform, double uniform0, void* scratch, int64_t scratch_bytes, int32_t* out,
+                        cudaStream_t s);
 // SM count of the current device (cached per device)
 int device_sm_count();
 // dense_tc.cu: the same product at any T on the tensor cores

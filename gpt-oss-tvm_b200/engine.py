@@ -20,6 +20,7 @@ next on the device.
 """
 from __future__ import annotations
 
+import ctypes
 from pathlib import Path
 
 import numpy as np
@@ -170,24 +171,30 @@ class Engine:
 
     def sample(self, logits: torch.Tensor) -> int:
         """Top-p sampling with the reference's parameters (temperature 0.7,
-        top_p 0.9, uniform draw 0.5; engine.py:39, :172-174): softmax of
-        logits / temperature, the smallest prefix of tokens by descending
-        probability whose mass reaches top_p, and the token at which that
-        prefix's renormalised cumulative mass first exceeds the draw."""
-        temperature = float(self.sample_parameters["temperature"])
-        top_p = float(self.sample_parameters["top_p"])
-        u = float(self.sample_parameters["random_seed"])
-        z = logits.reshape(-1).float()
-        if temperature <= 0:
-            return int(torch.argmax(z))
-        p = torch.softmax(z / temperature, dim=0)
-        sp, idx = torch.sort(p, descending=True)
-        cum = torch.cumsum(sp, 0)
-        keep = int(torch.searchsorted(cum, torch.tensor([top_p], device=cum.device)).item()) + 1
-        keep = min(max(keep, 1), sp.numel())
-        cum_k = cum[:keep] / cum[keep - 1]
-        j = int(torch.searchsorted(cum_k, torch.tensor([u], device=cum.device), right=True).item())
-        return int(idx[min(j, keep - 1)])
+        top_p 0.9, uniform draw 0.5; engine.py:38-39, :172-174) on the GPU:
+        gptoss_sample_top_p_from_logits, the device form of TVM's
+        vm.builtin.sample_top_p_from_logits that the reference calls."""
+        return int(self.sample_batch(logits.reshape(1, -1))[0])
+
+    def sample_batch(self, logits: torch.Tensor, uniform: torch.Tensor | None = None) -> torch.Tensor:
+        """One token per row of logits [B, V] (any float dtype; read as fp32),
+        returned as an int32 tensor on the device without a host round trip.
+        uniform: optional [B] float64 device tensor of draws in [0, 1)
+        (default: the reference's fixed 0.5 for every row)."""
+        z = logits.reshape(logits.shape[0], -1).float().contiguous()
+        B, V = z.shape
+        tok = torch.empty(B, dtype=torch.int32, device=z.device)
+        u = uniform.to(device=z.device, dtype=torch.float64).contiguous() if uniform is not None else None
+        p = self.sample_parameters
+        P = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        with torch.cuda.device(z.device):
+            # scratch for up to 8 rows at a time (16 bytes per vocabulary entry and row)
+            nbytes = int(_lib.load().gptoss_sample_top_p_scratch_bytes(min(B, 8), V))
+            scratch = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=z.device)
+            _lib.call("gptoss_sample_top_p_from_logits", P(z), B, V, float(p["temperature"]), float(p["top_p"]),
+                      P(u) if u is not None else None, float(p["random_seed"]), P(scratch), nbytes, P(tok),
+                      ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return tok
 
     def generate(self, prompt_tokens, max_new_tokens: int, sequence_id: int = 0) -> list[int]:
         """Greedy generation for one sequence: prefill, then decode."""

@@ -273,6 +273,22 @@ int gptoss_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* weight, cons
 int gptoss_dense_gemm(const uint16_t* x, int64_t T, const uint16_t* weight, const uint16_t* bias, int32_t N,
                       int32_t K, uint16_t* out, uint32_t* err, void* stream);
 
+/* Engine.sample (engine.py:38-39, :172-174), i.e. TVM's
+ * vm.builtin.sample_top_p_from_logits(logits, temperature, top_p,
+ * uniform_sample) (src/runtime/vm/lm_support.cc), on the device and batched:
+ * row b of logits [B, V] (fp32, device) gives tokens[b] (int32, device): the
+ * argmax when temperature < 1e-6, otherwise the top-p draw with
+ * uniform[b] (device, B doubles) or, when uniform is NULL, uniform0 for every
+ * row -- the reference's float running sums in its order, so the same token.
+ * Ties among logits go to the lower index.  scratch: device memory for the
+ * rows whose large elements do not fit on chip; gptoss_sample_top_p_scratch_bytes
+ * (B, V) bytes run all rows at once, less runs them in groups (at least one
+ * row's worth is required unless temperature < 1e-6). */
+int64_t gptoss_sample_top_p_scratch_bytes(int64_t B, int64_t V);
+int gptoss_sample_top_p_from_logits(const float* logits, int64_t B, int64_t V, double temperature, double top_p,
+                                    const double* uniform, double uniform0, void* scratch, int64_t scratch_bytes,
+                                    int32_t* tokens, void* stream);
+
 /* MLPBlock.forward like gptoss_moe_forward, but allocating nothing: no
  * cudaMalloc, no cudaFree, no workspace.  It has no counterpart in the
  * reference.  It is for callers that cannot allocate device memory when the

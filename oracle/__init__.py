@@ -11,9 +11,14 @@ target.  Parity is pinned by ``tests/golden/*.npz``: outputs of the reference
 itself, compiled by TVM's C target (``tests/golden/make_golden.py``), which
 ``tests/test_oracle_golden.py`` compares with this oracle bit for bit.
 The attention core (TVM/MLC paged-cache kernels, third-party and absent from
-the reference tree) and the MoE permutation (mlc_llm.op.moe_misc, absent) are
-restatements of the published algorithms; their parity is unpinned by
-reference outputs and is pinned instead by the property tests.
+the reference tree) is pinned by ``tests/golden/attention.npz``, outputs of
+TVM's own CPU kernels (``tests/golden/make_attn_golden.py``).  The sampler
+(``sample_top_p_from_logits``: TVM's ``vm.builtin.sample_top_p_from_logits``,
+src/runtime/vm/lm_support.cc, which the reference's Engine.sample calls) is
+pinned by ``tests/golden/sampling.npz``, tokens returned by that function
+(``tests/golden/make_sampling_golden.py``).  The MoE permutation
+(mlc_llm.op.moe_misc, absent) is a restatement of the published algorithm,
+pinned by the property tests.
 """
 from __future__ import annotations
 
@@ -274,3 +279,31 @@ def attention_block_core(q, k, v, sinks, causal=True, window=0, sm_scale=0.125):
     """self_attention + sink rescale (model/attention.py:218-247)."""
     o, lse = attention(q, k, v, causal, window, sm_scale)
     return sink_rescale(o, lse, sinks), lse
+
+
+def sample_top_p_from_logits(logits, temperature, top_p, uniform):
+    """Top-p sampling as TVM's SampleTopPFromLogits (src/runtime/vm/lm_support.cc,
+    called by the reference's Engine.sample, engine.py:38-39, :172-174), step
+    by step in float32: sort (logit, index) by descending logit; argmax when
+    temperature < 1e-6; e = expf((l - max) * float(1 / temperature)) with the
+    sum taken sequentially in that order; prob = e / sum; a sequential cumsum
+    of prob, with top_p_sum = the probabilities added while the running sum was
+    below top_p; the token is the first whose cumsum / top_p_sum exceeds the
+    uniform draw (compared in double).  Ties among logits are ordered by index
+    (std::sort leaves their order unspecified)."""
+    z = np.ascontiguousarray(logits, np.float32).reshape(-1)
+    order = np.argsort(-z, kind="stable")
+    if temperature < 1e-6:
+        return int(order[0])
+    zs = z[order]
+    scale = np.float32(1.0 / float(temperature))
+    e = np.exp((zs - zs[0]) * scale, dtype=np.float32)
+    total = np.cumsum(e, dtype=np.float32)[-1]
+    prob = (e / total).astype(np.float32)
+    cum = np.cumsum(prob, dtype=np.float32)
+    before = np.concatenate([np.zeros(1, np.float32), cum[:-1]])
+    k = int(np.count_nonzero(before.astype(np.float64) < float(top_p)))  # float running sum vs the double top_p
+    top_p_sum = cum[k - 1] if k > 0 else np.float32(0.0)
+    ratio = (cum / top_p_sum).astype(np.float32)
+    hit = np.nonzero(float(uniform) < ratio.astype(np.float64))[0]
+    return int(order[hit[0]]) if hit.size else int(order[0])

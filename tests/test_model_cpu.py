@@ -189,29 +189,6 @@ def test_engine_rejects_other_targets():
             engm.Engine(None, target, config=small_config(cfgm), seed=0)
 
 
-def _top_p_numpy(z, temperature, top_p, u):
-    p = np.exp((z - z.max()) / temperature)
-    p /= p.sum()
-    order = np.argsort(-p, kind="stable")
-    cum = np.cumsum(p[order])
-    keep = int(np.searchsorted(cum, top_p)) + 1
-    cum_k = cum[:keep] / cum[keep - 1]
-    j = int(np.searchsorted(cum_k, u, side="right"))
-    return int(order[min(j, keep - 1)])
-
-
-@pytest.mark.parametrize("seed", range(5))
-def test_top_p_sampling(seed):
-    _, _, _, engm, _ = mods()
-    rng = np.random.default_rng(seed)
-    z = (rng.standard_normal(500) * 3).astype(np.float32)
-    fake = types.SimpleNamespace(sample_parameters={"temperature": 0.7, "top_p": 0.9, "random_seed": 0.5})
-    got = engm.Engine.sample(fake, torch.from_numpy(z).reshape(1, 1, -1))
-    assert got == _top_p_numpy(z.astype(np.float64), 0.7, 0.9, 0.5)
-    fake.sample_parameters["temperature"] = 0.0
-    assert engm.Engine.sample(fake, torch.from_numpy(z)) == int(np.argmax(z))
-
-
 def test_expert_parallel_model_shards_experts_one_rank_gloo():
     """Construction over a one-rank gloo group: the expert shard of every
     layer, the same parameter names as the plain model, the loader slice."""
