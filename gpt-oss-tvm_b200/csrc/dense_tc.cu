@@ -287,6 +287,45 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 
 static int dense_slots_per_sm(int bn) { return bn <= 64 ? 2 : 1; }
 
+// Clusters of `split` CTAs of this configuration that can be resident at
+// once (cached per device, configuration and split; 0 when none fits).
+template <int kBN>
+static int dense_max_clusters(int split) {
+  constexpr int kMaxDev = 16;
+  static int cache[kMaxDev][kDnMaxSplit + 1];
+  static bool init = false;
+  if (!init) {
+    for (auto& row : cache)
+      for (int& v : row) v = -1;
+    init = true;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
+    (void)cudaGetLastError();
+    return 0;
+  }
+  if (cache[dev][split] < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = 1;
+    attrs[0].val.clusterDim.y = split;
+    attrs[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kDnThreads);
+    cfg.dynamicSmemBytes = DenseCfg<kBN>::kAlloc;
+    cfg.gridDim = dim3(1, split);
+    cfg.attrs = attrs;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, dense_gemm_tc_kernel<kBN>, &cfg) != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    cache[dev][split] = n;
+  }
+  return cache[dev][split];
+}
+
 template <int kBN>
 static int launch_dense_bn(const CUtensorMap& ta, const CUtensorMap& tb, const DenseParams& p, cudaStream_t s) {
   using C = DenseCfg<kBN>;
@@ -294,6 +333,8 @@ static int launch_dense_bn(const CUtensorMap& ta, const CUtensorMap& tb, const D
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
+    // all of the SM's unified memory as shared memory: two decode-size CTAs per SM
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     attr = true;
   }
   const int slots = device_sm_count() * dense_slots_per_sm(kBN);
@@ -301,8 +342,14 @@ static int launch_dense_bn(const CUtensorMap& ta, const CUtensorMap& tb, const D
   const int32_t nch = (p.K + kDnBK - 1) / kDnBK;
   int split = 1;
   if (tiles < slots) {
-    // the largest power of two that fits the CTA slots, at least four K chunks per CTA
-    while (split * 2 <= kDnMaxSplit && tiles * split * 2 <= slots && nch / (split * 2) >= 4) split *= 2;
+    // the largest split whose clusters all fit at once, at least four K chunks per CTA
+    for (int c = kDnMaxSplit; c >= 2; --c) {
+      if (tiles * c > slots || nch / c < 4) continue;
+      if (tiles <= dense_max_clusters<kBN>(c)) {
+        split = c;
+        break;
+      }
+    }
   }
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attrs[1];
