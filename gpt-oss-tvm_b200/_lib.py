@@ -46,6 +46,8 @@ SIGNATURES = {
     "gptoss_moe_router": (ctypes.c_int, [_P, _P, _P, _I64, _I32, _I32, _I32, _P, _P, _P, _P, _P]),
     "gptoss_moe_topk_softmax": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _P, _P, _P]),
     "gptoss_moe_permute": (ctypes.c_int, [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "gptoss_moe_route": (ctypes.c_int, [_P, _I64, ctypes.POINTER(gptoss_moe_weights), _P, _P, _P, _P, _P, _P, _P, _P,
+                                         _P, _P, _P]),
     "gptoss_moe_gather": (ctypes.c_int, [_P, _P, _I64, _I32, _I32, _P, _P]),
     "gptoss_moe_mlp1": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _F, _F, _I32, _P, _P, _P]),
     "gptoss_moe_mlp2": (ctypes.c_int, [_P, _I64, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _P, _P]),

@@ -624,6 +624,39 @@ extern "C" int gptoss_moe_uses_block_scaled(int64_t M, const gptoss_moe_weights*
   return (w && M > 0 && experts_block_scaled(M, w)) ? 1 : 0;
 }
 
+// Router logits, top-k + softmax and the expert-major permutation of M
+// normalised tokens t: one fused launch after the logits at decode sizes,
+// the separate kernels otherwise (same results either way).
+int gptoss::moe_route(const uint16_t* t, int64_t M, const gptoss_moe_weights* w, uint16_t* logits,
+                      uint16_t* topk_w, int32_t* topk_idx, int32_t* indptr, int32_t* token_of_row,
+                      int32_t* row_of_pair, int32_t* expert_of_row, int32_t* tile_ptr, int32_t* tile_rows,
+                      uint32_t* err, void* stream) {
+  const int32_t E = w->num_experts, K = w->top_k, H = w->hidden;
+  // (one CTA runs every token's top-k: it wins below ~64 tokens, the parallel kernels above)
+  if (M * K <= 256 && M * K <= route_small_max_pairs() && E <= 256 && E % 8 == 0 && K <= 8) {
+    int rc = launch_router(t, w->gate_weight, w->gate_bias, M, E, H, logits, err, GPTOSS_STREAM(stream));
+    if (rc) return check_launch(rc, "router");
+    return check_launch(launch_route_small(logits, M, E, K, topk_w, topk_idx, indptr, tile_ptr, tile_rows,
+                                           token_of_row, row_of_pair, expert_of_row, err, GPTOSS_STREAM(stream)),
+                        "route_small");
+  }
+  int rc;
+  if ((rc = gptoss_moe_router(t, w->gate_weight, w->gate_bias, M, E, H, K, logits, topk_w, topk_idx, err, stream)))
+    return rc;
+  return gptoss_moe_permute(topk_idx, M, K, E, indptr, token_of_row, row_of_pair, expert_of_row, tile_ptr, tile_rows,
+                            err, stream);
+}
+
+extern "C" int gptoss_moe_route(const uint16_t* t, int64_t M, const gptoss_moe_weights* w, uint16_t* logits,
+                                uint16_t* topk_weights, int32_t* topk_indices, int32_t* indptr, int32_t* token_of_row,
+                                int32_t* row_of_pair, int32_t* expert_of_row, int32_t* tile_ptr, int32_t* tile_rows,
+                                uint32_t* err, void* stream) {
+  if (!w || M < 0) return fail(-1, "gptoss_moe_route: null weights or M < 0");
+  if (M == 0) return 0;
+  return gptoss::moe_route(t, M, w, logits, topk_weights, topk_indices, indptr, token_of_row, row_of_pair,
+                           expert_of_row, tile_ptr, tile_rows, err, stream);
+}
+
 int gptoss::moe_experts_forward(const uint16_t* t, int64_t M, const gptoss_moe_weights* w, const int32_t* indptr,
                                 const int32_t* tile_ptr, const int32_t* tile_rows, const int32_t* token_of_row,
                                 uint16_t* act, uint16_t* y, float* h2, uint8_t* qs, uint32_t* err, void* stream) {
@@ -738,11 +771,8 @@ int gptoss_moe_forward(const uint16_t* x, int64_t M, const gptoss_moe_weights* w
   const int32_t E = w->num_experts, K = w->top_k, H = w->hidden;
   int rc;
   if ((rc = gptoss_rms_norm(x, w->norm_weight, M, H, w->rms_eps, ws->t, stream))) return rc;
-  if ((rc = gptoss_moe_router(ws->t, w->gate_weight, w->gate_bias, M, E, H, K, ws->logits, ws->topk_w, ws->topk_idx,
-                              ws->err, stream)))
-    return rc;
-  if ((rc = gptoss_moe_permute(ws->topk_idx, M, K, E, ws->indptr, ws->token_of_row, ws->row_of_pair,
-                               ws->expert_of_row, ws->tile_ptr, ws->tile_rows, ws->err, stream)))
+  if ((rc = moe_route(ws->t, M, w, ws->logits, ws->topk_w, ws->topk_idx, ws->indptr, ws->token_of_row,
+                      ws->row_of_pair, ws->expert_of_row, ws->tile_ptr, ws->tile_rows, ws->err, stream)))
     return rc;
   if ((rc = moe_experts_forward(ws->t, M, w, ws->indptr, ws->tile_ptr, ws->tile_rows, ws->token_of_row, ws->act,
                                  ws->y, ws->h2, ws->qs, ws->err, stream)))

@@ -73,6 +73,12 @@ int launch_rmsnorm(const uint16_t*, const uint16_t*, int64_t, int32_t, float, ui
 int launch_router(const uint16_t*, const uint16_t*, const uint16_t*, int64_t, int32_t, int32_t, uint16_t*,
                   uint32_t* err, cudaStream_t);
 int launch_topk_softmax(const uint16_t*, int64_t, int32_t, int32_t, uint16_t*, int32_t*, uint32_t*, cudaStream_t);
+// top-k + softmax + the permutation in one launch for M * K <= route_small_max_pairs()
+int route_small_max_pairs();
+int launch_route_small(const uint16_t* logits, int64_t M, int32_t E, int32_t K, uint16_t* weights,
+                       int32_t* indices, int32_t* indptr, int32_t* tile_ptr, int32_t* tile_rows,
+                       int32_t* token_of_row, int32_t* row_of_pair, int32_t* expert_of_row, uint32_t* err,
+                       cudaStream_t s);
 int launch_permute(const int32_t*, int64_t, int32_t, int32_t, int32_t*, int32_t*, int32_t*, int32_t*, int32_t*,
                    int32_t*, uint32_t*, cudaStream_t);
 int launch_gather(const uint16_t*, const int32_t*, int64_t, int32_t, uint16_t*, int32_t to_f16, cudaStream_t);
@@ -125,6 +131,9 @@ int launch_sink_rescale(uint16_t* o, const float* lse, const uint16_t* sinks, in
 // capi.cu: the expert part of the MoE block (gather or quantize, both grouped
 // GEMMs) on the path the sizes and GPTOSS_MOE_MX select; shared by the
 // workspace and the no-allocation forwards
+int moe_route(const uint16_t* t, int64_t M, const gptoss_moe_weights* w, uint16_t* logits, uint16_t* topk_w,
+              int32_t* topk_idx, int32_t* indptr, int32_t* token_of_row, int32_t* row_of_pair,
+              int32_t* expert_of_row, int32_t* tile_ptr, int32_t* tile_rows, uint32_t* err, void* stream);
 int moe_experts_forward(const uint16_t* t, int64_t M, const gptoss_moe_weights* w, const int32_t* indptr,
                         const int32_t* tile_ptr, const int32_t* tile_rows, const int32_t* token_of_row, uint16_t* act,
                         uint16_t* y, float* h2, uint8_t* qs, uint32_t* err, void* stream);

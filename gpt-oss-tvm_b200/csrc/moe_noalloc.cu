@@ -135,10 +135,8 @@ extern "C" int gptoss_moe_forward_noalloc(const uint16_t* x, int64_t M, const gp
   const int32_t E = w->num_experts, K = w->top_k, H = w->hidden;
   int rc;
   if ((rc = gptoss_rms_norm(x, w->norm_weight, M, H, w->rms_eps, t, stream))) return rc;
-  if ((rc = gptoss_moe_router(t, w->gate_weight, w->gate_bias, M, E, H, K, logits, topk_w, topk_idx, err,
+  if ((rc = gptoss::moe_route(t, M, w, logits, topk_w, topk_idx, indptr, tok, rev, exr, tile_ptr, tile_rows, err,
                               stream)))
-    return rc;
-  if ((rc = gptoss_moe_permute(topk_idx, M, K, E, indptr, tok, rev, exr, tile_ptr, tile_rows, err, stream)))
     return rc;
   if ((rc = gptoss::moe_experts_forward(t, M, w, indptr, tile_ptr, tile_rows, tok, act, y, h2, qs, err, stream)))
     return rc;

@@ -338,19 +338,20 @@ __global__ void __launch_bounds__(128) router_chain_kernel(const uint16_t* __res
 // exp is evaluated in double and rounded once to float (the correctly
 // rounded expf), matching a libm expf to the last bit in all but vanishingly
 // rare cases.  One warp per token.
-__global__ void topk_softmax_kernel(const uint16_t* __restrict__ logits, int64_t M, int32_t E, int32_t K,
-                                    uint16_t* __restrict__ weights, int32_t* __restrict__ indices,
-                                    uint32_t* err) {
-  const int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+// One token's top-k + softmax by one warp (all lanes call; lane 0 writes
+// weights[j], indices[j] for j < K and, when sidx is given, the indices to
+// shared memory too).
+__device__ __forceinline__ void topk_softmax_warp(const uint16_t* __restrict__ lg, int32_t E, int32_t K,
+                                                  uint16_t* __restrict__ weights, int32_t* __restrict__ indices,
+                                                  int32_t* sidx, uint32_t* err) {
   const int lane = threadIdx.x & 31;
-  if (m >= M) return;
   constexpr int kMaxPerLane = 8;  // E <= 256
   float v[kMaxPerLane];
   uint32_t taken = 0;
 #pragma unroll
   for (int i = 0; i < kMaxPerLane; ++i) {
     const int32_t e = lane + 32 * i;
-    v[i] = e < E ? bf16_bits_to_f32(logits[m * E + e]) : -INFINITY;
+    v[i] = e < E ? bf16_bits_to_f32(lg[e]) : -INFINITY;
     if (e >= E) taken |= 1u << i;
   }
   float sel_v[8];
@@ -383,11 +384,20 @@ __global__ void topk_softmax_kernel(const uint16_t* __restrict__ logits, int64_t
     float sum = 0.0f;
     for (int j = 0; j < K; ++j) sum = round_bf16(__fadd_rn(sum, ex[j]));
     for (int j = 0; j < K; ++j) {
-      weights[m * K + j] = f32_to_bf16_bits(__fdiv_rn(ex[j], sum));
-      indices[m * K + j] = sel_i[j];
+      weights[j] = f32_to_bf16_bits(__fdiv_rn(ex[j], sum));
+      indices[j] = sel_i[j];
+      if (sidx) sidx[j] = sel_i[j];
       if (sel_i[j] < 0 || sel_i[j] >= E) raise_error(err, kErrBadRouting);
     }
   }
+}
+
+__global__ void topk_softmax_kernel(const uint16_t* __restrict__ logits, int64_t M, int32_t E, int32_t K,
+                                    uint16_t* __restrict__ weights, int32_t* __restrict__ indices,
+                                    uint32_t* err) {
+  const int64_t m = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (m >= M) return;
+  topk_softmax_warp(logits + m * E, E, K, weights + m * K, indices + m * K, nullptr, err);
 }
 
 // ------------------------------------------------------ permutation --
@@ -470,6 +480,72 @@ __global__ void __launch_bounds__(1024) moe_place_kernel(const int32_t* __restri
 // optionally converted from bf16 to f16 for the f16 GEMM path (exact for
 // |v| in the f16 normal range, which RMSNorm output stays in when the norm
 // weights pass gptoss_moe_weights_prepare's check).
+// Decode sizes (M * K <= 1024 pairs, E <= 256): top-k + softmax, the
+// expert counts and scan, the token-tile plan and the stable placement in
+// one CTA -- the same results as topk_softmax_kernel, moe_count_scan_kernel
+// and moe_place_kernel, without two launches between them.  A pair's row
+// within its expert counts the earlier pairs with the same expert: within
+// the warp by __match_any_sync, across warps from per-warp counts.
+constexpr int kRouteSmallPairs = 1024;
+__global__ void __launch_bounds__(1024) moe_route_small_kernel(const uint16_t* __restrict__ logits, int64_t M,
+                                                                int32_t E, int32_t K, uint16_t* __restrict__ weights,
+                                                                int32_t* __restrict__ indices,
+                                                                int32_t* __restrict__ indptr,
+                                                                int32_t* __restrict__ tile_ptr,
+                                                                int32_t* __restrict__ tile_rows,
+                                                                int32_t* __restrict__ token_of_row,
+                                                                int32_t* __restrict__ row_of_pair,
+                                                                int32_t* __restrict__ expert_of_row, uint32_t* err) {
+  __shared__ int32_t sidx[kRouteSmallPairs];
+  __shared__ int32_t wcnt[32][256];  // pairs of each expert per warp
+  __shared__ int32_t sptr[257];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t pairs = M * K;
+  for (int64_t m = warp; m < M; m += 32)
+    topk_softmax_warp(logits + m * E, E, K, weights + m * K, indices + m * K, sidx + m * K, err);
+  for (int e = lane; e < E; e += 32) wcnt[warp][e] = 0;
+  __syncthreads();
+  const int i = threadIdx.x;  // one pair per thread
+  const bool live = i < pairs;
+  int32_t e = live ? sidx[i] : -1;
+  const bool ok = live && e >= 0 && e < E;
+  if (!ok) e = -1 - lane;  // a key no valid pair shares
+  const uint32_t same = __match_any_sync(0xffffffffu, e);
+  const int rank_w = __popc(same & ((1u << lane) - 1u));
+  if (ok && rank_w == 0) wcnt[warp][e] = __popc(same);
+  __syncthreads();
+  if ((int)threadIdx.x < E) {  // each expert's total, in parallel
+    int32_t c = 0;
+    for (int w = 0; w < 32; ++w) c += wcnt[w][threadIdx.x];
+    sptr[threadIdx.x] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int32_t tmax = moe_tile_rows_max(pairs, E);
+    int32_t acc = 0, tacc = 0;
+    for (int32_t x = 0; x < E; ++x) {
+      const int32_t c = sptr[x];
+      sptr[x] = acc;
+      indptr[x] = acc;
+      tile_ptr[x] = tacc;
+      const int32_t nt = (c + tmax - 1) / tmax;
+      tile_rows[x] = nt ? ((((c + nt - 1) / nt) + 15) & ~15) : 0;
+      acc += c;
+      tacc += nt;
+    }
+    indptr[E] = acc;
+    tile_ptr[E] = tacc;
+  }
+  __syncthreads();
+  if (ok) {
+    int32_t row = sptr[e] + rank_w;
+    for (int w = 0; w < warp; ++w) row += wcnt[w][e];
+    token_of_row[row] = i / K;
+    row_of_pair[i] = row;
+    expert_of_row[row] = e;
+  }
+}
+
 template <bool kToF16>
 __global__ void gather_rows_kernel(const uint16_t* __restrict__ t, const int32_t* __restrict__ token_of_row,
                                    int64_t rows, int32_t H, uint16_t* __restrict__ act) {
@@ -748,6 +824,18 @@ int launch_permute(const int32_t* idx, int64_t M, int32_t K, int32_t E, int32_t*
   if (pairs > 0) moe_place_kernel<<<E, 1024, 0, s>>>(idx, pairs, K, indptr, token_of_row, row_of_pair, expert_of_row);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
+
+int launch_route_small(const uint16_t* logits, int64_t M, int32_t E, int32_t K, uint16_t* weights,
+                       int32_t* indices, int32_t* indptr, int32_t* tile_ptr, int32_t* tile_rows,
+                       int32_t* token_of_row, int32_t* row_of_pair, int32_t* expert_of_row, uint32_t* err,
+                       cudaStream_t s) {
+  if (M <= 0) return 0;
+  if (M * K > kRouteSmallPairs || E > 256 || K > 8 || K < 1 || K > E) return -12;
+  moe_route_small_kernel<<<1, 1024, 0, s>>>(logits, M, E, K, weights, indices, indptr, tile_ptr, tile_rows,
+                                            token_of_row, row_of_pair, expert_of_row, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : -3;
+}
+int route_small_max_pairs() { return kRouteSmallPairs; }
 
 int launch_gather(const uint16_t* t, const int32_t* token_of_row, int64_t rows, int32_t H, uint16_t* act,
                   int32_t to_f16, cudaStream_t s) {

@@ -289,6 +289,17 @@ int gptoss_sample_top_p_from_logits(const float* logits, int64_t B, int64_t V, d
                                     const double* uniform, double uniform0, void* scratch, int64_t scratch_bytes,
                                     int32_t* tokens, void* stream);
 
+/* The routing half of gptoss_moe_forward for M normalised tokens t (the
+ * output of gptoss_rms_norm): router logits, top-k + softmax and the
+ * expert-major permutation with its token-tile plan -- the outputs of
+ * gptoss_moe_router followed by gptoss_moe_permute, bit for bit.  At decode
+ * sizes (M * top_k <= 256, E <= 256) the part after the logits is one
+ * launch. */
+int gptoss_moe_route(const uint16_t* t, int64_t M, const gptoss_moe_weights* w, uint16_t* logits,
+                     uint16_t* topk_weights, int32_t* topk_indices, int32_t* indptr, int32_t* token_of_row,
+                     int32_t* row_of_pair, int32_t* expert_of_row, int32_t* tile_ptr, int32_t* tile_rows,
+                     uint32_t* err, void* stream);
+
 /* MLPBlock.forward like gptoss_moe_forward, but allocating nothing: no
  * cudaMalloc, no cudaFree, no workspace.  It has no counterpart in the
  * reference.  It is for callers that cannot allocate device memory when the

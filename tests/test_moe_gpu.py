@@ -5,6 +5,8 @@ expert-major permutation and the MXFP4 decode.  Tolerance (bf16): the
 expert GEMM outputs and the block output, with
 max|gpu - ref| / max|ref| <= 2e-2 and cosine >= 0.9995.
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -400,3 +402,47 @@ def test_empty_inputs_and_oversized_calls(params_e8):
         lib.gptoss_moe_workspace_destroy(ws)
         blk.free_workspace()
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("E", [8, 32, 128])
+def test_fused_decode_routing_equals_separate_kernels(E):
+    """gptoss_moe_route (one launch after the logits at decode sizes) gives
+    the same logits, top-k, weights, permutation and tile plan as
+    gptoss_moe_router + gptoss_moe_permute, at sizes on both sides of its
+    256-pair limit, with ties in the logits (a coarse router weight)."""
+    import importlib
+    L = importlib.import_module("gpt-oss-tvm_b200._lib")
+    rng = np.random.default_rng(90 + E)
+    S = synth()
+    H, K = 2880, 4
+    Wg = S.bf16_bits(np.round(rng.standard_normal((E, H)) * 4) / 256)  # few distinct values: ties
+    bg = S.bf16_bits(rng.standard_normal(E).astype(np.float32) * 0.1)
+    w = L.gptoss_moe_weights()
+    w.num_experts = w.num_local_experts = E
+    w.hidden, w.intermediate, w.top_k = H, H, K
+    wd, bd = G.dev(Wg), G.dev(bg)
+    w.gate_weight, w.gate_bias = wd.data_ptr(), bd.data_ptr()
+    for M in (1, 5, 63, 64, 65, 256):
+        t = G.dev(S.bf16_bits(rng.standard_normal((M, H)).astype(np.float32)))
+        i32 = dict(dtype=torch.int32, device="cuda")
+        outs = []
+        for fused in (True, False):
+            o = dict(logits=torch.empty(M, E, dtype=torch.bfloat16, device="cuda"),
+                     w=torch.empty(M, K, dtype=torch.bfloat16, device="cuda"), idx=torch.empty(M, K, **i32),
+                     indptr=torch.empty(E + 1, **i32), tok=torch.empty(M * K, **i32), rev=torch.empty(M * K, **i32),
+                     exr=torch.empty(M * K, **i32), tp=torch.empty(E + 1, **i32), tr=torch.empty(E, **i32))
+            err = torch.zeros(1, **i32)
+            if fused:
+                G.call("gptoss_moe_route", G.P(t), M, ctypes.byref(w), G.P(o["logits"]), G.P(o["w"]), G.P(o["idx"]),
+                       G.P(o["indptr"]), G.P(o["tok"]), G.P(o["rev"]), G.P(o["exr"]), G.P(o["tp"]), G.P(o["tr"]),
+                       G.P(err), G.S())
+            else:
+                G.call("gptoss_moe_router", G.P(t), G.P(wd), G.P(bd), M, E, H, K, G.P(o["logits"]), G.P(o["w"]),
+                       G.P(o["idx"]), G.P(err), G.S())
+                G.call("gptoss_moe_permute", G.P(o["idx"]), M, K, E, G.P(o["indptr"]), G.P(o["tok"]), G.P(o["rev"]),
+                       G.P(o["exr"]), G.P(o["tp"]), G.P(o["tr"]), G.P(err), G.S())
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            outs.append(o)
+        for k in outs[0]:
+            assert torch.equal(outs[0][k], outs[1][k]), f"{k} differs at M={M} E={E}"
