@@ -480,6 +480,223 @@ __global__ void __launch_bounds__(1024) moe_place_kernel(const int32_t* __restri
 // optionally converted from bf16 to f16 for the f16 GEMM path (exact for
 // |v| in the f16 normal range, which RMSNorm output stays in when the norm
 // weights pass gptoss_moe_weights_prepare's check).
+// Permutation by warp ranges (E <= 256).  The pairs are cut into contiguous
+// ranges, one per warp.  Count: each warp counts its range per expert (lanes
+// with one expert found by __match_any_sync, one add per expert and batch
+// of 32 -- no atomics).  Scan: indptr, the tile plan, and each warp's
+// starting row per expert (indptr[e] + the pairs of expert e in the ranges
+// before it).  Place: each warp walks its range again in order, row = its
+// running row of the expert + rank among the batch's lanes of that expert.
+// Rows of one expert come out in pair order -- the stable order of
+// moe_place_kernel -- without every expert's CTA reading every pair.
+constexpr int kPermUnroll = 4;
+
+// Pairs [lo, hi) counted per expert into cnt[0, E) (the warp's own row).
+__device__ __forceinline__ void perm_warp_count(const int32_t* __restrict__ idx, int64_t lo, int64_t hi, int32_t E,
+                                                int32_t* cnt, uint32_t* err) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int e = lane; e < E; e += 32) cnt[e] = 0;
+  __syncwarp();
+  for (int64_t b0 = lo; b0 < hi; b0 += 32 * kPermUnroll) {
+    int32_t ev[kPermUnroll];
+#pragma unroll
+    for (int u = 0; u < kPermUnroll; ++u) {
+      const int64_t i = b0 + u * 32 + lane;
+      ev[u] = i < hi ? idx[i] : INT32_MIN;
+    }
+#pragma unroll
+    for (int u = 0; u < kPermUnroll; ++u) {
+      int32_t e = ev[u];
+      const bool ok = e >= 0 && e < E;
+      if (!ok) {
+        if (e != INT32_MIN) raise_error(err, kErrBadRouting);
+        e = -1 - lane;  // a key that no valid pair shares
+      }
+      const uint32_t same = __match_any_sync(0xffffffffu, e);
+      if (ok && (same & lt) == 0) cnt[e] += __popc(same);
+      __syncwarp();
+    }
+  }
+}
+
+// Pairs [lo, hi) placed from base[0, E) (the warp's own running rows).
+__device__ __forceinline__ void perm_warp_place(const int32_t* __restrict__ idx, int64_t lo, int64_t hi, int32_t K,
+                                                int32_t E, int32_t* base, int32_t* __restrict__ token_of_row,
+                                                int32_t* __restrict__ row_of_pair,
+                                                int32_t* __restrict__ expert_of_row) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t lt = (1u << lane) - 1u;
+  for (int64_t b0 = lo; b0 < hi; b0 += 32 * kPermUnroll) {
+    int32_t ev[kPermUnroll];
+#pragma unroll
+    for (int u = 0; u < kPermUnroll; ++u) {
+      const int64_t i = b0 + u * 32 + lane;
+      ev[u] = i < hi ? idx[i] : INT32_MIN;
+    }
+#pragma unroll
+    for (int u = 0; u < kPermUnroll; ++u) {
+      const int64_t i = b0 + u * 32 + lane;
+      int32_t e = ev[u];
+      const bool ok = e >= 0 && e < E;
+      if (!ok) e = -1 - lane;
+      const uint32_t same = __match_any_sync(0xffffffffu, e);
+      if (ok) {
+        const int32_t row = base[e] + __popc(same & lt);
+        token_of_row[row] = (int32_t)(i / K);
+        row_of_pair[i] = row;
+        expert_of_row[row] = e;
+      }
+      __syncwarp();
+      if (ok && (same & lt) == 0) base[e] += __popc(same);
+      __syncwarp();
+    }
+  }
+}
+
+// The tile plan of an expert with c rows (moe_count_scan_kernel's rule).
+__device__ __forceinline__ void perm_tiles(int32_t c, int32_t tmax, int32_t& nt, int32_t& per) {
+  nt = (c + tmax - 1) / tmax;
+  per = nt ? ((((c + nt - 1) / nt) + 15) & ~15) : 0;
+}
+
+// indptr / tile_ptr / tile_rows from the per-expert counts c (thread e of
+// the first 256 threads; all threads of the block call it).  Returns
+// indptr[e] for thread e < E.
+__device__ __forceinline__ int32_t perm_scan_experts(int32_t c, int32_t E, int64_t pairs, int32_t* __restrict__ indptr,
+                                                     int32_t* __restrict__ tile_ptr, int32_t* __restrict__ tile_rows,
+                                                     int32_t (*wtot)[8]) {
+  const int e = threadIdx.x, warp = e >> 5, lane = e & 31;
+  int32_t nt = 0, per = 0;
+  if (e < E) perm_tiles(c, moe_tile_rows_max(pairs, E), nt, per);
+  int32_t sc = e < E ? c : 0, sn = nt;  // inclusive scans within the warp
+  if (warp < 8) {
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int32_t xc = __shfl_up_sync(0xffffffffu, sc, d), xn = __shfl_up_sync(0xffffffffu, sn, d);
+      if (lane >= d) sc += xc, sn += xn;
+    }
+    if (lane == 31) wtot[0][warp] = sc, wtot[1][warp] = sn;
+  }
+  __syncthreads();
+  int32_t start = 0;
+  if (e < E) {
+    for (int w = 0; w < warp; ++w) sc += wtot[0][w], sn += wtot[1][w];
+    start = sc - c;
+    indptr[e] = start;
+    tile_ptr[e] = sn - nt;
+    tile_rows[e] = per;
+    if (e == E - 1) indptr[E] = sc, tile_ptr[E] = sn;
+  }
+  return start;
+}
+
+// Small pair counts: the three steps in one CTA of 32 warps.
+constexpr int kPermWarps = 32;
+
+__global__ void __launch_bounds__(kPermWarps * 32) moe_permute_onecta_kernel(
+    const int32_t* __restrict__ idx, int64_t pairs, int32_t K, int32_t E, int32_t* __restrict__ indptr,
+    int32_t* __restrict__ tile_ptr, int32_t* __restrict__ tile_rows, int32_t* __restrict__ token_of_row,
+    int32_t* __restrict__ row_of_pair, int32_t* __restrict__ expert_of_row, uint32_t* err) {
+  __shared__ int32_t wcnt[kPermWarps][256];  // counts, then running rows of each (warp, expert)
+  __shared__ int32_t wtot[2][8];
+  const int warp = threadIdx.x >> 5;
+  const int64_t span = ((pairs + kPermWarps * 32 - 1) / (kPermWarps * 32)) * 32;
+  const int64_t lo = (int64_t)warp * span, hi = min(pairs, lo + span);
+  perm_warp_count(idx, lo, hi, E, wcnt[warp], err);
+  __syncthreads();
+  const int e = threadIdx.x;
+  int32_t c = 0;
+  if (e < E)
+    for (int w = 0; w < kPermWarps; ++w) c += wcnt[w][e];
+  const int32_t start = perm_scan_experts(c, E, pairs, indptr, tile_ptr, tile_rows, wtot);
+  if (e < E) {
+    int32_t run = start;
+    for (int w = 0; w < kPermWarps; ++w) {
+      const int32_t k = wcnt[w][e];
+      wcnt[w][e] = run;
+      run += k;
+    }
+  }
+  __syncthreads();
+  perm_warp_place(idx, lo, hi, K, E, wcnt[warp], token_of_row, row_of_pair, expert_of_row);
+}
+
+// Many pairs: the three steps as three launches over kPermRanges-ish warp
+// ranges of 8-warp CTAs.  Range r = [r span, (r + 1) span), the last one
+// running to the end; span >= E, so every range holds at least E pairs, and
+// the range's counts, then its starting rows, live in row_of_pair[r span,
+// r span + E) -- the range's own pairs, which only its own warp overwrites,
+// after reading them.
+constexpr int kPermRangeTarget = 256;
+constexpr int64_t kPermOneCtaMaxPairs = 4096;
+constexpr int kPermRangeWarps = 8;
+
+__host__ __device__ __forceinline__ int64_t perm_span(int64_t pairs, int32_t E) {
+  const int64_t s = (pairs + kPermRangeTarget - 1) / kPermRangeTarget;
+  return ((max(s, (int64_t)E) + 31) / 32) * 32;
+}
+
+__global__ void __launch_bounds__(kPermRangeWarps * 32) moe_perm_count_kernel(const int32_t* __restrict__ idx,
+                                                                              int64_t pairs, int32_t E,
+                                                                              int32_t* __restrict__ row_of_pair,
+                                                                              uint32_t* err) {
+  __shared__ int32_t wcnt[kPermRangeWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t span = perm_span(pairs, E), nr = pairs / span;
+  const int64_t r = (int64_t)blockIdx.x * kPermRangeWarps + warp;
+  if (r >= nr) return;
+  const int64_t lo = r * span, hi = r == nr - 1 ? pairs : lo + span;
+  perm_warp_count(idx, lo, hi, E, wcnt[warp], err);
+  for (int e = lane; e < E; e += 32) row_of_pair[lo + e] = wcnt[warp][e];
+}
+
+// One CTA of 1024 threads: thread (p, e) = (tid / 256, tid % 256) adds up
+// the counts of expert e over the p-th quarter of the ranges.
+__global__ void __launch_bounds__(1024) moe_perm_scan_kernel(int64_t pairs, int32_t E, int32_t* __restrict__ indptr,
+                                                             int32_t* __restrict__ tile_ptr,
+                                                             int32_t* __restrict__ tile_rows,
+                                                             int32_t* __restrict__ row_of_pair) {
+  __shared__ int32_t part[4][256];
+  __shared__ int32_t wtot[2][8];
+  const int e = threadIdx.x & 255, p = threadIdx.x >> 8;
+  const int64_t span = perm_span(pairs, E), nr = pairs / span;
+  const int64_t r0 = nr * p / 4, r1 = nr * (p + 1) / 4;
+  int32_t sum = 0;
+  if (e < E)
+    for (int64_t r = r0; r < r1; ++r) sum += row_of_pair[r * span + e];
+  part[p][e] = sum;
+  __syncthreads();
+  const int32_t c = part[0][e] + part[1][e] + part[2][e] + part[3][e];
+  const int32_t start = perm_scan_experts(threadIdx.x < 256 ? c : 0, E, pairs, indptr, tile_ptr, tile_rows, wtot);
+  __shared__ int32_t first[256];
+  if (threadIdx.x < 256) first[e] = start;
+  __syncthreads();
+  if (e < E) {
+    int32_t run = first[e];
+    for (int q = 0; q < p; ++q) run += part[q][e];
+    for (int64_t r = r0; r < r1; ++r) {
+      const int32_t k = row_of_pair[r * span + e];
+      row_of_pair[r * span + e] = run;
+      run += k;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kPermRangeWarps * 32) moe_perm_place_kernel(
+    const int32_t* __restrict__ idx, int64_t pairs, int32_t K, int32_t E, int32_t* __restrict__ token_of_row,
+    int32_t* __restrict__ row_of_pair, int32_t* __restrict__ expert_of_row) {
+  __shared__ int32_t base[kPermRangeWarps][256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t span = perm_span(pairs, E), nr = pairs / span;
+  const int64_t r = (int64_t)blockIdx.x * kPermRangeWarps + warp;
+  if (r >= nr) return;
+  const int64_t lo = r * span, hi = r == nr - 1 ? pairs : lo + span;
+  for (int e = lane; e < E; e += 32) base[warp][e] = row_of_pair[lo + e];
+  __syncwarp();
+  perm_warp_place(idx, lo, hi, K, E, base[warp], token_of_row, row_of_pair, expert_of_row);
+}
+
 // Decode sizes (M * K <= 1024 pairs, E <= 256): top-k + softmax, the
 // expert counts and scan, the token-tile plan and the stable placement in
 // one CTA -- the same results as topk_softmax_kernel, moe_count_scan_kernel
@@ -820,6 +1037,20 @@ int launch_permute(const int32_t* idx, int64_t M, int32_t K, int32_t E, int32_t*
                    int32_t* tile_rows, int32_t* token_of_row, int32_t* row_of_pair, int32_t* expert_of_row,
                    uint32_t* err, cudaStream_t s) {
   const int64_t pairs = M * K;
+  if (E <= 256 && pairs > kPermOneCtaMaxPairs) {
+    const int64_t nr = pairs / perm_span(pairs, E);
+    const unsigned grid = (unsigned)((nr + kPermRangeWarps - 1) / kPermRangeWarps);
+    moe_perm_count_kernel<<<grid, kPermRangeWarps * 32, 0, s>>>(idx, pairs, E, row_of_pair, err);
+    moe_perm_scan_kernel<<<1, 1024, 0, s>>>(pairs, E, indptr, tile_ptr, tile_rows, row_of_pair);
+    moe_perm_place_kernel<<<grid, kPermRangeWarps * 32, 0, s>>>(idx, pairs, K, E, token_of_row, row_of_pair,
+                                                                 expert_of_row);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
+  if (E <= 256) {
+    moe_permute_onecta_kernel<<<1, kPermWarps * 32, 0, s>>>(idx, pairs, K, E, indptr, tile_ptr, tile_rows, token_of_row,
+                                                 row_of_pair, expert_of_row, err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
   moe_count_scan_kernel<<<1, 1024, (size_t)E * 4, s>>>(idx, pairs, E, indptr, tile_ptr, tile_rows, err);
   if (pairs > 0) moe_place_kernel<<<E, 1024, 0, s>>>(idx, pairs, K, indptr, token_of_row, row_of_pair, expert_of_row);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;

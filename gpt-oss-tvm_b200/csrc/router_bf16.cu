@@ -88,44 +88,84 @@ __device__ __forceinline__ uint32_t dup_lo(uint32_t x) { return prmt(x, x, 0x101
 __device__ __forceinline__ uint32_t dup_hi(uint32_t x) { return prmt(x, x, 0x3232u); }
 
 // =====================================================================
-// Throughput form (many tokens).  A CTA covers btok tokens x kBE experts;
-// a thread owns 2 tokens x 8 experts = 8 packed chain pairs (adjacent
-// experts share a register).  Per stage of kRbK k values the token values
-// are staged duplicated ({t, t} words, k-major) and the expert values as
-// pairs ({w_e, w_e+1} words, k-major), with the largest |t| and |w| of the
-// stage per row for the bounds.
-constexpr int kRbK = 32;
-constexpr int kRbParts = kRbK / 8;  // 16-byte pieces per row per stage
+// Throughput form (many tokens).  A CTA covers kTok tokens x kBE experts;
+// a thread owns kTT (1 or 2) tokens x 8 experts = 4 kTT packed chain pairs
+// (adjacent experts share a register).  Per stage of kK k values the token
+// values are staged duplicated ({t, t} words, k-major) and the expert values
+// as pairs ({w_e, w_e+1} words, k-major), with the largest |t| and |w| of
+// each 8-value piece of a row for the bounds.
+//
+// The stage's bound test runs first for the thread as a whole: one bound
+// from the largest exponents of its tokens and experts, against the
+// smallest |accumulator| of all its chains -- a superset of the per-chain
+// tests, with the per-chain form (and the reruns) only behind it.
 
-template <int kBE>
+// 16-bit lane-wise max / min of non-negative bf16 bit patterns (the integer
+// order is the numeric order there).
+__device__ __forceinline__ uint32_t rb_max2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t rb_min2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("min.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// Zero halves raised to 0xFFFF (out of the way of a minimum over nonzeros).
+__device__ __forceinline__ uint32_t rb_nz(uint32_t x) { return x | __vcmpeq2(x, 0u); }
+
+// The thread-wide test.  tw: halves = stage maxima of the thread's tokens
+// (kTT = 1: the high half is 0); w4: halves = stage maxima of its 8
+// experts; mn_min: the smallest |accumulator| (bf16 bits) of its chains.
+// True when some chain of the thread may need the rerun: a nonzero product
+// whose bound rb_bound makes "always" (subnormal maxima, exponent sums
+// below 158 or above 354) or an accumulator at or below the largest bound.
+__device__ __forceinline__ bool rb_thread_flag(uint32_t tw, const uint32_t (&w4)[4], uint32_t mn_min) {
+  const uint32_t wmx = rb_max2(rb_max2(w4[0], w4[1]), rb_max2(w4[2], w4[3]));
+  const uint32_t tmax = max(tw & 0xFFFFu, tw >> 16), wmax = max(wmx & 0xFFFFu, wmx >> 16);
+  if (tmax == 0 || wmax == 0) return false;  // every product of the stage is zero
+  const uint32_t wn = rb_min2(rb_min2(rb_nz(w4[0]), rb_nz(w4[1])), rb_min2(rb_nz(w4[2]), rb_nz(w4[3])));
+  const uint32_t tn2 = rb_nz(tw);
+  const int etn = (int)(min(tn2 & 0xFFFFu, tn2 >> 16) >> 7), ewn = (int)(min(wn & 0xFFFFu, wn >> 16) >> 7);
+  const int et = (int)(tmax >> 7), ew = (int)(wmax >> 7);
+  if (etn == 0 || ewn == 0 || etn + ewn < 158 || et + ew > 254 + 100) return true;
+  return mn_min <= (uint32_t)(et + ew - 150) << 7;
+}
+
+template <int kBE, int kTT, int kK>
 struct RbCfg {
-  static constexpr int kEGroups = kBE / 8;            // expert groups of 8 per CTA
-  static constexpr int kTGroups = 128 / kEGroups;     // token groups of 2 per CTA
-  static constexpr int kTok = 2 * kTGroups;           // tokens per CTA
+  static constexpr int kParts = kK / 8;                // 16-byte pieces per row per stage
+  static constexpr int kEGroups = kBE / 8;             // expert groups of 8 per CTA
+  static constexpr int kTGroups = 128 / kEGroups;      // token groups of kTT per CTA
+  static constexpr int kTok = kTT * kTGroups;          // tokens per CTA
   static constexpr int kPairs = kBE / 2;
-  static constexpr int kTPitch = kTok + 2;            // words per staged k row (8-byte aligned rows)
-  static constexpr int kWPitch = kPairs + 4;          // words per staged k row (16-byte aligned rows)
-  static constexpr int kTPieces = kTok * kRbParts / 128;  // token pieces per thread
-  static constexpr int kWPieces = kPairs * kRbParts;      // pair pieces per CTA (<= 128)
+  static constexpr int kTPitch = kTok + 2;             // words per staged k row (8-byte aligned rows)
+  static constexpr int kWPitch = kPairs + 4;           // words per staged k row (16-byte aligned rows)
+  static constexpr int kTPieces = kTok * kParts / 128;  // token pieces per thread
+  static constexpr int kWAll = kPairs * kParts;         // pair pieces per CTA
+  static constexpr int kWPieces = (kWAll + 127) / 128;  // pair pieces per thread (the last may be partial)
   static_assert(kBE == 8 || kBE == 16 || kBE == 32 || kBE == 64, "experts per CTA");
+  static_assert((kTT == 1 || kTT == 2) && kTPieces >= 1 && kTok * kParts % 128 == 0, "tokens per thread");
+  static_assert(kK == 32 || kK == 64, "stage depth");
 };
 
-template <int kBE>
+template <int kBE, int kTT, int kK>
 __global__ void __launch_bounds__(128) router_bf16_kernel(const uint16_t* __restrict__ t,
                                                           const uint16_t* __restrict__ W,
                                                           const uint16_t* __restrict__ b, int64_t M, int32_t E,
                                                           int32_t H, uint16_t* __restrict__ logits) {
-  using C = RbCfg<kBE>;
-  __shared__ __align__(16) uint32_t ts[kRbK][C::kTPitch];
-  __shared__ __align__(16) uint32_t ws[kRbK][C::kWPitch];
-  __shared__ uint16_t tmx[kRbParts][C::kTok];
-  __shared__ uint16_t wmx[kRbParts][kBE];
+  using C = RbCfg<kBE, kTT, kK>;
+  __shared__ __align__(16) uint32_t ts[kK][C::kTPitch];
+  __shared__ __align__(16) uint32_t ws[kK][C::kWPitch];
+  __shared__ __align__(16) uint16_t tmx[C::kParts][C::kTok];
+  __shared__ __align__(16) uint16_t wmx[C::kParts][kBE];
   const int tid = threadIdx.x;
   const int tg = tid % C::kTGroups, eg = tid / C::kTGroups;
   const int64_t tok0 = (int64_t)blockIdx.x * C::kTok;
   const int32_t e0 = blockIdx.y * kBE;
 
-  uint4 tq[C::kTPieces], wq0 = make_uint4(0, 0, 0, 0), wq1 = make_uint4(0, 0, 0, 0);
+  uint4 tq[C::kTPieces], wq0[C::kWPieces], wq1[C::kWPieces];
   auto load_stage = [&](int32_t k0) {
 #pragma unroll
     for (int q = 0; q < C::kTPieces; ++q) {
@@ -135,13 +175,15 @@ __global__ void __launch_bounds__(128) router_bf16_kernel(const uint16_t* __rest
       tq[q] = make_uint4(0, 0, 0, 0);
       if (m < M && k0 + part * 8 < H) tq[q] = *(const uint4*)(t + m * H + k0 + part * 8);
     }
-    if (tid < C::kWPieces) {
-      const int pr = tid % C::kPairs, part = tid / C::kPairs;
+#pragma unroll
+    for (int q = 0; q < C::kWPieces; ++q) {
+      const int j = tid + 128 * q;
+      const int pr = j % C::kPairs, part = j / C::kPairs;
       const int32_t e = e0 + 2 * pr;
-      wq0 = wq1 = make_uint4(0, 0, 0, 0);
-      if (k0 + part * 8 < H) {
-        wq0 = *(const uint4*)(W + (int64_t)e * H + k0 + part * 8);
-        wq1 = *(const uint4*)(W + (int64_t)(e + 1) * H + k0 + part * 8);
+      wq0[q] = wq1[q] = make_uint4(0, 0, 0, 0);
+      if (j < C::kWAll && k0 + part * 8 < H) {
+        wq0[q] = *(const uint4*)(W + (int64_t)e * H + k0 + part * 8);
+        wq1[q] = *(const uint4*)(W + (int64_t)(e + 1) * H + k0 + part * 8);
       }
     }
   };
@@ -161,88 +203,118 @@ __global__ void __launch_bounds__(128) router_bf16_kernel(const uint16_t* __rest
       mx &= 0x7FFF7FFFu;
       tmx[part][tok] = (uint16_t)max(mx & 0xFFFFu, mx >> 16);
     }
-    if (tid < C::kWPieces) {
-      const int pr = tid % C::kPairs, part = tid / C::kPairs;
-      const uint32_t a[4] = {wq0.x, wq0.y, wq0.z, wq0.w}, c[4] = {wq1.x, wq1.y, wq1.z, wq1.w};
-      uint32_t ma = 0, mc = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        ws[part * 8 + 2 * i][pr] = prmt(a[i], c[i], 0x5410u);      // {w_e[k], w_e+1[k]}
-        ws[part * 8 + 2 * i + 1][pr] = prmt(a[i], c[i], 0x7632u);  // {w_e[k+1], w_e+1[k+1]}
-        rb_absmax(ma, a[i]);
-        rb_absmax(mc, c[i]);
+    for (int q = 0; q < C::kWPieces; ++q) {
+      const int j = tid + 128 * q;
+      if (j < C::kWAll) {
+        const int pr = j % C::kPairs, part = j / C::kPairs;
+        const uint32_t a[4] = {wq0[q].x, wq0[q].y, wq0[q].z, wq0[q].w};
+        const uint32_t c[4] = {wq1[q].x, wq1[q].y, wq1[q].z, wq1[q].w};
+        uint32_t ma = 0, mc = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          ws[part * 8 + 2 * i][pr] = prmt(a[i], c[i], 0x5410u);      // {w_e[k], w_e+1[k]}
+          ws[part * 8 + 2 * i + 1][pr] = prmt(a[i], c[i], 0x7632u);  // {w_e[k+1], w_e+1[k+1]}
+          rb_absmax(ma, a[i]);
+          rb_absmax(mc, c[i]);
+        }
+        ma &= 0x7FFF7FFFu;
+        mc &= 0x7FFF7FFFu;
+        wmx[part][2 * pr] = (uint16_t)max(ma & 0xFFFFu, ma >> 16);
+        wmx[part][2 * pr + 1] = (uint16_t)max(mc & 0xFFFFu, mc >> 16);
       }
-      ma &= 0x7FFF7FFFu;
-      mc &= 0x7FFF7FFFu;
-      wmx[part][2 * pr] = (uint16_t)max(ma & 0xFFFFu, ma >> 16);
-      wmx[part][2 * pr + 1] = (uint16_t)max(mc & 0xFFFFu, mc >> 16);
+    }
+  };
+  auto load_t = [&](int kk, uint32_t (&t2)[kTT]) {
+    if constexpr (kTT == 2) {
+      const uint2 tv = *(const uint2*)&ts[kk][2 * tg];
+      t2[0] = tv.x;
+      t2[1] = tv.y;
+    } else {
+      t2[0] = ts[kk][tg];
     }
   };
 
-  uint32_t acc[2][4];
+  uint32_t acc[kTT][4];
   load_stage(0);
-  for (int32_t k0 = 0; k0 < H; k0 += kRbK) {
+  for (int32_t k0 = 0; k0 < H; k0 += kK) {
     __syncthreads();
     store_stage();
     __syncthreads();
-    if (k0 + kRbK < H) load_stage(k0 + kRbK);  // the next stage's loads overlap this stage's chains
-    const int32_t kn = min(kRbK, H - k0);
+    if (k0 + kK < H) load_stage(k0 + kK);  // the next stage's loads overlap this stage's chains
+    const int32_t kn = min(kK, H - k0);
     int32_t kk0 = 0;
     if (k0 == 0) {
-      const uint2 tv = *(const uint2*)&ts[0][2 * tg];
+      uint32_t t2[kTT];
+      load_t(0, t2);
       const uint4 wv = *(const uint4*)&ws[0][4 * eg];
-      const uint32_t t2[2] = {tv.x, tv.y}, w2[4] = {wv.x, wv.y, wv.z, wv.w};
+      const uint32_t w2[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < kTT; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = rb_first(t2[i], w2[j]);
       kk0 = 1;
     }
-    uint32_t save[2][4], mn[2][4];
+    uint32_t save[kTT][4], mn[kTT][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < kTT; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         save[i][j] = acc[i][j];
         mn[i][j] = kBf16InfPair;
       }
     for (int32_t kk = kk0; kk < kn; ++kk) {
-      const uint2 tv = *(const uint2*)&ts[kk][2 * tg];
+      uint32_t t2[kTT];
+      load_t(kk, t2);
       const uint4 wv = *(const uint4*)&ws[kk][4 * eg];
-      const uint32_t t2[2] = {tv.x, tv.y}, w2[4] = {wv.x, wv.y, wv.z, wv.w};
+      const uint32_t w2[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-      for (int i = 0; i < 2; ++i)
+      for (int i = 0; i < kTT; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) rb_step(acc[i][j], mn[i][j], t2[i], w2[j]);
     }
-    // the stage's bounds; a chain pair that may have met the double-rounding
-    // case reruns the stage with the reference's two roundings
+    // the stage's bounds: the thread-wide test, then per chain pair; a chain
+    // pair that may have met the double-rounding case reruns the stage with
+    // the reference's two roundings
+    uint32_t tw = 0, w4[4] = {0, 0, 0, 0}, mall = kBf16InfPair;
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int tok = 2 * tg + i;
-      uint32_t tm = 0;
+    for (int pp = 0; pp < C::kParts; ++pp) {
+      if constexpr (kTT == 2) {
+        tw = rb_max2(tw, *(const uint32_t*)&tmx[pp][2 * tg]);
+      } else {
+        tw = rb_max2(tw, (uint32_t)tmx[pp][tg]);
+      }
+      const uint4 wv = *(const uint4*)&wmx[pp][8 * eg];
+      w4[0] = rb_max2(w4[0], wv.x);
+      w4[1] = rb_max2(w4[1], wv.y);
+      w4[2] = rb_max2(w4[2], wv.z);
+      w4[3] = rb_max2(w4[3], wv.w);
+    }
 #pragma unroll
-      for (int pp = 0; pp < kRbParts; ++pp) tm = max(tm, (uint32_t)tmx[pp][tok]);
+    for (int i = 0; i < kTT; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int el = 8 * eg + 2 * j;
-        uint32_t wa = 0, wb = 0;
+      for (int j = 0; j < 4; ++j) asm("min.xorsign.abs.bf16x2 %0, %0, %1;" : "+r"(mall) : "r"(mn[i][j]));
+    mall &= 0x7FFF7FFFu;
+    if (rb_thread_flag(tw, w4, min(mall & 0xFFFFu, mall >> 16))) {
 #pragma unroll
-        for (int pp = 0; pp < kRbParts; ++pp) {
-          wa = max(wa, (uint32_t)wmx[pp][el]);
-          wb = max(wb, (uint32_t)wmx[pp][el + 1]);
-        }
-        if (rb_flag(mn[i][j], rb_bound(tm, wa), rb_bound(tm, wb))) {
-          uint32_t a = save[i][j];
-          for (int32_t kk = kk0; kk < kn; ++kk) a = rb_step_exact(a, ts[kk][tok], ws[kk][4 * eg + j]);
-          acc[i][j] = a;
+      for (int i = 0; i < kTT; ++i) {
+        const int tok = kTT * tg + i;
+        const uint32_t tm = kTT == 2 ? (i ? tw >> 16 : tw & 0xFFFFu) : tw;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t wpair = w4[j];
+          if (rb_flag(mn[i][j], rb_bound(tm, wpair & 0xFFFFu), rb_bound(tm, wpair >> 16))) {
+            uint32_t a = save[i][j];
+            for (int32_t kk = kk0; kk < kn; ++kk) a = rb_step_exact(a, ts[kk][tok], ws[kk][4 * eg + j]);
+            acc[i][j] = a;
+          }
         }
       }
     }
   }
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int64_t m = tok0 + 2 * tg + i;
+  for (int i = 0; i < kTT; ++i) {
+    const int64_t m = tok0 + kTT * tg + i;
     if (m >= M) continue;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -412,21 +484,24 @@ __global__ void __launch_bounds__(kRcThreads, 1) router_bf16_chain_kernel(const 
 }
 
 // ------------------------------------------------------------------ host --
-constexpr int64_t kRbChainMaxTokens = 512;
 
-template <int kBE>
+template <int kBE, int kTT, int kK>
 static void launch_rb(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H,
                       uint16_t* logits, cudaStream_t s) {
-  using C = RbCfg<kBE>;
+  using C = RbCfg<kBE, kTT, kK>;
   dim3 grid((unsigned)((M + C::kTok - 1) / C::kTok), (unsigned)(E / kBE));
-  router_bf16_kernel<kBE><<<grid, 128, 0, s>>>(t, W, b, M, E, H, logits);
+  router_bf16_kernel<kBE, kTT, kK><<<grid, 128, 0, s>>>(t, W, b, M, E, H, logits);
 }
 
 int launch_router_bf16(const uint16_t* t, const uint16_t* W, const uint16_t* b, int64_t M, int32_t E, int32_t H,
                        uint16_t* logits, uint32_t* err, cudaStream_t s) {
   if (M <= 0) return 0;
   if (E % 8 || E > 1024 || H % 8 || H <= 0 || ((uintptr_t)t & 15) || ((uintptr_t)W & 15)) return -12;
-  if (M <= kRbChainMaxTokens && H <= kRcMaxH) {
+  // The latency form while its CTAs (one per SM) fit in two waves; past
+  // that the throughput form, whose time grows more slowly with M.
+  const int64_t sms = device_sm_count();
+  const int64_t chain_ctas = ((E + kRcExp - 1) / kRcExp) * ((M + kRcTok - 1) / kRcTok);
+  if (chain_ctas <= 2 * sms && H <= kRcMaxH) {
     static bool attr = false;
     if (!attr) {
       cudaFuncSetAttribute(router_bf16_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -435,14 +510,23 @@ int launch_router_bf16(const uint16_t* t, const uint16_t* W, const uint16_t* b, 
     }
     dim3 grid((unsigned)((E + kRcExp - 1) / kRcExp), (unsigned)((M + kRcTok - 1) / kRcTok));
     router_bf16_chain_kernel<<<grid, kRcThreads, rc_smem_bytes(H), s>>>(t, W, b, M, E, H, logits, err);
-  } else if (E % 64 == 0) {
-    launch_rb<64>(t, W, b, M, E, H, logits, s);
-  } else if (E % 32 == 0) {
-    launch_rb<32>(t, W, b, M, E, H, logits, s);
-  } else if (E % 16 == 0) {
-    launch_rb<16>(t, W, b, M, E, H, logits, s);
   } else {
-    launch_rb<8>(t, W, b, M, E, H, logits, s);
+    // two tokens a thread (each staged value feeds more chains) once that
+    // gives 1.5 CTAs per SM; one token a thread (twice the CTAs) below that
+    auto ctas = [&](int be, int tt) { return ((M + tt * 1024 / be - 1) / (tt * 1024 / be)) * (E / be); };
+    if (E % 64 == 0 && 2 * ctas(64, 2) >= 3 * sms) {
+      launch_rb<64, 2, 64>(t, W, b, M, E, H, logits, s);
+    } else if (E % 32 == 0 && 2 * ctas(32, 2) >= 3 * sms) {
+      launch_rb<32, 2, 64>(t, W, b, M, E, H, logits, s);
+    } else if (E % 32 == 0) {
+      launch_rb<32, 1, 64>(t, W, b, M, E, H, logits, s);
+    } else if (E % 16 == 0 && 2 * ctas(16, 2) >= 3 * sms) {
+      launch_rb<16, 2, 64>(t, W, b, M, E, H, logits, s);
+    } else if (E % 16 == 0) {
+      launch_rb<16, 1, 64>(t, W, b, M, E, H, logits, s);
+    } else {
+      launch_rb<8, 1, 32>(t, W, b, M, E, H, logits, s);
+    }
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }

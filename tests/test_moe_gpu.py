@@ -446,3 +446,73 @@ def test_fused_decode_routing_equals_separate_kernels(E):
             outs.append(o)
         for k in outs[0]:
             assert torch.equal(outs[0][k], outs[1][k]), f"{k} differs at M={M} E={E}"
+
+
+def _tile_plan(indptr, pairs, E):
+    """The tile plan gptoss_moe_permute documents: at most 32 rows a tile when
+    pairs <= 8 E, else 160; an expert's rows split evenly over its tiles,
+    rounded up to 16."""
+    c = np.diff(indptr.astype(np.int64))
+    tmax = 32 if pairs <= 8 * E else 160
+    nt = (c + tmax - 1) // tmax
+    per = np.where(nt > 0, ((-(-c // np.maximum(nt, 1))) + 15) // 16 * 16, 0)
+    return np.concatenate([[0], np.cumsum(nt)]).astype(np.int32), per.astype(np.int32)
+
+
+@pytest.mark.parametrize("E", [8, 32, 128, 256, 300])
+def test_permutation_matches_oracle_at_all_sizes(oracle, E):
+    """gptoss_moe_permute against the oracle's stable sort of the pairs by
+    expert, from no tokens to 20000 (80000 pairs), with uniform, skewed (one
+    expert holding every pair) and sparse (few experts used) routings; E = 300
+    takes the two-kernel path for more than 256 experts."""
+    rng = np.random.default_rng(E)
+    K = 4
+    for M in (0, 1, 7, 33, 257, 1000, 8192, 20000):
+        for kind in ("uniform", "one", "sparse"):
+            if kind == "uniform":
+                idx = rng.integers(0, E, (M, K))
+            elif kind == "one":
+                idx = np.full((M, K), E - 1)
+            else:
+                idx = rng.choice(np.array([0, E // 2, E - 1]), (M, K))
+            idx = idx.astype(np.int32)
+            i32 = dict(dtype=torch.int32, device="cuda")
+            n = M * K
+            d = dict(indptr=torch.full((E + 1,), -7, **i32), tok=torch.full((max(n, 1),), -7, **i32),
+                     rev=torch.full((max(n, 1),), -7, **i32), exr=torch.full((max(n, 1),), -7, **i32),
+                     tp=torch.full((E + 1,), -7, **i32), tr=torch.full((E,), -7, **i32))
+            err = torch.zeros(1, **i32)
+            idx_d = G.dev(idx) if n else torch.empty(1, **i32)
+            G.call("gptoss_moe_permute", G.P(idx_d), M, K, E, G.P(d["indptr"]), G.P(d["tok"]), G.P(d["rev"]),
+                   G.P(d["exr"]), G.P(d["tp"]), G.P(d["tr"]), G.P(err), G.S())
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            h = {k: v.cpu().numpy() for k, v in d.items()}
+            indptr, tok, rev, exr = oracle.moe_permute(idx.reshape(M, K), E)
+            what = f"E={E} M={M} {kind}"
+            np.testing.assert_array_equal(h["indptr"], indptr, err_msg=what)
+            np.testing.assert_array_equal(h["tok"][:n], tok, err_msg=what)
+            np.testing.assert_array_equal(h["rev"][:n], rev, err_msg=what)
+            np.testing.assert_array_equal(h["exr"][:n], exr, err_msg=what)
+            tp, tr = _tile_plan(indptr, n, E)
+            np.testing.assert_array_equal(h["tp"], tp, err_msg=what)
+            np.testing.assert_array_equal(h["tr"], tr, err_msg=what)
+
+
+@pytest.mark.parametrize("E", [32, 300])
+def test_permutation_flags_expert_indices_out_of_range(E):
+    """An expert index outside [0, E) sets the routing error bit; the valid
+    pairs are still placed."""
+    i32 = dict(dtype=torch.int32, device="cuda")
+    M, K = 50, 4
+    idx = np.random.default_rng(3).integers(0, E, (M, K)).astype(np.int32)
+    idx[7, 2] = E
+    idx[40, 0] = -1
+    n = M * K
+    d = [torch.zeros(E + 1, **i32), torch.zeros(n, **i32), torch.zeros(n, **i32), torch.zeros(n, **i32),
+         torch.zeros(E + 1, **i32), torch.zeros(E, **i32)]
+    err = torch.zeros(1, **i32)
+    G.call("gptoss_moe_permute", G.P(G.dev(idx)), M, K, E, *[G.P(x) for x in d], G.P(err), G.S())
+    torch.cuda.synchronize()
+    assert int(err.item()) & (1 << 3)
+    assert int(d[0][E].item()) == n - 2

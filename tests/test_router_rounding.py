@@ -8,8 +8,8 @@ more than 2^23 times smaller.  These inputs build that case on purpose:
 exact cancellations leave acc = +-2^-8, the next product is a midpoint
 (1.5 * 2^8 x 1.359375 * 2^7 = 66816, between 66560 and 67072; and
 1.5 * 2^8 x 1.390625 * 2^7 = 68352, tie going up), placed at the start of a
-chain, across the 32-wide stages of the many-token kernel and the 256-wide
-chunks of the few-token kernel, and at the end of the row; plus rows drawn
+chain, across the 32- and 64-wide stages of the many-token kernel and the
+256-wide chunks of the few-token kernel, and at the end of the row; plus rows drawn
 from a small set of such values at random.
 
 CPU: the oracle (two roundings) differs from a one-rounding emulation on the
@@ -27,7 +27,7 @@ PATTERNS = [
     [(1.0, -1.0), (1.0, 0.99609375), (384.0, 178.0)],    # acc = -2^-8, M = 68352: two roundings go up
     [(-1.0, 1.0), (1.0, 0.99609375), (-384.0, 174.0)],   # mirrored
 ]
-OFFSETS = [0, 30, 31, 254, 255, 1000, H - 3]
+OFFSETS = [0, 30, 31, 62, 63, 254, 255, 1000, H - 3]
 
 
 def _bits(x):
@@ -106,19 +106,27 @@ def test_crafted_chains_differ_between_one_and_two_roundings(oracle):
     assert total == len(PATTERNS) * len(OFFSETS) and differ == total, (differ, total)
 
 
+# Token counts past the few-token kernel's limit (its CTAs, one per 16
+# tokens x 16 experts, fill two waves of 148 SMs up to 4736 tokens at E = 8),
+# where each shape of the many-token kernel runs: one token a thread, and
+# two (E = 32 and 48 at 20000 tokens, E = 128 at 5000).
+MANY = {8: (5000,), 16: (5000,), 32: (5000, 20000), 48: (5000, 20000), 128: (2000, 5000)}
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("E", [8, 32, 128])
+@pytest.mark.parametrize("E", [8, 16, 32, 48, 128])
 def test_router_kernels_bit_exact_on_double_rounding_cases(oracle, E):
     torch = pytest.importorskip("torch")
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
     import gpu_util as G
     cases = crafted(E=E, seed=E)
-    for M in (5, 600):  # the few-token kernel and the many-token kernel
+    cases.append(random_nice(5, E, seed=5 + E))  # the few-token kernel
+    for M in MANY[E]:  # the many-token kernel
         cases.append(random_nice(M, E, seed=M + E))
-    # the crafted rows also through the many-token kernel (> 512 tokens)
-    for t0, w0 in crafted(E=E, seed=E + 1):
-        cases.append((np.concatenate([t0] * (600 // t0.shape[0] + 1))[:600], w0))
+        # the crafted rows again, repeated down the tokens
+        for t0, w0 in crafted(E=E, seed=E + 1):
+            cases.append((np.concatenate([t0] * (M // t0.shape[0] + 1))[:M], w0))
     for t, w in cases:
         M = t.shape[0]
         b = _bits(np.random.default_rng(M).standard_normal(E).astype(np.float32) * 0.1)
