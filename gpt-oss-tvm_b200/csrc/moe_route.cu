@@ -83,6 +83,143 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(const uint16_t* __restrict
   }
 }
 
+// Streaming form: every row's chain starts as soon as its first 256 values
+// are in.  A CTA takes rows_per_cta (<= 32) rows; lane r of warp 0 runs row
+// r's serial sum over `stages` chunk slots, each chunk of each row one bulk
+// copy on the slot's mbarrier.  Few rows per CTA (decode): one slot per
+// chunk, the rows stay resident and the block writes the normalised rows
+// from shared memory.  Many rows: a ring of kNsStages slots, each refilled
+// by the same warp once its lanes have read it, so up to 32 rows per CTA
+// and three CTAs per SM run their chains at once (all 8192 rows of a
+// prefill in one wave); the block then writes the normalised rows from a
+// second, L2-resident read of x.
+constexpr int kNsChunk = 256;                // values per row per stage
+constexpr int kNsStages = 4;                 // ring slots
+constexpr int kNsMaxSlots = 16;              // resident rows: H <= 4096
+constexpr int kNsResidentBytes = 100 * 1024;
+constexpr int kNsMaxRows = 32;
+constexpr int kNsPitch = kNsChunk * 2 + 16;  // bytes per row slot: rows start 4 banks apart
+
+__global__ void __launch_bounds__(128) rmsnorm_stream_kernel(const uint16_t* __restrict__ x,
+                                                              const uint16_t* __restrict__ w, int64_t M, int32_t H,
+                                                              int32_t rows_per_cta, int32_t stages, float eps,
+                                                              uint16_t* __restrict__ out, uint32_t* err) {
+  extern __shared__ __align__(128) uint8_t ns_smem[];  // [stages][rows_per_cta][kNsPitch]
+  __shared__ uint64_t bar[kNsMaxSlots];
+  __shared__ float rs[kNsMaxRows];
+  __shared__ int all_ok;
+  const int64_t m0 = (int64_t)blockIdx.x * rows_per_cta;
+  const int nrows = (int)min64(rows_per_cta, M - m0);
+  const int nch = (H + kNsChunk - 1) / kNsChunk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x < stages) mbar_init(&bar[threadIdx.x], 1);
+  if (threadIdx.x == 0) all_ok = 1;
+  fence_mbar_init();
+  __syncthreads();
+  if (warp == 0) {
+    auto slot_row = [&](int c, int r) { return ns_smem + ((size_t)(c % stages) * rows_per_cta + r) * kNsPitch; };
+    auto issue = [&](int c) {
+      const int32_t k0 = c * kNsChunk;
+      const uint32_t bytes = (uint32_t)min(kNsChunk, H - k0) * 2;
+      uint64_t* b = &bar[c % stages];
+      if (lane == 0) mbar_arrive_expect_tx(b, bytes * (uint32_t)nrows);
+      if (lane < nrows)
+        asm volatile(
+            "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                smem_u32(slot_row(c, lane))),
+            "l"(x + (m0 + lane) * H + k0), "r"(bytes), "r"(smem_u32(b))
+            : "memory");
+    };
+    const int first = min(nch, stages);
+    for (int c = 0; c < first; ++c) issue(c);
+    int issued = first, c = 0;
+    bool ok = true;
+    float ss = 0.0f;
+    for (; c < nch; ++c) {
+      // (warp-uniform: every lane leaves the loop together)
+      if (!__all_sync(0xffffffffu, mbar_wait(&bar[c % stages], (uint32_t)(c / stages) & 1u, err,
+                                             kErrTimeoutOther))) {
+        ok = false;
+        break;
+      }
+      if (lane < nrows) {
+        const uint4* row = (const uint4*)slot_row(c, lane);
+        const int n8 = min(kNsChunk, H - c * kNsChunk) / 8;
+        uint4 vn = row[0];
+        for (int k8 = 0; k8 < n8; ++k8) {
+          const uint4 v = vn;
+          if (k8 + 1 < n8) vn = row[k8 + 1];
+          const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float a = __uint_as_float(wv[q] << 16), bb = __uint_as_float(wv[q] & 0xFFFF0000u);
+            ss = __fadd_rn(ss, __fmul_rn(a, a));
+            ss = __fadd_rn(ss, __fmul_rn(bb, bb));
+          }
+        }
+      }
+      __syncwarp();
+      if (c + stages < nch) {
+        // the slot's reads (generic proxy) before the next bulk copy into it (async proxy)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(c + stages);
+        ++issued;
+      }
+    }
+    if (!ok) {
+      // copies still in flight land before the CTA leaves (bounded waits)
+      for (int d = c + 1; d < issued; ++d) mbar_wait(&bar[d % stages], (uint32_t)(d / stages) & 1u, err,
+                                                     kErrTimeoutOther);
+      if (lane == 0) all_ok = 0;
+    }
+    if (lane < nrows) rs[lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)H), eps)));
+  }
+  __syncthreads();
+  if (!all_ok) return;
+  if (stages >= nch)  // resident rows: every thread sees the copies' completion itself
+    for (int c = 0; c < nch; ++c) mbar_wait(&bar[c], 0u, err, kErrTimeoutOther);
+  // the CTA's rows are contiguous in x and out: one flat loop over their
+  // 16-byte pieces, kNsUnroll loads in flight per thread; resident rows are
+  // read back from their chunk slots
+  constexpr int kNsUnroll = 8;
+  const int32_t h8 = H / 8;
+  const int32_t total = nrows * h8;
+  const bool resident = stages >= nch;
+  const uint4* src = (const uint4*)(x + m0 * H);
+  uint4* dst = (uint4*)(out + m0 * H);
+  for (int32_t i0 = threadIdx.x; i0 < total; i0 += blockDim.x * kNsUnroll) {
+    uint4 v[kNsUnroll], wq[kNsUnroll];
+#pragma unroll
+    for (int u = 0; u < kNsUnroll; ++u) {
+      const int32_t i = i0 + u * (int32_t)blockDim.x;
+      if (i < total) {
+        const int32_t r = i / h8, j = i - r * h8;
+        v[u] = resident ? *(const uint4*)(ns_smem + ((size_t)(j / (kNsChunk / 8)) * rows_per_cta + r) * kNsPitch +
+                                          (j % (kNsChunk / 8)) * 16)
+                        : src[i];
+        wq[u] = __ldg((const uint4*)w + j);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kNsUnroll; ++u) {
+      const int32_t i = i0 + u * (int32_t)blockDim.x;
+      if (i < total) {
+        const float rr = rs[i / h8];
+        const uint32_t vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w}, ww[4] = {wq[u].x, wq[u].y, wq[u].z, wq[u].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float a = __fmul_rn(__fmul_rn(rr, __uint_as_float(vv[q] << 16)), __uint_as_float(ww[q] << 16));
+          const float b = __fmul_rn(__fmul_rn(rr, __uint_as_float(vv[q] & 0xFFFF0000u)),
+                                    __uint_as_float(ww[q] & 0xFFFF0000u));
+          o[q] = (uint32_t)f32_to_bf16_bits(a) | ((uint32_t)f32_to_bf16_bits(b) << 16);
+        }
+        dst[i] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+}
+
 // -------------------------------------------------------------- router --
 // logits[m, e] = bf16(float(acc) + float(b[e])) where acc is a bf16 running
 // sum: acc = bf16(float(acc) + t[m,k]*W[e,k]) for k = 0..H-1 in order
@@ -953,6 +1090,24 @@ int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, f
                    uint32_t* err, cudaStream_t s) {
   if (M <= 0) return 0;
   if (H % 8 || ((uintptr_t)x & 15)) return -12;
+  if (!((uintptr_t)w & 15) && !((uintptr_t)out & 15)) {
+    // rows per CTA: all rows in one wave of CTAs where they fit, <= 32
+    const int64_t sms = device_sm_count();
+    const int rows = (int)min64(kNsMaxRows, max64(1, (M + sms - 1) / sms));
+    const int nch = (H + kNsChunk - 1) / kNsChunk;
+    const bool resident = nch <= kNsMaxSlots && (size_t)nch * rows * kNsPitch <= (size_t)kNsResidentBytes;
+    const int stages = resident ? nch : kNsStages;
+    const size_t smem = (size_t)stages * rows * kNsPitch;
+    static bool attr_s = false;
+    if (!attr_s) {
+      cudaFuncSetAttribute(rmsnorm_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)max64(kNsStages * kNsMaxRows * kNsPitch, kNsResidentBytes));
+      attr_s = true;
+    }
+    rmsnorm_stream_kernel<<<(unsigned)((M + rows - 1) / rows), 128, smem, s>>>(x, w, M, H, rows, stages, eps, out,
+                                                                              err);
+    return cudaGetLastError() == cudaSuccess ? 0 : -3;
+  }
   const size_t row = (size_t)(H + 8) * 2;
   const size_t fit = (size_t)(100 * 1024) / row;
   int rows = fit < (size_t)kNormRows ? (int)fit : kNormRows;

@@ -332,15 +332,27 @@ def test_mxfp4_dequant_golden_reference():
 
 
 def test_rmsnorm_bit_exact_odd_sizes(oracle):
+    """The streaming kernel (rows in 256-value chunks through a 4-slot ring)
+    at decode and prefill token counts, row lengths with a short last chunk
+    (520) or fewer values than one chunk (64), and the whole-row kernel it
+    falls back to when the weight or output is not 16-byte aligned."""
     rng = np.random.default_rng(12)
-    for M in (1, 33, 257):
-        x = synth().bf16_bits(rng.standard_normal((M, 2880)).astype(np.float32) * 3)
-        w = synth().bf16_bits(rng.standard_normal(2880).astype(np.float32))
-        out = torch.empty(M, 2880, dtype=torch.bfloat16, device="cuda")
+    for M, H in ((1, 2880), (33, 2880), (257, 2880), (5000, 2880), (8192, 2880), (300, 520), (70, 64),
+                 (9, 4096)):
+        x = synth().bf16_bits(rng.standard_normal((M, H)).astype(np.float32) * 3)
+        w = synth().bf16_bits(rng.standard_normal(H).astype(np.float32))
+        ref = oracle.rms_norm(x, w)
         xd, wd = G.dev(x), G.dev(w)  # keep the device copies alive until the kernel has run
-        G.call("gptoss_rms_norm", G.P(xd), G.P(wd), M, 2880, G.ctypes.c_float(1e-5), G.P(out), G.S())
+        out = torch.empty(M, H, dtype=torch.bfloat16, device="cuda")
+        G.call("gptoss_rms_norm", G.P(xd), G.P(wd), M, H, G.ctypes.c_float(1e-5), G.P(out), G.S())
         torch.cuda.synchronize()
-        np.testing.assert_array_equal(G.host(out), oracle.rms_norm(x, w))
+        np.testing.assert_array_equal(G.host(out), ref, err_msg=f"M={M} H={H}")
+        if M <= 257:  # unaligned output: the whole-row kernel
+            buf = torch.empty(M * H + 4, dtype=torch.bfloat16, device="cuda")
+            out2 = buf[4:].view(M, H)
+            G.call("gptoss_rms_norm", G.P(xd), G.P(wd), M, H, G.ctypes.c_float(1e-5), G.P(out2), G.S())
+            torch.cuda.synchronize()
+            np.testing.assert_array_equal(G.host(out2.contiguous()), ref, err_msg=f"M={M} H={H} unaligned")
 
 
 @pytest.mark.parametrize("E", [8, 32, 128])
