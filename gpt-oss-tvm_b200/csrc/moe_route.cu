@@ -788,34 +788,50 @@ __global__ void __launch_bounds__(kPermRangeWarps * 32) moe_perm_count_kernel(co
   for (int e = lane; e < E; e += 32) row_of_pair[lo + e] = wcnt[warp][e];
 }
 
-// One CTA of 1024 threads: thread (p, e) = (tid / 256, tid % 256) adds up
-// the counts of expert e over the p-th quarter of the ranges.
+// One CTA of 1024 threads: thread (p, e) = (tid / E, tid % E), p < 1024 / E,
+// adds up the counts of expert e over the p-th part of the ranges (loads
+// eight at a time), then writes that part's starting rows.
 __global__ void __launch_bounds__(1024) moe_perm_scan_kernel(int64_t pairs, int32_t E, int32_t* __restrict__ indptr,
                                                              int32_t* __restrict__ tile_ptr,
                                                              int32_t* __restrict__ tile_rows,
                                                              int32_t* __restrict__ row_of_pair) {
-  __shared__ int32_t part[4][256];
+  constexpr int kU = 8;
+  __shared__ int32_t part[1024];  // [P][E]
   __shared__ int32_t wtot[2][8];
-  const int e = threadIdx.x & 255, p = threadIdx.x >> 8;
-  const int64_t span = perm_span(pairs, E), nr = pairs / span;
-  const int64_t r0 = nr * p / 4, r1 = nr * (p + 1) / 4;
-  int32_t sum = 0;
-  if (e < E)
-    for (int64_t r = r0; r < r1; ++r) sum += row_of_pair[r * span + e];
-  part[p][e] = sum;
-  __syncthreads();
-  const int32_t c = part[0][e] + part[1][e] + part[2][e] + part[3][e];
-  const int32_t start = perm_scan_experts(threadIdx.x < 256 ? c : 0, E, pairs, indptr, tile_ptr, tile_rows, wtot);
   __shared__ int32_t first[256];
-  if (threadIdx.x < 256) first[e] = start;
+  const int P = 1024 / E;
+  const int e = threadIdx.x % E, p = threadIdx.x / E;
+  const bool mine = p < P;
+  const int64_t span = perm_span(pairs, E), nr = pairs / span;
+  const int64_t r0 = mine ? nr * p / P : 0, r1 = mine ? nr * (p + 1) / P : 0;
+  int32_t sum = 0;
+  for (int64_t r = r0; r < r1; r += kU) {
+    int32_t v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) v[u] = r + u < r1 ? row_of_pair[(r + u) * span + e] : 0;
+#pragma unroll
+    for (int u = 0; u < kU; ++u) sum += v[u];
+  }
+  if (mine) part[p * E + e] = sum;
   __syncthreads();
-  if (e < E) {
+  int32_t c = 0;
+  if (threadIdx.x < E)
+    for (int q = 0; q < P; ++q) c += part[q * E + threadIdx.x];
+  const int32_t start = perm_scan_experts(c, E, pairs, indptr, tile_ptr, tile_rows, wtot);
+  if (threadIdx.x < E) first[threadIdx.x] = start;
+  __syncthreads();
+  if (mine) {
     int32_t run = first[e];
-    for (int q = 0; q < p; ++q) run += part[q][e];
-    for (int64_t r = r0; r < r1; ++r) {
-      const int32_t k = row_of_pair[r * span + e];
-      row_of_pair[r * span + e] = run;
-      run += k;
+    for (int q = 0; q < p; ++q) run += part[q * E + e];
+    for (int64_t r = r0; r < r1; r += kU) {
+      int32_t v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) v[u] = r + u < r1 ? row_of_pair[(r + u) * span + e] : 0;
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (r + u < r1) row_of_pair[(r + u) * span + e] = run;
+        run += v[u];
+      }
     }
   }
 }

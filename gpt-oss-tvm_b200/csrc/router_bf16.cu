@@ -263,6 +263,7 @@ __global__ void __launch_bounds__(128) router_bf16_kernel(const uint16_t* __rest
         save[i][j] = acc[i][j];
         mn[i][j] = kBf16InfPair;
       }
+#pragma unroll 8
     for (int32_t kk = kk0; kk < kn; ++kk) {
       uint32_t t2[kTT];
       load_t(kk, t2);
