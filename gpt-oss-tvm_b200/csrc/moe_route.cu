@@ -100,7 +100,7 @@ constexpr int kNsResidentBytes = 100 * 1024;
 constexpr int kNsMaxRows = 32;
 constexpr int kNsPitch = kNsChunk * 2 + 16;  // bytes per row slot: rows start 4 banks apart
 
-__global__ void __launch_bounds__(128) rmsnorm_stream_kernel(const uint16_t* __restrict__ x,
+__global__ void __launch_bounds__(256) rmsnorm_stream_kernel(const uint16_t* __restrict__ x,
                                                               const uint16_t* __restrict__ w, int64_t M, int32_t H,
                                                               int32_t rows_per_cta, int32_t stages, float eps,
                                                               uint16_t* __restrict__ out, uint32_t* err) {
@@ -1120,8 +1120,10 @@ int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, f
                            (int)max64(kNsStages * kNsMaxRows * kNsPitch, kNsResidentBytes));
       attr_s = true;
     }
-    rmsnorm_stream_kernel<<<(unsigned)((M + rows - 1) / rows), 128, smem, s>>>(x, w, M, H, rows, stages, eps, out,
-                                                                              err);
+    // (the ring form's second read of x and its stores want more loads in
+    // flight: eight warps; the resident form four)
+    rmsnorm_stream_kernel<<<(unsigned)((M + rows - 1) / rows), resident ? 128 : 256, smem, s>>>(x, w, M, H, rows,
+                                                                                               stages, eps, out, err);
     return cudaGetLastError() == cudaSuccess ? 0 : -3;
   }
   const size_t row = (size_t)(H + 8) * 2;
