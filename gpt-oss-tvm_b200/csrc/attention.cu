@@ -989,11 +989,8 @@ int launch_attn_prefill(const uint16_t* q, const uint16_t* k, const uint16_t* v,
       make_tmap_3d(&tk, k, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dk, sk_, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
       make_tmap_3d(&tv, v, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, dk, sk_, box, CU_TENSOR_MAP_SWIZZLE_128B))
     return -2;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmemAlloc);
-    attr = true;
-  }
+  static FuncSmemAttr attr;
+  ensure_dyn_smem(attr, (const void*)attn_prefill_tc_kernel, kTcSmemAlloc);
   dim3 grid((unsigned)((Sq + 2 * kTcBQ - 1) / (2 * kTcBQ)), (unsigned)Hq);
   attn_prefill_tc_kernel<<<grid, kTcThreads, kTcSmemAlloc, s>>>(tq, tk, tv, sinks, Sq, Skv, Hq, Hkv, window,
                                                                 sm_scale, o, lse);
@@ -1029,11 +1026,8 @@ int launch_attn_decode(const uint16_t* q, const uint16_t* kc, const uint16_t* vc
   float* part_o = scratch;
   float* part_ml = scratch + (size_t)B * Hq * splits * kAttD;
   const size_t smem = 16 * 128 + kDecWarps * 2 * 2 * kAttBK * 128 + kDecWarps * (16 + 16 + 16 * 64) * 4;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    attr = true;
-  }
+  static FuncSmemAttr attr;
+  ensure_dyn_smem(attr, (const void*)attn_decode_kernel, (int)smem);
   dim3 grid((unsigned)(B * Hkv), (unsigned)splits);
   attn_decode_kernel<<<grid, 128, smem, s>>>(q, kc, vc, kv_len, max_len, Hq, Hkv, window, sm_scale, splits, part_o,
                                              part_ml, table, tstride);

@@ -68,14 +68,13 @@ int launch_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* W, const uin
   if (T > kDenseMaxT || N <= 0 || K <= 0 || K % 8 || K > kDenseMaxK || ((uintptr_t)W & 15)) return -12;
   const size_t smem = (size_t)T * K * sizeof(float);
   const unsigned grid = (unsigned)((N + kDenseWarps - 1) / kDenseWarps);
-  static bool attr = false;
-  if (!attr) {
+  static FuncSmemAttr attr1, attr2, attr3, attr4;
+  {
     const int mx = kDenseMaxT * kDenseMaxK * (int)sizeof(float);
-    cudaFuncSetAttribute(dense_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-    cudaFuncSetAttribute(dense_gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-    cudaFuncSetAttribute(dense_gemv_kernel<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-    cudaFuncSetAttribute(dense_gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, mx);
-    attr = true;
+    ensure_dyn_smem(attr1, (const void*)dense_gemv_kernel<1>, mx);
+    ensure_dyn_smem(attr2, (const void*)dense_gemv_kernel<2>, mx);
+    ensure_dyn_smem(attr3, (const void*)dense_gemv_kernel<3>, mx);
+    ensure_dyn_smem(attr4, (const void*)dense_gemv_kernel<4>, mx);
   }
   switch (T) {
     case 1: dense_gemv_kernel<1><<<grid, kDenseWarps * 32, smem, s>>>(x, W, bias, N, K, out); break;

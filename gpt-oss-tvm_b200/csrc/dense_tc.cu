@@ -292,19 +292,14 @@ static int dense_slots_per_sm(int bn) { return bn <= 64 ? 2 : 1; }
 template <int kBN>
 static int dense_max_clusters(int split) {
   constexpr int kMaxDev = 16;
-  static int cache[kMaxDev][kDnMaxSplit + 1];
-  static bool init = false;
-  if (!init) {
-    for (auto& row : cache)
-      for (int& v : row) v = -1;
-    init = true;
-  }
+  static std::atomic<int> cache[kMaxDev][kDnMaxSplit + 1] = {};  // clusters + 1; 0 = not measured yet
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) {
     (void)cudaGetLastError();
     return 0;
   }
-  if (cache[dev][split] < 0) {
+  int c = cache[dev][split].load(std::memory_order_acquire);
+  if (c == 0) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attrs[1];
     attrs[0].id = cudaLaunchAttributeClusterDimension;
@@ -321,22 +316,19 @@ static int dense_max_clusters(int split) {
       (void)cudaGetLastError();
       n = 0;
     }
-    cache[dev][split] = n;
+    c = n + 1;
+    cache[dev][split].store(c, std::memory_order_release);
   }
-  return cache[dev][split];
+  return c - 1;
 }
 
 template <int kBN>
 static int launch_dense_bn(const CUtensorMap& ta, const CUtensorMap& tb, const DenseParams& p, cudaStream_t s) {
   using C = DenseCfg<kBN>;
   auto kern = dense_gemm_tc_kernel<kBN>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kAlloc);
-    // all of the SM's unified memory as shared memory: two decode-size CTAs per SM
-    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-    attr = true;
-  }
+  static FuncSmemAttr attr;
+  // (all of the SM's unified memory as shared memory: two decode-size CTAs per SM)
+  ensure_dyn_smem(attr, (const void*)kern, C::kAlloc, 100);
   const int slots = device_sm_count() * dense_slots_per_sm(kBN);
   const int32_t tiles = p.tiles_a * p.tiles_b;
   const int32_t nch = (p.K + kDnBK - 1) / kDnBK;

@@ -5,6 +5,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../../include/gptoss_b200.h"
 
 namespace gptoss {
@@ -51,6 +54,28 @@ int launch_sample_top_p(const float* logits, int64_t B, int64_t V, double temper
                         cudaStream_t s);
 // SM count of the current device (cached per device)
 int device_sm_count();
+
+// A kernel's dynamic shared-memory limit, raised on the current device the
+// first time a launch needs more than what was set there (function
+// attributes are per device; thread-safe; never lowered).
+constexpr int kMaxAttrDevices = 64;
+struct FuncSmemAttr {
+  std::atomic<int> bytes[kMaxAttrDevices] = {};
+  std::mutex mu;
+};
+inline void ensure_dyn_smem(FuncSmemAttr& a, const void* func, int bytes, int carveout = -1) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxAttrDevices) {
+    (void)cudaGetLastError();
+    dev = 0;
+  }
+  if (a.bytes[dev].load(std::memory_order_acquire) >= bytes) return;
+  std::lock_guard<std::mutex> g(a.mu);
+  if (a.bytes[dev].load(std::memory_order_relaxed) >= bytes) return;
+  cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (carveout >= 0) cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, carveout);
+  a.bytes[dev].store(bytes, std::memory_order_release);
+}
 // dense_tc.cu: the same product at any T on the tensor cores
 int launch_dense_gemm(const uint16_t* x, int64_t T, const uint16_t* W, const uint16_t* bias, int32_t N, int32_t K,
                       uint16_t* out, uint32_t* err, cudaStream_t s);

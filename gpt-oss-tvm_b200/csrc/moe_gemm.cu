@@ -575,11 +575,8 @@ template <int kMode, bool kF16, int kVar>
 static void launch_variant(const CUtensorMap& ta, const CUtensorMap& ta64, const CUtensorMap& tw, const GemmParams& p,
                            int grid, cudaStream_t stream) {
   const int smem = GemmCfg<kVar>::kAlloc;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(moe_gemm_tc_kernel<kMode, kF16, kVar>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    attr = true;
-  }
+  static FuncSmemAttr attr;
+  ensure_dyn_smem(attr, (const void*)moe_gemm_tc_kernel<kMode, kF16, kVar>, (int)smem);
   moe_gemm_tc_kernel<kMode, kF16, kVar><<<grid, kGemmThreads, smem, stream>>>(ta, ta64, tw, p);
 }
 
@@ -590,7 +587,14 @@ static bool launch_pair(const CUtensorMap& ta, const CUtensorMap& ta64, const CU
                         int grid, cudaStream_t stream) {
   auto kern = moe_gemm_tc_kernel<kMode, kF16, kVarPair>;
   const int smem = GemmCfg<kVarPair>::kAlloc;
-  static int max_pairs = -1;
+  static FuncSmemAttr smem_attr;
+  static std::atomic<int> fit[kMaxAttrDevices] = {};  // clusters that fit at once + 1 per device; 0 = unknown
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxAttrDevices) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  ensure_dyn_smem(smem_attr, (const void*)kern, smem);
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -602,8 +606,8 @@ static bool launch_pair(const CUtensorMap& ta, const CUtensorMap& ta64, const CU
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  int max_pairs = fit[dev].load(std::memory_order_acquire) - 1;
   if (max_pairs < 0) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     cfg.gridDim = dim3((unsigned)(grid & ~1));
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
@@ -611,6 +615,7 @@ static bool launch_pair(const CUtensorMap& ta, const CUtensorMap& ta64, const CU
       n = 0;
     }
     max_pairs = n;
+    fit[dev].store(n + 1, std::memory_order_release);
   }
   const int pairs = grid / 2 < max_pairs ? grid / 2 : max_pairs;
   if (pairs <= 0) return false;

@@ -326,20 +326,12 @@ int launch_moe_gemv(int mode, const GemmLaunch& L, cudaStream_t stream) {
   // at most act_rows experts have rows: CTAs for the routed experts only
   const dim3 grid((unsigned)((L.N + kGvRowsCta - 1) / kGvRowsCta), (unsigned)min64(L.E, L.act_rows));
   if (mode == 0) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(moe_gemv_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kGvTok * (2 * kGvMaxK + 32) + kGvRedBytes);
-      attr = true;
-    }
+    static FuncSmemAttr attr;
+    ensure_dyn_smem(attr, (const void*)moe_gemv_kernel<0>, kGvTok * (2 * kGvMaxK + 32) + kGvRedBytes);
     moe_gemv_kernel<0><<<grid, kGvWarps * 32, smem, stream>>>(p);
   } else {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(moe_gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           kGvTok * (2 * kGvMaxK + 32) + kGvRedBytes);
-      attr = true;
-    }
+    static FuncSmemAttr attr;
+    ensure_dyn_smem(attr, (const void*)moe_gemv_kernel<1>, kGvTok * (2 * kGvMaxK + 32) + kGvRedBytes);
     moe_gemv_kernel<1><<<grid, kGvWarps * 32, smem, stream>>>(p);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;

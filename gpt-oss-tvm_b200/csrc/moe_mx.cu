@@ -587,18 +587,12 @@ int launch_moe_gemm_mx(int mode, const GemmLaunch& L, const uint8_t* q, const ui
   mp.blocks = L.blocks;
   mp.act_sc = act_sc;
   if (mode == 0) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(moe_gemm_mx_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxSmem);
-      attr = true;
-    }
+    static FuncSmemAttr attr;
+    ensure_dyn_smem(attr, (const void*)moe_gemm_mx_kernel<0>, kMxSmem);
     moe_gemm_mx_kernel<0><<<L.grid, kMxThreads, kMxSmem, stream>>>(tw, th, tlo, mp);
   } else {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(moe_gemm_mx_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMxSmem);
-      attr = true;
-    }
+    static FuncSmemAttr attr;
+    ensure_dyn_smem(attr, (const void*)moe_gemm_mx_kernel<1>, kMxSmem);
     moe_gemm_mx_kernel<1><<<L.grid, kMxThreads, kMxSmem, stream>>>(tw, th, tlo, mp);
   }
   return cudaGetLastError() == cudaSuccess ? 0 : -3;

@@ -1114,12 +1114,9 @@ int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, f
     const bool resident = nch <= kNsMaxSlots && (size_t)nch * rows * kNsPitch <= (size_t)kNsResidentBytes;
     const int stages = resident ? nch : kNsStages;
     const size_t smem = (size_t)stages * rows * kNsPitch;
-    static bool attr_s = false;
-    if (!attr_s) {
-      cudaFuncSetAttribute(rmsnorm_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)max64(kNsStages * kNsMaxRows * kNsPitch, kNsResidentBytes));
-      attr_s = true;
-    }
+    static FuncSmemAttr attr_s;
+    ensure_dyn_smem(attr_s, (const void*)rmsnorm_stream_kernel,
+                    (int)max64(kNsStages * kNsMaxRows * kNsPitch, kNsResidentBytes));
     // (the ring form's second read of x and its stores want more loads in
     // flight: eight warps; the resident form four)
     rmsnorm_stream_kernel<<<(unsigned)((M + rows - 1) / rows), resident ? 128 : 256, smem, s>>>(x, w, M, H, rows,
@@ -1131,11 +1128,8 @@ int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, f
   int rows = fit < (size_t)kNormRows ? (int)fit : kNormRows;
   if (rows < 1) return -12;
   const size_t smem = row * rows;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 100 * 1024 + 1024);
-    attr = true;
-  }
+  static FuncSmemAttr attr;
+  ensure_dyn_smem(attr, (const void*)rmsnorm_kernel, 100 * 1024 + 1024);
   const int64_t blocks = (M + rows - 1) / rows;
   rmsnorm_kernel<<<(unsigned)blocks, 128, smem, s>>>(x, w, M, H, rows, eps, out, err);
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
@@ -1144,11 +1138,8 @@ int launch_rmsnorm(const uint16_t* x, const uint16_t* w, int64_t M, int32_t H, f
 template <int kTQ, int kWQ>
 static void launch_router_variant(dim3 grid, size_t smem, cudaStream_t s, const uint16_t* t, const uint16_t* W,
                                   const uint16_t* b, int64_t M, int32_t E, int32_t H, int32_t be, uint16_t* logits) {
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(router_kernel<kTQ, kWQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr = true;
-  }
+  static FuncSmemAttr attr;
+  ensure_dyn_smem(attr, (const void*)router_kernel<kTQ, kWQ>, 200 * 1024);
   router_kernel<kTQ, kWQ><<<grid, 128, smem, s>>>(t, W, b, M, E, H, be, logits);
 }
 

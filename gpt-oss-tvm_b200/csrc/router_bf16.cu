@@ -503,12 +503,8 @@ int launch_router_bf16(const uint16_t* t, const uint16_t* W, const uint16_t* b, 
   const int64_t sms = device_sm_count();
   const int64_t chain_ctas = ((E + kRcExp - 1) / kRcExp) * ((M + kRcTok - 1) / kRcTok);
   if (chain_ctas <= 2 * sms && H <= kRcMaxH) {
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(router_bf16_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)rc_smem_bytes(kRcMaxH));
-      attr = true;
-    }
+    static FuncSmemAttr attr;
+    ensure_dyn_smem(attr, (const void*)router_bf16_chain_kernel, (int)rc_smem_bytes(kRcMaxH));
     dim3 grid((unsigned)((E + kRcExp - 1) / kRcExp), (unsigned)((M + kRcTok - 1) / kRcTok));
     router_bf16_chain_kernel<<<grid, kRcThreads, rc_smem_bytes(H), s>>>(t, W, b, M, E, H, logits, err);
   } else {

@@ -282,11 +282,8 @@ int launch_sample_top_p(const float* logits, int64_t B, int64_t V, double temper
   const int64_t per_row = sample_top_p_scratch_bytes_per_row(V);
   const int64_t rows = greedy ? B : (scratch ? scratch_bytes / per_row : 0);
   if (rows < 1) return -13;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(sample_top_p_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(SmpShared));
-    attr = true;
-  }
+  static FuncSmemAttr attr;
+  ensure_dyn_smem(attr, (const void*)sample_top_p_kernel, (int)sizeof(SmpShared));
   // rows in groups that the scratch holds
   for (int64_t r0 = 0; r0 < B; r0 += rows) {
     const int64_t nb = min64(rows, B - r0);
