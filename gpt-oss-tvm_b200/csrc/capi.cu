@@ -674,10 +674,40 @@ int gptoss::moe_experts_forward(const uint16_t* t, int64_t M, const gptoss_moe_w
     return gptoss_moe_mlp2_mx(q, qs, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp2_blocks, w->mlp2_scales,
                               w->mlp2_bias, h2, err, stream);
   }
-  if ((rc = gptoss_moe_gather(t, token_of_row, R, H, f16, act, stream))) return rc;
-  if ((rc = gptoss_moe_mlp1(act, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp1_blocks, w->mlp1_scales, w->mlp1_bias,
-                            w->swiglu_alpha, w->swiglu_limit, f16, y, err, stream)))
-    return rc;
+  bool gathered = false;
+  if (f16 && token_of_row) {
+    // the decode GEMV stages its token rows straight from t (no gather launch)
+    GemmLaunch L;
+    L.act = t;
+    L.act_rows = R;
+    L.blocks = w->mlp1_blocks;
+    L.scales = w->mlp1_scales;
+    L.bias = w->mlp1_bias;
+    L.indptr = indptr;
+    L.tile_ptr = tile_ptr;
+    L.tile_rows = tile_rows;
+    L.out = y;
+    L.E = E;
+    L.N = 2 * I;
+    L.K = H;
+    L.ldo = I;
+    L.alpha = w->swiglu_alpha;
+    L.limit = w->swiglu_limit;
+    L.err = err;
+    L.grid = num_sms();
+    L.f16 = 1;
+    L.act_gather = token_of_row;
+    if (moe_gemm_gathers(L)) {
+      if ((rc = check_launch(launch_moe_gemm(0, L, GPTOSS_STREAM(stream)), "moe_mlp1"))) return rc;
+      gathered = true;
+    }
+  }
+  if (!gathered) {
+    if ((rc = gptoss_moe_gather(t, token_of_row, R, H, f16, act, stream))) return rc;
+    if ((rc = gptoss_moe_mlp1(act, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp1_blocks, w->mlp1_scales,
+                              w->mlp1_bias, w->swiglu_alpha, w->swiglu_limit, f16, y, err, stream)))
+      return rc;
+  }
   return gptoss_moe_mlp2(y, R, indptr, tile_ptr, tile_rows, E, H, I, w->mlp2_blocks, w->mlp2_scales, w->mlp2_bias, f16,
                          h2, err, stream);
 }

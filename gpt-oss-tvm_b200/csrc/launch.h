@@ -37,8 +37,15 @@ struct GemmLaunch {
   void* peer_out[kMaxPeerRanks] = {};
   int64_t peer_out_rows = 0;  // rows of each peer_out buffer; stores beyond it are dropped
   int out_bf16 = 0;
+  // optional, decode GEMV only (moe_gemm_gathers): act holds bf16 token rows
+  // and activation row r is f16(act[act_gather[r]]) -- the gather into the
+  // expert-major rows happens while the GEMV stages its token rows
+  const int32_t* act_gather = nullptr;
 };
 int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream);
+// Whether launch_moe_gemm takes L to the decode GEMV, the one form that can
+// gather its activation rows itself (act_gather).
+bool moe_gemm_gathers(const GemmLaunch& L);
 // dense.cu: y = x W^T + b for at most dense_gemv_max_tokens() token rows
 int dense_gemv_max_tokens();
 int launch_dense_gemv(const uint16_t* x, int64_t T, const uint16_t* W, const uint16_t* bias, int32_t N, int32_t K,

@@ -636,11 +636,15 @@ static bool gemv_enabled() {
   return !(e && e[0] == '0');
 }
 
+bool moe_gemm_gathers(const GemmLaunch& L) {
+  return moe_tile_rows_max(L.act_rows, L.E) <= kMoeTileRowsSmall && gemv_enabled() && moe_gemv_supported(L);
+}
+
 int launch_moe_gemm(int mode, const GemmLaunch& L, cudaStream_t stream) {
   // decode sizes (the same rule as the token-tile plan's small tiles): the
   // weights are streamed once through the MXFP4 GEMV kernel
-  if (moe_tile_rows_max(L.act_rows, L.E) <= kMoeTileRowsSmall && gemv_enabled() && moe_gemv_supported(L))
-    return launch_moe_gemv(mode, L, stream);
+  if (moe_gemm_gathers(L)) return launch_moe_gemv(mode, L, stream);
+  if (L.act_gather) return -10;  // only the GEMV gathers
   if (L.K % kBK != 0 || L.K / 32 > kMaxGroups || L.K / 2 < kWRowBytes) return -10;
   {
     // every tile's scale block must be a whole number of 16-byte units

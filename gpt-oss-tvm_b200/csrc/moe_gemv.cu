@@ -49,6 +49,7 @@ struct GemvParams {
   float alpha, limit;
   int32_t tok_cap;  // token rows staged per pass (<= kGvTok)
   uint32_t* err;
+  const int32_t* gather;  // optional: act holds bf16 token rows, row r = f16(act[gather[r]])
 };
 
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -206,7 +207,16 @@ __global__ void __launch_bounds__(kGvWarps * 32) moe_gemv_kernel(const GemvParam
     if (warp < rounds) gv_load(A, wrow, srow, 4 * warp + q, G);
     for (int i = threadIdx.x; i < nv * chunks_row; i += blockDim.x) {
       const int n = i / chunks_row, ch = i - n * chunks_row;
-      const uint4 v = __ldg((const uint4*)(p.act + (size_t)(r0 + c0 + n) * p.K) + ch);
+      const int64_t src = p.gather ? (int64_t)__ldg(p.gather + r0 + c0 + n) : r0 + c0 + n;
+      uint4 v = __ldg((const uint4*)(p.act + (size_t)src * p.K) + ch);
+      if (p.gather) {  // bf16 token row -> f16 (exact in the f16 path's range)
+        uint32_t* w = (uint32_t*)&v;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const __half2 h = __floats2half2_rn(__uint_as_float(w[q] << 16), __uint_as_float(w[q] & 0xFFFF0000u));
+          w[q] = *(const uint32_t*)&h;
+        }
+      }
       *(uint4*)(gv_smem + (size_t)n * S + gv_chunk_ofs(ch >> 2, ch & 3)) = v;
     }
     __syncthreads();
@@ -322,6 +332,7 @@ int launch_moe_gemv(int mode, const GemmLaunch& L, cudaStream_t stream) {
   p.limit = L.limit;
   p.tok_cap = (int32_t)min64(kGvTokDecode, L.act_rows);
   p.err = L.err;
+  p.gather = L.act_gather;
   const size_t smem = (size_t)p.tok_cap * (2 * (size_t)L.K + 32) + kGvRedBytes;
   // at most act_rows experts have rows: CTAs for the routed experts only
   const dim3 grid((unsigned)((L.N + kGvRowsCta - 1) / kGvRowsCta), (unsigned)min64(L.E, L.act_rows));
