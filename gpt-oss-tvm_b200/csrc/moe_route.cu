@@ -128,6 +128,13 @@ __global__ void __launch_bounds__(256) rmsnorm_stream_kernel(const uint16_t* __r
   if (threadIdx.x == 0) all_ok = 1;
   fence_mbar_init();
   __syncthreads();
+  if (warp != 0) {
+    // the other warps bring the norm weight into L2 while the chains run (its
+    // loads come right after the chains; from HBM they would add their
+    // latency to every decode-size call)
+    for (int32_t i = threadIdx.x - 32; i < H / 64; i += blockDim.x - 32)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(w + (size_t)i * 64));
+  }
   if (warp == 0) {
     auto slot_row = [&](int c, int r) { return ns_smem + ((size_t)(c % stages) * rows_per_cta + r) * kNsPitch; };
     auto issue = [&](int c) {
