@@ -856,7 +856,8 @@ DENSE_SHAPES = {"qkv 5120x2880": (5120, 2880, True), "out 2880x4096": (2880, 409
 def dense_bench(dev, peaks, iters=10, tokens=(1, 8, 64, 256, 4096)):
     """The attention block's projections and the unembedding (bf16, fp32
     accumulation): gptoss_dense_gemm (tcgen05) beside torch's nn.Linear
-    (cuBLAS) on the same inputs; CUDA events per call after a 256 MB L2
+    (cuBLAS), and for up to gptoss_dense_gemv_max_tokens() tokens the
+    warp-per-row gptoss_dense_gemv, on the same inputs; CUDA events per call after a 256 MB L2
     flush, median of `iters`.  Inputs resident."""
     import torch
     import torch.nn.functional as F
@@ -883,8 +884,14 @@ def dense_bench(dev, peaks, iters=10, tokens=(1, 8, 64, 256, 4096)):
             def theirs():
                 F.linear(x, w, b)
 
+            def gemv():
+                lib.call("gptoss_dense_gemv", P(x), T, P(w), P(b), N, K, P(out), stream)
+
+            fns = [("gptoss_dense_gemm", ours), ("cublas", theirs)]
+            if T <= lib.load().gptoss_dense_gemv_max_tokens():
+                fns.append(("gptoss_dense_gemv", gemv))
             times = {}
-            for tag, fn in (("gptoss_dense_gemm", ours), ("cublas", theirs)):
+            for tag, fn in fns:
                 ts = []
                 for i in range(iters + 2):
                     flush.zero_()
@@ -904,6 +911,8 @@ def dense_bench(dev, peaks, iters=10, tokens=(1, 8, 64, 256, 4096)):
                 "speedup_vs_cublas": round(times["cublas"] / ms, 3),
                 "achieved_gbs": round(bytes_ / ms / 1e6, 1), "hbm_frac": round(bytes_ / ms / 1e6 / hbm, 4),
                 "tflops": round(flops / ms / 1e9, 1), "tensor_frac": round(flops / ms / 1e9 / tc_peak, 4)}
+            if "gptoss_dense_gemv" in times:
+                res[f"{name} T={T}"]["gemv_ms"] = round(times["gptoss_dense_gemv"], 4)
     res["note"] = "L2 flushed (256 MB write) before every call; bytes = weights + inputs + outputs once"
     return res
 

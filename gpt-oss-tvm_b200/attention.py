@@ -332,17 +332,31 @@ class KVCache:
 
 
 DENSE_GEMV = False  # decode-size projections through gptoss_dense_gemv instead of cuBLAS
+# Decode-size projections with a long reduction (the out projection, K = 4096)
+# on the library's tcgen05 GEMM (split-K clusters), where it beats cuBLAS in
+# the decode graphs (gpt-oss-20b batch 1: 3.26 -> 3.20 ms per step; batch 8:
+# 5.85 -> 5.81); the qkv projection (K = 2880) stays on cuBLAS, which is faster
+# there.  0 turns it off.
+DENSE_TC_MAX_TOKENS = 8
+DENSE_TC_MIN_K = 4096
 
 
 def _linear(x2: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
-    """nn.Linear with bias on [T, K] bf16: cuBLAS, or with DENSE_GEMV the
-    library GEMV for few tokens (a weight stream)."""
+    """nn.Linear with bias on [T, K] bf16: cuBLAS; the library's tcgen05 GEMM
+    for few tokens and K >= DENSE_TC_MIN_K; with DENSE_GEMV the library GEMV
+    for few tokens (a weight stream)."""
     T = x2.shape[0]
     if DENSE_GEMV and 0 < T <= _lib.dense_max_tokens():
         x2 = x2.contiguous()
         out = torch.empty(T, weight.shape[0], dtype=torch.bfloat16, device=x2.device)
         _lib.call("gptoss_dense_gemv", _ptr(x2), T, _ptr(weight), _ptr(bias), weight.shape[0], weight.shape[1],
                   _ptr(out), _stream())
+        return out
+    if 0 < T <= DENSE_TC_MAX_TOKENS and weight.shape[1] >= DENSE_TC_MIN_K and x2.is_cuda:
+        x2 = x2.contiguous()
+        out = torch.empty(T, weight.shape[0], dtype=torch.bfloat16, device=x2.device)
+        _lib.call("gptoss_dense_gemm", _ptr(x2), T, _ptr(weight), _ptr(bias), weight.shape[0], weight.shape[1],
+                  _ptr(out), None, _stream())
         return out
     return F.linear(x2, weight, bias)
 
