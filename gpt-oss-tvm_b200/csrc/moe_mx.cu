@@ -42,6 +42,8 @@ constexpr int kMxStages = 6;
 constexpr int kMxMaxN = kMoeTileRowsSmall;       // token rows per tile (32)
 constexpr int kMxWBytes = kBM * kMxBK;           // 16 KB: 128 weight rows x 128 codes
 constexpr int kMxActBytes = kMxMaxN * kMxBK;     // 4 KB: one activation term of one stage
+constexpr int kMxActStage = 2 * kMxActBytes;     // a stage's two terms: the 32 hi rows, then the 32 lo rows
+constexpr int kMxMmaN = 2 * kMxMaxN;             // MMA N: hi and lo rows in one MMA (64)
 constexpr int kMxSfBytes = 512;                  // one scale-factor chunk: 128 rows x 4 K-blocks
 constexpr int kMxMaxGroups = 96;                 // K / 32 <= 96 (K <= 3072)
 constexpr int kMxScRow = 2 * kMxMaxGroups;       // bytes per row of the activation scales: hi, then lo
@@ -52,21 +54,21 @@ constexpr int kMxScRow = 2 * kMxMaxGroups;       // bytes per row of the activat
 constexpr int kMxWarpW = 0, kMxWarpSf = 1, kMxWarpAct = 2, kMxWarpMma = 3, kMxWarpEpi0 = 4, kMxWarpSf1 = 8,
               kMxWarpMma1 = 9;
 // TMEM columns: two accumulator buffers (tile i / i + 1), each a pair of
-// 32-column accumulators (even / odd stages: one per MMA issuer, summed by the
-// epilogue), then per pipeline stage its three scale-factor chunks (4 columns
-// each), so that copying the chunks of one stage never writes columns the MMAs
-// of another stage still read
-constexpr int kMxAccCols = 32;
-constexpr int kMxSfCol0 = 4 * kMxAccCols, kMxSfStageCols = 12;
-constexpr int kMxTmemCols = 256;
+// 64-column accumulators (even / odd stages: one per MMA issuer; columns
+// 0-31 the hi term, 32-63 the lo term of the tile's token rows; all four
+// summed by the epilogue), then per pipeline stage its two scale-factor
+// chunks (4 columns each), so that copying the chunks of one stage never
+// writes columns the MMAs of another stage still read
+constexpr int kMxAccCols = kMxMmaN;
+constexpr int kMxSfCol0 = 4 * kMxAccCols, kMxSfStageCols = 8;
+constexpr int kMxTmemCols = 512;
 static_assert(kMxSfCol0 + kMxStages * kMxSfStageCols <= kMxTmemCols, "TMEM budget");
 
 // shared memory layout (offsets from the 1024-aligned base)
 constexpr int kMxOffW = 0;
-constexpr int kMxOffAh = kMxOffW + kMxStages * kMxWBytes;
-constexpr int kMxOffAl = kMxOffAh + kMxStages * kMxActBytes;
-constexpr int kMxOffSf = kMxOffAl + kMxStages * kMxActBytes;              // [stage][3][512]
-constexpr int kMxOffScW = kMxOffSf + kMxStages * 3 * kMxSfBytes;          // [2][128 x G] weight scales of a tile
+constexpr int kMxOffA = kMxOffW + kMxStages * kMxWBytes;                 // [stage][hi rows | lo rows][128 B]
+constexpr int kMxOffSf = kMxOffA + kMxStages * kMxActStage;              // [stage][2][512]
+constexpr int kMxOffScW = kMxOffSf + kMxStages * 2 * kMxSfBytes;          // [2][128 x G] weight scales of a tile
 constexpr int kMxOffScA = kMxOffScW + 2 * kBM * kMxMaxGroups;             // [2][32 x 192] activation scales
 constexpr int kMxOffBar = kMxOffScA + 2 * kMxMaxN * kMxScRow;
 constexpr int kMxNumBars = 2 * kMxStages + 2 + 2 + 2 + 2 + 1;
@@ -74,8 +76,7 @@ constexpr int kMxOffMisc = kMxOffBar + kMxNumBars * 8;
 constexpr int kMxOffEpi = (kMxOffMisc + 64 + 15) & ~15;                  // 4 warps x 2 KB
 constexpr int kMxSmem = kMxOffEpi + 4 * 2048 + 1024;
 static_assert(kMxSmem <= 227 * 1024, "shared memory budget");
-static_assert(kMxOffAh % 1024 == 0 && kMxOffAl % 1024 == 0 && kMxActBytes % 1024 == 0,
-              "128-byte swizzle atoms stay 1024-aligned");
+static_assert(kMxOffA % 1024 == 0 && kMxActBytes % 1024 == 0, "128-byte swizzle atoms stay 1024-aligned");
 
 // ------------------------------------------------------------------ PTX --
 // Instruction descriptor of kind::mxf8f6f4.block_scale: A e2m1 (K-major), B
@@ -323,10 +324,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           if (!mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[s], (uint32_t)(2 * nbox * 16 * kMxBK));
           for (int32_t b = 0; b < nbox; ++b) {
-            tma_load_2d(smem + kMxOffAh + s * kMxActBytes + b * 16 * kMxBK, &tmap_hi, j * kMxBK, ti.row0 + 16 * b,
-                        &full_bar[s]);
-            tma_load_2d(smem + kMxOffAl + s * kMxActBytes + b * 16 * kMxBK, &tmap_lo, j * kMxBK, ti.row0 + 16 * b,
-                        &full_bar[s]);
+            uint8_t* dst = smem + kMxOffA + s * kMxActStage + b * 16 * kMxBK;
+            tma_load_2d(dst, &tmap_hi, j * kMxBK, ti.row0 + 16 * b, &full_bar[s]);
+            tma_load_2d(dst + kMxActBytes, &tmap_lo, j * kMxBK, ti.row0 + 16 * b, &full_bar[s]);
           }
         }
         if (!ok) { *abort_s = 1; break; }
@@ -351,7 +351,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         const uint32_t s = it % kMxStages, ph = (it / kMxStages) & 1;
         ok = mbar_wait(&empty_bar[s], ph ^ 1, p.err, kErrTimeoutEmpty);
         if (!ok) break;
-        uint8_t* sf = smem + kMxOffSf + s * 3 * kMxSfBytes;
+        uint8_t* sf = smem + kMxOffSf + s * 2 * kMxSfBytes;
         // weights: line `lane` holds rows lane, lane + 32, lane + 64, lane + 96;
         // a row's 4 bytes are two 16-bit reads (rows are G bytes apart, G even)
         const int32_t g0 = 4 * j;
@@ -371,15 +371,17 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           w4[qq] = v;
         }
         *(uint4*)(sf + lane * 16) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-        // activations: one 32-bit read per term (rows are 192 bytes apart); rows
-        // beyond the tile's count get exponent 127 (their MMA columns are never stored)
+        // activations: one 32-bit read per term (rows are 192 bytes apart); the
+        // MMA's B rows are the 32 hi rows then the 32 lo rows, so lane r holds
+        // B row r (hi of token row r) in word 0 and B row r + 32 (lo) in word 1,
+        // the layout of the weights' rows r and r + 32.  Rows beyond the tile's
+        // count get exponent 127 (their MMA columns are never stored)
         uint32_t vh = 0x7F7F7F7Fu, vl = 0x7F7F7F7Fu;
         if (lane < ti.nrows) {
           vh = (*(const uint32_t*)(sca + lane * kMxScRow + g0) & keep) | pad;
           vl = (*(const uint32_t*)(sca + lane * kMxScRow + kMxMaxGroups + g0) & keep) | pad;
         }
-        *(uint4*)(sf + kMxSfBytes + lane * 16) = make_uint4(vh, vh, vh, vh);
-        *(uint4*)(sf + 2 * kMxSfBytes + lane * 16) = make_uint4(vl, vl, vl, vl);
+        *(uint4*)(sf + kMxSfBytes + lane * 16) = make_uint4(vh, vl, 0x7F7F7F7Fu, 0x7F7F7F7Fu);
         if (j == nmain) {
           // the row tails (codes nmain*128 .. K-1, 32 packed bytes per row) in
           // the form the TMA type writes: each 8 packed bytes (16 codes) then 8
@@ -417,12 +419,10 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       uint32_t it = 0, tl = 0;
       bool ok = true;
       const uint64_t wdesc0 = make_sdesc_sw128(smem_u32(smem + kMxOffW));
-      const uint64_t hdesc0 = make_sdesc_sw128(smem_u32(smem + kMxOffAh));
-      const uint64_t ldesc0 = make_sdesc_sw128(smem_u32(smem + kMxOffAl));
+      const uint64_t bdesc0 = make_sdesc_sw128(smem_u32(smem + kMxOffA));
       for (int32_t t = blockIdx.x; t < total_tiles && !*abort_s; t += gridDim.x) {
         TileInfo ti;
         if (!decode_tile<kMxMaxN>(p, t, ftiles, ti)) continue;
-        const uint32_t n_mma = (uint32_t)((ti.nrows + 15) & ~15);
         const uint32_t ab = tl & 1, aph = (tl >> 1) & 1;
         if (!mbar_wait(&accempty_bar[ab], aph ^ 1, p.err, kErrTimeoutAccum)) { ok = false; break; }
         tc_fence_after();
@@ -433,21 +433,18 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           const uint32_t s = it % kMxStages, ph = (it / kMxStages) & 1;
           if (!mbar_wait(&full_bar[s], ph, p.err, kErrTimeoutFull)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t sfs = smem_u32(smem + kMxOffSf + s * 3 * kMxSfBytes);
-          const uint32_t sfa = tmem_base + kMxSfCol0 + s * kMxSfStageCols, sfbh = sfa + 4, sfbl = sfa + 8;
+          const uint32_t sfs = smem_u32(smem + kMxOffSf + s * 2 * kMxSfBytes);
+          const uint32_t sfa = tmem_base + kMxSfCol0 + s * kMxSfStageCols, sfb = sfa + 4;
           tc_cp_sf(sfa, make_sdesc_sf(sfs));
-          tc_cp_sf(sfbh, make_sdesc_sf(sfs + kMxSfBytes));
-          tc_cp_sf(sfbl, make_sdesc_sf(sfs + 2 * kMxSfBytes));
+          tc_cp_sf(sfb, make_sdesc_sf(sfs + kMxSfBytes));
           const int32_t nkb = j < nmain ? kMxBK / 32 : (p.K - nmain * kMxBK) / 32;
           for (int32_t kb = 0; kb < nkb; ++kb) {
             // start-address field: (byte offset >> 4), 32 bytes (one K-block) per step
             const uint64_t adesc = wdesc0 + (uint64_t)((uint32_t)(s * kMxWBytes + kb * 32) >> 4);
-            const uint64_t hdesc = hdesc0 + (uint64_t)((uint32_t)(s * kMxActBytes + kb * 32) >> 4);
-            const uint64_t ldesc = ldesc0 + (uint64_t)((uint32_t)(s * kMxActBytes + kb * 32) >> 4);
-            const uint32_t idesc = make_idesc_mx(n_mma, (uint32_t)kb);
+            const uint64_t bdesc = bdesc0 + (uint64_t)((uint32_t)(s * kMxActStage + kb * 32) >> 4);
+            const uint32_t idesc = make_idesc_mx((uint32_t)kMxMmaN, (uint32_t)kb);
             const uint32_t byte = (uint32_t)kb << 30;
-            tc_mma_mx(d_tmem, adesc, hdesc, idesc, sfa | byte, sfbh | byte, (!first || kb > 0) ? 1u : 0u);
-            tc_mma_mx(d_tmem, adesc, ldesc, idesc, sfa | byte, sfbl | byte, 1u);
+            tc_mma_mx(d_tmem, adesc, bdesc, idesc, sfa | byte, sfb | byte, (!first || kb > 0) ? 1u : 0u);
           }
           tc_commit(&empty_bar[s]);
           first = false;
@@ -478,12 +475,17 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       if (!mbar_wait(&accfull_bar[ab], aph, p.err, kErrTimeoutAccum)) { *abort_s = 1; break; }
       __syncwarp();
       tc_fence_after();
+      // the four partial accumulators of each token row: even / odd stages x hi / lo term
       uint32_t v[32], v1[32];
-      tmem_ld_x32(tmem_base + lane_base + (2 * ab) * kMxAccCols, v);
-      tmem_ld_x32(tmem_base + lane_base + (2 * ab + 1) * kMxAccCols, v1);
-      tmem_ld_wait();
+      const uint32_t acc0 = tmem_base + lane_base + (2 * ab) * kMxAccCols;
+      tmem_ld_x32(acc0, v);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) + __uint_as_float(v1[i]));
+      for (int part = 1; part < 4; ++part) {
+        tmem_ld_x32(acc0 + (part >> 1) * kMxAccCols + (part & 1) * kMxMaxN, v1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) + __uint_as_float(v1[i]));
+      }
       epilogue_block<kMode, true>(p, ti, v, 0, q, lane, bias, row_ok, frow, (uint16_t*)(smem + kMxOffEpi) + q * 1024);
       tc_fence_before();
       __syncwarp();
