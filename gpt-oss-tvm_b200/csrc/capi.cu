@@ -613,9 +613,15 @@ bool moe_mx_enabled() {
 // run moe_gemm_mx_kernel; everything else gathers f16 / bf16 rows into `act`
 // for the decode GEMV or the kind::f16 kernels.  h2 receives the fp32 expert
 // outputs; y is the SwiGLU output (f16 on the f16 and block-scaled paths).
+// The decode GEMV keeps the routed rows of a single token (top-k rows): in
+// the gpt-oss-20b decode graphs (ms per step, GEMV / block-scaled) batch 1
+// 3.18 / 3.37, batch 2 3.77 / 3.75, batch 4 4.58 / 4.23, batch 8 5.70 /
+// 4.94, batch 16 7.32 / 5.53.  Without the block-scaled kernels (or weights
+// it does not take) the GEMV still serves up to 64 rows.
+constexpr int64_t kGemvBeforeMxRows = 4;
 static bool experts_block_scaled(int64_t M, const gptoss_moe_weights* w) {
   const int64_t R = M * w->top_k;
-  const bool gemv = (w->flags & GPTOSS_MOE_F16) && R <= 64;
+  const bool gemv = (w->flags & GPTOSS_MOE_F16) && R <= kGemvBeforeMxRows;
   return !gemv && moe_mx_enabled() && moe_mx_supported(R, w->num_experts, 2 * w->intermediate, w->hidden, w->mlp1_blocks) &&
          moe_mx_supported(R, w->num_experts, w->hidden, w->intermediate, w->mlp2_blocks);
 }
